@@ -1,0 +1,116 @@
+// Operator-level entry points of the B200 layer path (libppocr_b200.so).
+//
+// Each function runs one operator of the reference's Runtime
+// (native/src/compiled/runtime.cuh) on plain device pointers, with the same
+// operand layouts and rounding as the Runtime method it names; the C++
+// Runtime (operator API for model.inc graphs) and these functions launch the
+// same kernels. Tensors are FP16 unless stated, activations NHWC, filters
+// OHWI ([Co][KH][KW][Ci], the exporter's channels-last layout).
+// Return 0 on success, -1 on failure (message: ppocr_b200_last_error()).
+//
+// Activation codes (conv, gemm, deconv): 0 bias only, 1 ReLU, 2 erf-GELU
+// (runtime.cuh activation codes), and extensions 3 hardswish
+// x*clamp(x/6+1/2), 4 sigmoid, 5 swish x*sigmoid(x), 6 hardsigmoid.
+// Fused epilogue rounding: y = round(act(round(acc) + bias)); with a
+// residual y = round(act(round(round(acc) + bias) + residual)).
+#pragma once
+#include <cuda_runtime_api.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// Runtime::conv (runtime.cuh:647-815) for channels-last tensors: depthwise
+// (groups == Ci == Co), 1x1 stride-1 GEMM, stride-1 implicit GEMM, or a
+// direct convolution for small Ci (the stem). bias may be null.
+int ppocr_b200_conv_nhwc(const void *x, const void *w, const void *bias,
+                         void *y, int batch, int ci, int h, int w_, int co,
+                         int kh, int kw, int stride_h, int stride_w, int pad_h,
+                         int pad_w, int groups, int activation,
+                         cudaStream_t stream);
+
+// Runtime::gemm_epilogue (runtime.cuh:514-646): y[rows][co] =
+// act(x[rows][ci] . w[co][ci]^T + bias) (+ residual[rows][co]).
+int ppocr_b200_gemm_epilogue(const void *x, const void *w, const void *bias,
+                             const void *residual, void *y, int rows, int ci,
+                             int co, int activation, cudaStream_t stream);
+
+// Runtime::matmul (runtime.cuh:1013-1024): y[b] = a[b] (m x k) . b[b] (k x n),
+// contiguous batches, fp32 accumulation.
+int ppocr_b200_matmul(const void *a, const void *b, void *y, int batches,
+                      int m, int n, int k, cudaStream_t stream);
+
+// Runtime::layernorm (runtime.cuh:1000-1006, kernel 227-261).
+int ppocr_b200_layernorm(const void *x, const void *scale, const void *bias,
+                         void *y, int rows, int cols, float epsilon,
+                         cudaStream_t stream);
+// Runtime::softmax (runtime.cuh:1007-1011, kernel 189-225).
+int ppocr_b200_softmax(const void *x, void *y, int rows, int cols,
+                       cudaStream_t stream);
+// Extension: fused SVTR multi-head self-attention. qkv [lines][seq][3*H*dh]
+// (q | k | v, head-major inside each), y [lines][seq][H*dh]. Matches the
+// unfused matmul / scale / softmax / matmul chain of runtime.cuh:1013-1024,
+// 189-225 with rounding after each step: q' = round(q*scale),
+// S = round(q'.k^T), P = round(softmax(S)), O = round(P.v).
+int ppocr_b200_attention(const void *qkv, void *y, int lines, int seq,
+                         int heads, int head_dim, float scale,
+                         cudaStream_t stream);
+
+// Runtime::pool_nhwc (runtime.cuh:970-999): max or average (count excludes
+// padding) pooling.
+int ppocr_b200_pool_nhwc(const void *x, void *y, int batch, int c, int h,
+                         int w, int kh, int kw, int stride_h, int stride_w,
+                         int pad_h, int pad_w, int maximum,
+                         cudaStream_t stream);
+// Runtime::pad_nhwc (runtime.cuh:957-969): zero padding, top/left offsets.
+int ppocr_b200_pad_nhwc(const void *x, void *y, int batch, int c, int h, int w,
+                        int oh, int ow, int pad_h, int pad_w,
+                        cudaStream_t stream);
+// Runtime::resize_nearest_nhwc (runtime.cuh:461-468), asymmetric/floor;
+// with a non-null addend the FPN add is fused: y = resize(x) + addend.
+int ppocr_b200_resize_nearest_nhwc(const void *x, const void *addend, void *y,
+                                   int batch, int c, int h, int w, int oh,
+                                   int ow, float scale_h, float scale_w,
+                                   cudaStream_t stream);
+// Runtime::concat (runtime.cuh:901-915): y[r] = [a[r] | b[r]].
+int ppocr_b200_concat(const void *a, const void *b, void *y, long long rows,
+                      int na, int nb, cudaStream_t stream);
+// Runtime::transpose fast path (runtime.cuh:838-885): [batch][rows][cols] ->
+// [batch][cols][rows].
+int ppocr_b200_transpose(const void *x, void *y, int batch, int rows, int cols,
+                         cudaStream_t stream);
+// Runtime::unary (runtime.cuh:832-837): op 0 relu, 1 sigmoid, 2 hardsigmoid
+// (alpha*x+beta clamped), 3 erf, 4 sqrt, 5 cast.
+int ppocr_b200_unary(const void *x, void *y, long long n, int op, float alpha,
+                     float beta, cudaStream_t stream);
+// Runtime::binary_fast (runtime.cuh:825-831): flat broadcast indices
+// (divisor, modulus) per operand; op 0 add, 1 sub, 2 mul, 3 div, 4 pow.
+int ppocr_b200_binary_flat(const void *a, const void *b, void *y, long long n,
+                           int a_div, int a_mod, int b_div, int b_mod, int op,
+                           cudaStream_t stream);
+// Runtime::mean_nhwc (runtime.cuh:937-956): global average over h*w.
+int ppocr_b200_mean_nhwc(const void *x, void *y, int batch, int c, int spatial,
+                         cudaStream_t stream);
+// Runtime::deconv (runtime.cuh:426-453) for kernel == stride, no padding
+// (the DB head's 2x2 stride-2 upsampling). w [ci][kh][kw][co]; bias may be
+// null (extension: fused bias + activation).
+int ppocr_b200_deconv_nhwc(const void *x, const void *w, const void *bias,
+                           void *y, int batch, int h, int w_, int ci, int co,
+                           int kh, int kw, int activation, cudaStream_t stream);
+// DB binarize (native/src/detection/db_postprocess.cpp:189-190, on device):
+// map[i] = prob[i] > thresh ? 255 : 0. prob float32, map uint8.
+int ppocr_b200_binarize(const float *prob, uint8_t *map, size_t n,
+                        float thresh, cudaStream_t stream);
+// Frees device memory returned by ppocr_model_load_weights (cudaFree).
+int ppocr_b200_device_free(void *device_pointer);
+// copy_input / copy_float_output (native/src/compiled/model_library.cu:15-25).
+int ppocr_b200_f32_to_f16(const float *x, void *y, size_t valid, size_t total,
+                          cudaStream_t stream);
+int ppocr_b200_f16_to_f32(const void *x, float *y, size_t n,
+                          cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,383 @@
+// extern "C" boundary of libppocr_b200.so: the head API
+// (include/ppocr_b200_head.h) and the operator-level entry points
+// (include/ppocr_b200_ops.h). Thin argument checks + kernels.h launchers.
+#include "../../include/ppocr_b200_head.h"
+#include "../../include/ppocr_b200_ops.h"
+#include "kernels.h"
+#include <mutex>
+#include <string>
+
+using namespace pb2;
+
+namespace {
+thread_local std::string g_error;
+
+int fail(const std::string &msg) {
+  g_error = msg;
+  return -1;
+}
+int status(cudaError_t e, const char *what) {
+  if (e == cudaSuccess)
+    return 0;
+  return fail(std::string(what) + ": " + cudaGetErrorString(e));
+}
+const half *H(const void *p) { return static_cast<const half *>(p); }
+half *Hm(void *p) { return static_cast<half *>(p); }
+
+// Library-owned grow-only buffer per device for the transposed classifier
+// weight used by the reference-signature entry point.
+struct PackCache {
+  std::mutex m;
+  void *ptr[64] = {};
+  size_t bytes[64] = {};
+} g_pack;
+
+half *pack_buffer(size_t bytes) {
+  int d = 0;
+  cudaGetDevice(&d);
+  d &= 63;
+  std::lock_guard<std::mutex> lock(g_pack.m);
+  if (g_pack.bytes[d] < bytes) {
+    if (g_pack.ptr[d])
+      cudaFree(g_pack.ptr[d]);
+    g_pack.ptr[d] = nullptr;
+    g_pack.bytes[d] = 0;
+    if (cudaMalloc(&g_pack.ptr[d], bytes) != cudaSuccess)
+      return nullptr;
+    g_pack.bytes[d] = bytes;
+  }
+  return static_cast<half *>(g_pack.ptr[d]);
+}
+} // namespace
+
+extern "C" {
+
+const char *ppocr_b200_last_error(void) { return g_error.c_str(); }
+
+int ppocr_b200_device_error(void) {
+  cudaDeviceSynchronize();
+  return take_device_error();
+}
+
+int ppocr_b200_classifier_workspace(int rows, int vocab, int row_block,
+                                    int vocab_tile, int *num_row_blocks,
+                                    int *num_vocab_blocks,
+                                    size_t *partial_count) {
+  g_error.clear();
+  if (!num_row_blocks || !num_vocab_blocks || !partial_count)
+    return fail("null output pointer");
+  if (rows <= 0 || vocab <= 0) {
+    *num_row_blocks = *num_vocab_blocks = 0;
+    *partial_count = 0;
+    return 0;
+  }
+  if (row_block <= 0 || row_block > 16 || vocab_tile <= 0)
+    return fail("invalid tiled classifier workspace shape");
+  *num_row_blocks = (rows + 15) / 16;
+  *num_vocab_blocks = vocab_tiles(vocab);
+  *partial_count = static_cast<size_t>(*num_row_blocks) * 16 *
+                   static_cast<size_t>(*num_vocab_blocks);
+  return 0;
+}
+
+int ppocr_b200_classifier_pack(const void *weight, void *packed, int hidden,
+                               int vocab, cudaStream_t stream) {
+  g_error.clear();
+  if (!weight || !packed || hidden <= 0 || vocab <= 0)
+    return fail("invalid classifier pack arguments");
+  return status(pack_vocab_weight(H(weight), Hm(packed), hidden, vocab, stream),
+                "classifier pack");
+}
+
+int ppocr_b200_classifier_run_packed(
+    const void *hidden, const void *packed, const void *bias, int *ids,
+    float *prob, float *max_logits, int rows, int hidden_size, int vocab,
+    int *part_id, float *part_max, float *part_sum, int calc_prob,
+    cudaStream_t stream) {
+  g_error.clear();
+  if (rows <= 0)
+    return 0;
+  if (!hidden || !packed || !bias || !ids || !prob || !max_logits ||
+      !part_id || !part_max || !part_sum || hidden_size <= 0 ||
+      hidden_size % 8 || vocab <= 0)
+    return fail("invalid classifier launch arguments");
+  cudaError_t e = tc_vocab_partials(H(hidden), rows, hidden_size, H(packed),
+                                    H(bias), vocab, part_max, part_id, part_sum,
+                                    calc_prob, stream);
+  if (e != cudaSuccess)
+    return status(e, "vocab projection");
+  return status(vocab_merge(part_max, part_id, part_sum, rows,
+                            vocab_tiles(vocab), ids, prob, max_logits,
+                            calc_prob, stream),
+                "vocab merge");
+}
+
+int ppocr_b200_linear_argmax_prob(
+    const void *hidden, const void *weight, const void *bias, int *ids,
+    float *prob, float *max_logits, int rows, int hidden_size, int vocab,
+    int vocab_tile, int *part_id, float *part_max, float *part_sum,
+    int calc_prob, cudaStream_t stream) {
+  g_error.clear();
+  if (rows <= 0)
+    return 0;
+  // Same rejections as classifier.cu:619-623 (H % 16, tile % 16, buffers).
+  if (hidden_size <= 0 || vocab <= 0 || hidden_size % 16 != 0 ||
+      vocab_tile <= 0 || vocab_tile % 16 != 0 || !part_id || !part_max ||
+      !part_sum || !hidden || !weight || !bias)
+    return fail("invalid WMMA classifier launch arguments");
+  half *packed = pack_buffer(static_cast<size_t>(hidden_size) * vocab * 2);
+  if (!packed)
+    return fail("cannot allocate classifier pack buffer");
+  cudaError_t e = pack_vocab_weight(H(weight), packed, hidden_size, vocab, stream);
+  if (e != cudaSuccess)
+    return status(e, "classifier pack");
+  return ppocr_b200_classifier_run_packed(hidden, packed, bias, ids, prob,
+                                          max_logits, rows, hidden_size, vocab,
+                                          part_id, part_max, part_sum,
+                                          calc_prob, stream);
+}
+
+int ppocr_b200_selected_class_vs_max_probability(
+    const void *hidden, const void *weight, const void *bias,
+    const float *max_logits, float *out, int rows, int hidden_size, int vocab,
+    int class_id, cudaStream_t stream) {
+  g_error.clear();
+  if (rows <= 0)
+    return 0;
+  if (!hidden || !weight || !bias || !max_logits || !out || hidden_size <= 0 ||
+      vocab <= 0 || class_id < 0 || class_id >= vocab)
+    return fail("invalid selected-class classifier launch arguments");
+  return status(selected_class_vs_max(H(hidden), H(weight), H(bias), max_logits,
+                                      out, rows, hidden_size, vocab, class_id,
+                                      stream),
+                "selected class");
+}
+
+int ppocr_b200_logits_argmax_prob(const void *logits, int rows, int vocab,
+                                  int *ids, float *prob, float *max_logits,
+                                  int calc_prob, cudaStream_t stream) {
+  g_error.clear();
+  if (rows <= 0)
+    return 0;
+  if (!logits || !ids || !prob || !max_logits || vocab <= 0)
+    return fail("invalid logits argmax arguments");
+  return status(logits_argmax_prob(H(logits), rows, vocab, ids, prob,
+                                   max_logits, calc_prob, stream),
+                "logits argmax");
+}
+
+int ppocr_b200_ctc_collapse(const int *ids, const float *probs, int lines,
+                            int T, int blank, int *out_ids, int *out_len,
+                            float *out_score, cudaStream_t stream) {
+  g_error.clear();
+  if (lines < 0 || T < 0)
+    return fail("batch_size and seq_len must be non-negative");
+  if (lines == 0 || T == 0) {
+    if (lines > 0 && out_len && out_score) {
+      cudaMemsetAsync(out_len, 0, sizeof(int) * lines, stream);
+      cudaMemsetAsync(out_score, 0, sizeof(float) * lines, stream);
+    }
+    return 0;
+  }
+  if (!ids || !out_ids || !out_len || !out_score)
+    return fail("null collapse buffer");
+  return status(ctc_collapse(ids, probs, lines, T, blank, out_ids, out_len,
+                             out_score, stream),
+                "ctc collapse");
+}
+
+// ------------------------------------------------------------- operators
+int ppocr_b200_conv_nhwc(const void *x, const void *w, const void *bias,
+                         void *y, int batch, int ci, int h, int w_, int co,
+                         int kh, int kw, int sh, int sw, int ph, int pw,
+                         int groups, int act, cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !w || !y || batch <= 0 || ci <= 0 || co <= 0 || kh <= 0 ||
+      kw <= 0 || sh <= 0 || sw <= 0 || ph < 0 || pw < 0 || groups <= 0)
+    return fail("invalid conv arguments");
+  const int oh = (h + 2 * ph - kh) / sh + 1, ow = (w_ + 2 * pw - kw) / sw + 1;
+  if (oh <= 0 || ow <= 0)
+    return fail("conv output is empty");
+  cudaError_t e = conv_nhwc(H(x), H(w), H(bias), Hm(y), batch, ci, h, w_, co,
+                            kh, kw, sh, sw, ph, pw, groups, act, stream);
+  if (e == cudaErrorNotSupported)
+    return fail("unsupported conv form");
+  return status(e, "conv");
+}
+
+int ppocr_b200_gemm_epilogue(const void *x, const void *w, const void *bias,
+                             const void *residual, void *y, int rows, int ci,
+                             int co, int act, cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !w || !y || rows < 0 || ci <= 0 || co <= 0 || ci % 8 || co % 8)
+    return fail("invalid gemm_epilogue arguments");
+  GemmEpilogue e;
+  e.bias = H(bias);
+  e.residual = H(residual);
+  e.ldr = co;
+  e.out = Hm(y);
+  e.ldo = co;
+  e.act = act;
+  return status(tc_gemm(H(x), rows, ci, ci, H(w), co, ci, e, stream), "gemm");
+}
+
+int ppocr_b200_matmul(const void *a, const void *b, void *y, int batches,
+                      int m, int n, int k, cudaStream_t stream) {
+  g_error.clear();
+  if (!a || !b || !y || batches < 0 || m < 0 || n < 0 || k < 0)
+    return fail("invalid matmul arguments");
+  return status(matmul_batched(H(a), H(b), Hm(y), batches, m, n, k,
+                               static_cast<long long>(m) * k,
+                               static_cast<long long>(k) * n,
+                               static_cast<long long>(m) * n, stream),
+                "matmul");
+}
+
+int ppocr_b200_layernorm(const void *x, const void *scale, const void *bias,
+                         void *y, int rows, int cols, float eps,
+                         cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !scale || !bias || !y || rows < 0 || cols <= 0)
+    return fail("invalid layernorm arguments");
+  return status(layernorm(H(x), H(scale), H(bias), Hm(y), rows, cols, eps,
+                          stream),
+                "layernorm");
+}
+
+int ppocr_b200_softmax(const void *x, void *y, int rows, int cols,
+                       cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !y || rows < 0 || cols <= 0)
+    return fail("invalid softmax arguments");
+  return status(softmax_rows(H(x), Hm(y), rows, cols, stream), "softmax");
+}
+
+int ppocr_b200_attention(const void *qkv, void *y, int lines, int seq,
+                         int heads, int dh, float scale, cudaStream_t stream) {
+  g_error.clear();
+  if (!qkv || !y || lines < 0 || seq <= 0 || heads <= 0 || dh <= 0)
+    return fail("invalid attention arguments");
+  cudaError_t e = attention(H(qkv), Hm(y), lines, seq, heads, dh, scale, stream);
+  if (e == cudaErrorInvalidValue)
+    return fail("attention line does not fit in shared memory");
+  return status(e, "attention");
+}
+
+int ppocr_b200_pool_nhwc(const void *x, void *y, int batch, int c, int h,
+                         int w, int kh, int kw, int sh, int sw, int ph, int pw,
+                         int maximum, cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !y || batch <= 0 || c <= 0 || kh <= 0 || kw <= 0 || sh <= 0 ||
+      sw <= 0)
+    return fail("invalid pool arguments");
+  const int oh = (h + 2 * ph - kh) / sh + 1, ow = (w + 2 * pw - kw) / sw + 1;
+  return status(pool_nhwc(H(x), Hm(y), batch, c, h, w, oh, ow, kh, kw, sh, sw,
+                          ph, pw, maximum != 0, stream),
+                "pool");
+}
+
+int ppocr_b200_pad_nhwc(const void *x, void *y, int batch, int c, int h, int w,
+                        int oh, int ow, int ph, int pw, cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !y || batch <= 0 || c <= 0)
+    return fail("invalid pad arguments");
+  return status(pad_nhwc(H(x), Hm(y), batch, c, h, w, oh, ow, ph, pw, stream),
+                "pad");
+}
+
+int ppocr_b200_resize_nearest_nhwc(const void *x, const void *addend, void *y,
+                                   int batch, int c, int h, int w, int oh,
+                                   int ow, float sh, float sw,
+                                   cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !y || batch <= 0 || c <= 0 || sh <= 0 || sw <= 0)
+    return fail("invalid resize arguments");
+  return status(resize_nearest_nhwc(H(x), H(addend), Hm(y), batch, c, h, w, oh,
+                                    ow, sh, sw, stream),
+                "resize");
+}
+
+int ppocr_b200_concat(const void *a, const void *b, void *y, long long rows,
+                      int na, int nb, cudaStream_t stream) {
+  g_error.clear();
+  if (!a || !b || !y || rows < 0 || na < 0 || nb < 0)
+    return fail("invalid concat arguments");
+  return status(concat_rows(H(a), H(b), Hm(y), rows, na, nb, stream), "concat");
+}
+
+int ppocr_b200_transpose(const void *x, void *y, int batch, int rows, int cols,
+                         cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !y)
+    return fail("invalid transpose arguments");
+  return status(transpose2d(H(x), Hm(y), batch, rows, cols, stream),
+                "transpose");
+}
+
+int ppocr_b200_unary(const void *x, void *y, long long n, int op, float alpha,
+                     float beta, cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !y || n < 0 || op < 0 || op > 5)
+    return fail("invalid unary arguments");
+  return status(unary(H(x), Hm(y), n, op, alpha, beta, stream), "unary");
+}
+
+int ppocr_b200_binary_flat(const void *a, const void *b, void *y, long long n,
+                           int ad, int am, int bd, int bm, int op,
+                           cudaStream_t stream) {
+  g_error.clear();
+  if (!a || !b || !y || n < 0 || op < 0 || op > 4 || ad <= 0 || bd <= 0)
+    return fail("invalid binary arguments");
+  return status(binary_flat(H(a), H(b), Hm(y), n, ad, am, bd, bm, op, stream),
+                "binary");
+}
+
+int ppocr_b200_mean_nhwc(const void *x, void *y, int batch, int c, int spatial,
+                         cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !y || batch < 0 || c <= 0 || spatial <= 0)
+    return fail("invalid mean arguments");
+  return status(mean_nhwc(H(x), Hm(y), batch, c, spatial, stream), "mean");
+}
+
+int ppocr_b200_deconv_nhwc(const void *x, const void *w, const void *bias,
+                           void *y, int batch, int h, int w_, int ci, int co,
+                           int kh, int kw, int act, cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !w || !y || batch < 0 || ci <= 0 || co <= 0 || kh <= 0 || kw <= 0)
+    return fail("invalid deconv arguments");
+  return status(deconv_kxk(H(x), H(w), H(bias), Hm(y), batch, h, w_, ci, co,
+                           kh, kw, act, stream),
+                "deconv");
+}
+
+int ppocr_b200_binarize(const float *prob, uint8_t *map, size_t n, float thresh,
+                        cudaStream_t stream) {
+  g_error.clear();
+  if (!prob || !map)
+    return fail("invalid binarize arguments");
+  return status(binarize(prob, map, n, thresh, stream), "binarize");
+}
+
+int ppocr_b200_device_free(void *p) {
+  g_error.clear();
+  return status(cudaFree(p), "cudaFree");
+}
+
+int ppocr_b200_f32_to_f16(const float *x, void *y, size_t valid, size_t total,
+                          cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !y || valid > total)
+    return fail("invalid conversion arguments");
+  return status(copy_input_f32(x, Hm(y), valid, total, stream), "f32_to_f16");
+}
+
+int ppocr_b200_f16_to_f32(const void *x, float *y, size_t n,
+                          cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !y)
+    return fail("invalid conversion arguments");
+  return status(half_to_float(H(x), y, n, stream), "f16_to_f32");
+}
+
+} // extern "C"

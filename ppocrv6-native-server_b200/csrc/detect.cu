@@ -1,0 +1,124 @@
+// DB detector tail: transposed convolution with kernel == stride (the DB
+// head's 2x2 stride-2 upsampling) and the binarize step.
+//
+// Reference semantics (ppocrv6-native-server):
+//   deconv    native/src/compiled/runtime.cuh:426-453 (cuDNN backward-data,
+//             weights [Ci][KH][KW][Co] after the channels-last pass,
+//             tools/compiled_models/export.py:590-600)
+//   binarize  native/src/detection/db_postprocess.cpp:189-190
+//             (cv::compare(pred, thresh, CMP_GT) -> 255 / 0)
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace pb2 {
+namespace {
+
+// Thread = one output pixel x 8 output channels (Co % 8 == 0) or one output
+// element (otherwise). With kernel == stride each output pixel has exactly
+// one contributing input pixel and one filter tap.
+__global__ void __launch_bounds__(256)
+    deconv_kernel(const half *__restrict__ x, const half *__restrict__ w,
+                  const half *__restrict__ bias, half *__restrict__ y,
+                  long long total, int H, int W, int Ci, int Co, int KH,
+                  int KW, int act, bool vec) {
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total)
+    return;
+  const int per = vec ? Co / 8 : Co;
+  const int g = static_cast<int>(i % per);
+  long long p = i / per;
+  const int OW = W * KW, OH = H * KH;
+  const int ox = static_cast<int>(p % OW);
+  const int oy = static_cast<int>((p / OW) % OH);
+  const long long n = p / (static_cast<long long>(OW) * OH);
+  const int ix = ox / KW, dx = ox - ix * KW;
+  const int iy = oy / KH, dy = oy - iy * KH;
+  const half *px = x + ((n * H + iy) * W + ix) * Ci;
+  const long long tap = static_cast<long long>(dy * KW + dx) * Co;
+  const long long cstride = static_cast<long long>(KH) * KW * Co;
+  if (vec) {
+    const int co0 = g * 8;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int ci = 0; ci < Ci; ++ci) {
+      const float xv = __half2float(px[ci]);
+      uint4 wv = __ldg(reinterpret_cast<const uint4 *>(w + ci * cstride + tap + co0));
+      const half2 *wh = reinterpret_cast<const half2 *>(&wv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __half22float2(wh[j]);
+        acc[2 * j] = fmaf(xv, f.x, acc[2 * j]);
+        acc[2 * j + 1] = fmaf(xv, f.y, acc[2 * j + 1]);
+      }
+    }
+    uint4 o;
+    half2 *oh = reinterpret_cast<half2 *>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float v0 = round_half(acc[2 * j]), v1 = round_half(acc[2 * j + 1]);
+      if (bias) {
+        v0 += __half2float(bias[co0 + 2 * j]);
+        v1 += __half2float(bias[co0 + 2 * j + 1]);
+      }
+      oh[j] = __floats2half2_rn(apply_act(v0, act), apply_act(v1, act));
+    }
+    *reinterpret_cast<uint4 *>(y + p * Co + co0) = o;
+  } else {
+    float acc = 0.f;
+    for (int ci = 0; ci < Ci; ++ci)
+      acc = fmaf(__half2float(px[ci]), __half2float(w[ci * cstride + tap + g]),
+                 acc);
+    float v = round_half(acc);
+    if (bias)
+      v += __half2float(bias[g]);
+    y[p * Co + g] = __float2half_rn(apply_act(v, act));
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    binarize_kernel(const float *__restrict__ prob, uint8_t *__restrict__ map,
+                    size_t n, float thresh) {
+  const size_t i4 = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  if (i4 + 4 <= n) {
+    const float4 v = __ldg(reinterpret_cast<const float4 *>(prob + i4));
+    uchar4 o;
+    o.x = v.x > thresh ? 255 : 0;
+    o.y = v.y > thresh ? 255 : 0;
+    o.z = v.z > thresh ? 255 : 0;
+    o.w = v.w > thresh ? 255 : 0;
+    *reinterpret_cast<uchar4 *>(map + i4) = o;
+  } else {
+    for (size_t i = i4; i < n; ++i)
+      map[i] = prob[i] > thresh ? 255 : 0;
+  }
+}
+
+} // namespace
+
+cudaError_t binarize(const float *prob, uint8_t *map, size_t n, float thresh,
+                     cudaStream_t s) {
+  if (!n)
+    return cudaSuccess;
+  if ((reinterpret_cast<uintptr_t>(prob) & 15) ||
+      (reinterpret_cast<uintptr_t>(map) & 3))
+    return cudaErrorInvalidValue;
+  const size_t threads = (n + 3) / 4;
+  binarize_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(
+      prob, map, n, thresh);
+  return cudaGetLastError();
+}
+
+cudaError_t deconv_kxk(const half *x, const half *w, const half *bias, half *y,
+                       int batch, int H, int W, int Ci, int Co, int KH, int KW,
+                       int act, cudaStream_t s) {
+  if (batch <= 0)
+    return cudaSuccess;
+  const bool vec = Co % 8 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+  const long long total = static_cast<long long>(batch) * H * KH * W * KW *
+                          (vec ? Co / 8 : Co);
+  deconv_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(
+      x, w, bias, y, total, H, W, Ci, Co, KH, KW, act, vec);
+  return cudaGetLastError();
+}
+
+} // namespace pb2

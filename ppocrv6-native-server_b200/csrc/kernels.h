@@ -1,0 +1,181 @@
+// Host-side launchers for every device kernel of the B200 layer path.
+// These are the internal C++ entry points used by the Runtime (operator API),
+// the model ABI shell and the extern "C" boundary in capi.cu.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace pb2 {
+
+// Per-device error word written by kernels whose bounded waits ran out
+// (see ptx.cuh). Allocated once per device on first use; never freed.
+int *device_error_word();
+// Reads and clears the error word of the current device (synchronizes).
+int take_device_error();
+int sm_count();
+
+// ------------------------------------------------------------ tensor cores
+// Implicit-GEMM / GEMM on tcgen05. Weights are K-major: [N][taps][Ci].
+// Epilogue: v = round_half(acc) + bias[n]; with a residual
+// v = round_half(v) + residual[row][n]; v = act(v); y = round_half(v).
+struct GemmEpilogue {
+  const half *bias = nullptr;     // [N] or null
+  const half *residual = nullptr; // [rows][ldr] or null
+  int ldr = 0;
+  half *out = nullptr; // [rows][ldo]
+  int ldo = 0;
+  int act = 0;
+};
+// Plain GEMM: out[M][N] = A[M][K] (row stride lda) x W[N][K]^T (row stride ldw).
+cudaError_t tc_gemm(const half *A, int M, int K, int lda, const half *W, int N,
+                    int ldw, const GemmEpilogue &epi, cudaStream_t stream);
+
+// Stride-1 dense NHWC convolution as implicit GEMM:
+// x [batch][H][W][Ci], w [Co][KH][KW][Ci], y [batch][OH][OW][Co] with
+// OH = H + 2*pad_h - KH + 1, OW = W + 2*pad_w - KW + 1.
+struct ConvShape {
+  int batch, H, W, Ci, Co, KH, KW, pad_h, pad_w;
+};
+cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
+                    const GemmEpilogue &epi, cudaStream_t stream);
+
+// Vocabulary projection with fused row argmax / softmax-max reduction:
+// logits[r][v] = hidden[r][:] . wt[v][:] + bias[v] (fp32), reduced over v to
+// (max, lowest argmax, sum exp(l - max)) per vocabulary tile of 256 columns.
+// Partials are laid out [tile][rows]. hidden [rows][H], wt [V][H] (K-major).
+cudaError_t tc_vocab_partials(const half *hidden, int rows, int H,
+                              const half *wt, const half *bias, int V,
+                              float *part_max, int *part_id, float *part_sum,
+                              int calc_prob, cudaStream_t stream);
+int vocab_tiles(int V);
+// Merges the per-tile partials into ids/prob/max_logit per row.
+cudaError_t vocab_merge(const float *part_max, const int *part_id,
+                        const float *part_sum, int rows, int tiles, int *ids,
+                        float *prob, float *max_logit, int calc_prob,
+                        cudaStream_t stream);
+
+// NHWC convolution dispatcher used by Runtime::conv and the C entry point
+// (depthwise / 1x1 GEMM / implicit GEMM / direct). Weights OHWI.
+cudaError_t conv_nhwc(const half *x, const half *w, const half *bias, half *y,
+                      int B, int C, int H, int W, int Co, int KH, int KW,
+                      int SH, int SW, int PH, int PW, int groups, int act,
+                      cudaStream_t stream);
+
+// --------------------------------------------------------------- SIMT ops
+// Depthwise NHWC conv with fused bias + activation, reference rounding:
+// y = round(act(round(sum) + bias)). Weights [C][KH][KW]. C % 8 == 0.
+cudaError_t depthwise(const half *x, const half *w, const half *bias, half *y,
+                      int batch, int C, int H, int W, int OH, int OW, int KH,
+                      int KW, int SH, int SW, int PH, int PW, int act,
+                      cudaStream_t stream);
+// Generic NHWC direct conv for small Ci (stem): w [Co][KH][KW][Ci].
+cudaError_t direct_conv(const half *x, const half *w, const half *bias,
+                        half *y, int batch, int Ci, int H, int W, int Co,
+                        int OH, int OW, int KH, int KW, int SH, int SW, int PH,
+                        int PW, int act, cudaStream_t stream);
+cudaError_t pool_nhwc(const half *x, half *y, int batch, int C, int H, int W,
+                      int OH, int OW, int KH, int KW, int SH, int SW, int PH,
+                      int PW, bool maximum, cudaStream_t stream);
+cudaError_t pool_nchw(const half *x, half *y, int planes, int H, int W, int OH,
+                      int OW, int KH, int KW, int SH, int SW, int PH, int PW,
+                      bool maximum, cudaStream_t stream);
+cudaError_t pad_nhwc(const half *x, half *y, int batch, int C, int H, int W,
+                     int OH, int OW, int PH, int PW, cudaStream_t stream);
+cudaError_t pad_nchw(const half *x, half *y, int planes, int H, int W, int OH,
+                     int OW, int PH, int PW, cudaStream_t stream);
+// Nearest-neighbour resize (asymmetric coordinates, floor), optional fused add
+// of `addend` (same shape as y): y = round(round(resize(x)) + addend).
+cudaError_t resize_nearest_nhwc(const half *x, const half *addend, half *y,
+                                int batch, int C, int H, int W, int OH, int OW,
+                                float scale_h, float scale_w,
+                                cudaStream_t stream);
+cudaError_t resize_nearest_nchw(const half *x, half *y, int planes, int H,
+                                int W, int OH, int OW, float scale_h,
+                                float scale_w, cudaStream_t stream);
+// Row-wise concat: y[r] = [a[r] (na) | b[r] (nb)].
+cudaError_t concat_rows(const half *a, const half *b, half *y, long long rows,
+                        int na, int nb, cudaStream_t stream);
+// Batched 2D transpose: x [batch][rows][cols] -> y [batch][cols][rows].
+cudaError_t transpose2d(const half *x, half *y, int batch, int rows, int cols,
+                        cudaStream_t stream);
+// Generic strided gather (rank <= 6): y[i] = x[offset + sum_d idx_d * stride_d].
+struct Gather {
+  int rank = 0;
+  int shape[6] = {};
+  long long stride[6] = {};
+  long long offset = 0;
+};
+cudaError_t gather(const half *x, half *y, long long n, const Gather &g,
+                   cudaStream_t stream);
+// Broadcast binary: each operand indexed through its own Gather map.
+cudaError_t binary(const half *a, const half *b, half *y, long long n,
+                   const Gather &ga, const Gather &gb, int op,
+                   cudaStream_t stream);
+// Flat broadcast binary with constant divisor/modulus index maps.
+cudaError_t binary_flat(const half *a, const half *b, half *y, long long n,
+                        int ad, int am, int bd, int bm, int op,
+                        cudaStream_t stream);
+cudaError_t unary(const half *x, half *y, long long n, int op, float alpha,
+                  float beta, cudaStream_t stream);
+// NCHW f32 (batch rows valid, rest zero) -> NCHW fp16, the ABI input copy.
+cudaError_t copy_input_f32(const float *x, half *y, size_t valid, size_t total,
+                           cudaStream_t stream);
+// NHWC fp16 (valid images) -> NCHW fp16 with zero tail.
+cudaError_t copy_input_nhwc_f16(const half *x, half *y, int valid, int batch,
+                                int C, int H, int W, cudaStream_t stream);
+cudaError_t half_to_float(const half *x, float *y, size_t n,
+                          cudaStream_t stream);
+
+// ------------------------------------------------------ sequence kernels
+cudaError_t layernorm(const half *x, const half *scale, const half *bias,
+                      half *y, int rows, int cols, float eps,
+                      cudaStream_t stream);
+cudaError_t softmax_rows(const half *x, half *y, int rows, int cols,
+                         cudaStream_t stream);
+cudaError_t mean_rows(const half *x, half *y, int rows, int cols,
+                      cudaStream_t stream);
+cudaError_t mean_nhwc(const half *x, half *y, int batch, int C, int spatial,
+                      cudaStream_t stream);
+// Batched row-major matmul y[b] = a[b] (m x k) . b[b] (k x n), fp32 accumulate.
+cudaError_t matmul_batched(const half *a, const half *b, half *y, int batches,
+                           int m, int n, int k, long long sa, long long sb,
+                           long long sy, cudaStream_t stream);
+// Fused multi-head self-attention over packed qkv rows:
+// qkv [lines][seq][3*heads*dh] (q | k | v), out [lines][seq][heads*dh].
+// Reference rounding points: S = round(q.k^T), S = round(S*scale),
+// P = round(softmax(S)), O = round(P.v).
+cudaError_t attention(const half *qkv, half *out, int lines, int seq, int heads,
+                      int dh, float scale, cudaStream_t stream);
+
+// ----------------------------------------------------------- head kernels
+// Row argmax / softmax-max over fp16 logits [rows][V].
+cudaError_t logits_argmax_prob(const half *logits, int rows, int V, int *ids,
+                               float *prob, float *max_logit, int calc_prob,
+                               cudaStream_t stream);
+// CTC greedy collapse per line: drop repeats, then blanks; mean kept prob.
+// out_ids [lines][T] (compacted, -1 padded), out_len [lines], out_score.
+cudaError_t ctc_collapse(const int *ids, const float *probs, int lines, int T,
+                         int blank, int *out_ids, int *out_len,
+                         float *out_score, cudaStream_t stream);
+// Transpose W [H][V] -> wt [V][H] (K-major) for the vocabulary projection.
+cudaError_t pack_vocab_weight(const half *w, half *wt, int H, int V,
+                              cudaStream_t stream);
+// p(class)/(p(class)+p(max)) for one selected class.
+cudaError_t selected_class_vs_max(const half *hidden, const half *w,
+                                  const half *bias, const float *max_logits,
+                                  float *out, int rows, int H, int V,
+                                  int class_id, cudaStream_t stream);
+
+// ------------------------------------------------------- detector kernels
+// DB binarize: map[i] = prob[i] > thresh ? 255 : 0.
+cudaError_t binarize(const float *prob, uint8_t *map, size_t n, float thresh,
+                     cudaStream_t stream);
+// Transposed conv, kernel == stride, no padding (DB head 2x2 s2):
+// x [batch][H][W][Ci], w [Ci][KH][KW][Co], y [batch][H*KH][W*KW][Co].
+cudaError_t deconv_kxk(const half *x, const half *w, const half *bias, half *y,
+                       int batch, int H, int W, int Ci, int Co, int KH, int KW,
+                       int act, cudaStream_t stream);
+
+} // namespace pb2

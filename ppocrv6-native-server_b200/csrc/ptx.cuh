@@ -1,0 +1,226 @@
+// Inline-PTX primitives for sm_100a: mbarriers, TMA tile loads, tcgen05 (TMEM
+// allocation, UMMA issue/commit, TMEM loads) and shared-memory descriptors.
+//
+// Every wait in this file is bounded: mbar_wait() gives up after a cycle budget
+// and returns false so that the calling kernel can record an error, drain its
+// own in-flight work and exit instead of spinning forever.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace pb2 {
+
+// ~2 s at 1.9 GHz. A legitimate wait in these kernels is at most one tile's
+// K loop (tens of microseconds), so hitting this budget means a lost arrival.
+constexpr long long kWaitBudgetCycles = 4000000000LL;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\t"
+               "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar,
+                                                      uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\t"
+               "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::
+                   "r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n\t.reg .pred p;\n\t"
+               "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+               "selp.b32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok)
+               : "r"(smem_u32(bar)), "r"(parity)
+               : "memory");
+  return ok != 0;
+}
+// Waits for the phase with the given parity to complete. Returns false if the
+// cycle budget runs out or if *abort becomes non-zero (another role failed).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
+                                          volatile int *abort) {
+  if (mbar_try_wait(bar, parity))
+    return true;
+  long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort)
+      return false;
+    if (clock64() - t0 > kWaitBudgetCycles)
+      return false;
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------- TMA loads
+// Tiled bulk-tensor loads into this CTA's shared memory, completing on an
+// mbarrier (complete_tx). No multicast variant exists in this code base.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map,
+                                            uint64_t *bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_"
+      "tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map,
+                                            uint64_t *bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_"
+      "tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1),
+      "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map,
+                                            uint64_t *bar, int c0, int c1,
+                                            int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_"
+      "tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1),
+      "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map))
+               : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
+  asm volatile(
+      "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+          smem_u32(slot)),
+      "r"(ncols)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(
+                   taddr),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (fp16 in, fp32 acc).
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc,
+                                         uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile("{\n\t.reg .pred p;\n\t"
+               "setp.ne.b32 p, %4, 0;\n\t"
+               "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::
+                   "r"(d_tmem),
+               "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+               : "memory");
+}
+// Arrives once on `bar` when every previously issued tcgen05.mma of this
+// thread has completed.
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::"
+               "cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// 32 TMEM lanes x 16 consecutive 32-bit columns: lane i of the warp receives
+// row (lane base + i), columns [col, col+16).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+               "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]),
+                 "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+                 "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+                 "=r"(r[14]), "=r"(r[15])
+               : "r"(taddr)
+               : "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand tile written by TMA
+// with 128-byte swizzle: rows of 64 fp16 (128 B), 8-row swizzle atoms of
+// 1024 B. SBO = 1024 B between 8-row groups; LBO is unused for this layout
+// (encoded as 1); version field = 1 (sm_100); layout type 2 = SWIZZLE_128B.
+// The tile base must be 1024-byte aligned; the K offset inside the 128-byte
+// row is added to the start address (32 B per 16-element K step).
+__device__ __forceinline__ uint64_t sdesc_k_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16 with fp16 A/B, fp32 accumulator, both
+// operands K-major, dense. M in {64,128}, N a multiple of 16 up to 256.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+  return (1u << 4)                                   // D format: f32
+         | (0u << 7) | (0u << 10)                    // A, B: f16
+         | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
+         | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
+}
+
+__device__ __forceinline__ float round_half(float v) {
+  return __half2float(__float2half_rn(v));
+}
+
+// Activation codes shared by every fused epilogue. 0..2 follow the reference
+// runtime (bias only, ReLU, erf-GELU); 3..6 extend it for folded
+// HardSigmoid*x, Sigmoid, x*Sigmoid and HardSigmoid chains.
+enum Act : int {
+  kActNone = 0,
+  kActRelu = 1,
+  kActGelu = 2,
+  kActHardSwish = 3,
+  kActSigmoid = 4,
+  kActSwish = 5,
+  kActHardSigmoid = 6,
+};
+
+__device__ __forceinline__ float apply_act(float x, int act) {
+  switch (act) {
+  case kActRelu:
+    return fmaxf(x, 0.f);
+  case kActGelu:
+    return (x * (erff(x / 1.41421354f) + 1.f)) * 0.5f;
+  case kActHardSwish:
+    return x * fminf(1.f, fmaxf(0.f, 0.166666671634f * x + 0.5f));
+  case kActSigmoid:
+    return 1.f / (1.f + expf(-x));
+  case kActSwish:
+    return x * (1.f / (1.f + expf(-x)));
+  case kActHardSigmoid:
+    return fminf(1.f, fmaxf(0.f, 0.166666671634f * x + 0.5f));
+  default:
+    return x;
+  }
+}
+
+} // namespace pb2

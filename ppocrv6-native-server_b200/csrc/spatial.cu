@@ -1,0 +1,768 @@
+// Memory-bound NHWC kernels of the layer path: depthwise convolution with the
+// fused bias/activation epilogue, small-Ci direct convolution (stem), pooling,
+// padding, nearest resize (+ fused FPN add), row concat, transposes, gathers,
+// broadcast elementwise ops and the ABI input/output conversions.
+//
+// Reference semantics followed (file:line in ppocrv6-native-server):
+//   depthwise    native/src/compiled/spatial_kernels.cuh:31-109 (tap order,
+//                fp16 rounding of the sum before bias, activation after)
+//   pool         spatial_kernels.cuh:156-193, 289-308 (count excludes pad)
+//   pad          spatial_kernels.cuh:9-22, 225-236
+//   resize       native/src/compiled/runtime.cuh:356-376 (asymmetric, floor)
+//   concat       runtime.cuh:145-160
+//   transpose    runtime.cuh:125-144, gather/slice 125-129
+//   binary/unary runtime.cuh:73-124
+//   copy_input   native/src/compiled/model_library.cu:15-25
+// All kernels move 16-byte vectors (8 fp16 channels) where the layout allows.
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace pb2 {
+namespace {
+
+constexpr int kBlock = 256;
+
+union Pack8 {
+  uint4 u;
+  half2 h[4];
+};
+
+inline unsigned blocks_for(long long n, int per_block = kBlock) {
+  long long b = (n + per_block - 1) / per_block;
+  return static_cast<unsigned>(b < 1 ? 1 : b);
+}
+
+// ------------------------------------------------------------- depthwise
+// Thread = 8 channels x PIX consecutive output columns of one output row.
+// Threads of a warp walk the channel groups of the same pixels, so every
+// 16-byte load and store is coalesced across the warp.
+template <int KH, int KW, int SH, int SW, int PIX>
+__global__ void __launch_bounds__(kBlock)
+    depthwise_kernel(const half *__restrict__ x, const half *__restrict__ w,
+                     const half *__restrict__ bias, half *__restrict__ y,
+                     int batch, int C, int H, int W, int OH, int OW, int PH,
+                     int PW, int act) {
+  const int groups = C >> 3;
+  const int tiles = (OW + PIX - 1) / PIX;
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(batch) * OH * tiles * groups;
+  if (i >= total)
+    return;
+  const int g = static_cast<int>(i % groups);
+  long long t = i / groups;
+  const int tile = static_cast<int>(t % tiles);
+  t /= tiles;
+  const int oh = static_cast<int>(t % OH);
+  const int n = static_cast<int>(t / OH);
+  const int c0 = g * 8;
+  const int ow0 = tile * PIX;
+
+  float acc[PIX][8];
+#pragma unroll
+  for (int p = 0; p < PIX; ++p)
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      acc[p][j] = 0.f;
+
+  const half *xn = x + static_cast<long long>(n) * H * W * C;
+#pragma unroll
+  for (int a = 0; a < KH; ++a) {
+    const int r = oh * SH - PH + a;
+    if (r < 0 || r >= H)
+      continue;
+#pragma unroll
+    for (int b = 0; b < KW; ++b) {
+      float wv[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        wv[j] = __half2float(w[(c0 + j) * (KH * KW) + a * KW + b]);
+#pragma unroll
+      for (int p = 0; p < PIX; ++p) {
+        const int c = (ow0 + p) * SW - PW + b;
+        if (c < 0 || c >= W)
+          continue;
+        Pack8 v;
+        v.u = __ldg(reinterpret_cast<const uint4 *>(
+            xn + (static_cast<long long>(r) * W + c) * C + c0));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = __half22float2(v.h[j]);
+          acc[p][2 * j] = fmaf(f.x, wv[2 * j], acc[p][2 * j]);
+          acc[p][2 * j + 1] = fmaf(f.y, wv[2 * j + 1], acc[p][2 * j + 1]);
+        }
+      }
+    }
+  }
+  float bv[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    bv[j] = bias ? __half2float(bias[c0 + j]) : 0.f;
+#pragma unroll
+  for (int p = 0; p < PIX; ++p) {
+    const int ow = ow0 + p;
+    if (ow >= OW)
+      break;
+    Pack8 o;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float v0 = round_half(acc[p][2 * j]);
+      float v1 = round_half(acc[p][2 * j + 1]);
+      if (bias) {
+        v0 = apply_act(v0 + bv[2 * j], act);
+        v1 = apply_act(v1 + bv[2 * j + 1], act);
+      }
+      o.h[j] = __floats2half2_rn(v0, v1);
+    }
+    *reinterpret_cast<uint4 *>(
+        y + ((static_cast<long long>(n) * OH + oh) * OW + ow) * C + c0) = o.u;
+  }
+}
+
+// Any filter size / stride: same structure, runtime loop bounds.
+__global__ void __launch_bounds__(kBlock)
+    depthwise_generic_kernel(const half *__restrict__ x,
+                             const half *__restrict__ w,
+                             const half *__restrict__ bias,
+                             half *__restrict__ y, int batch, int C, int H,
+                             int W, int OH, int OW, int KH, int KW, int SH,
+                             int SW, int PH, int PW, int act) {
+  const int groups = C >> 3;
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(batch) * OH * OW * groups;
+  if (i >= total)
+    return;
+  const int g = static_cast<int>(i % groups);
+  long long t = i / groups;
+  const int ow = static_cast<int>(t % OW);
+  t /= OW;
+  const int oh = static_cast<int>(t % OH);
+  const int n = static_cast<int>(t / OH);
+  const int c0 = g * 8;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const half *xn = x + static_cast<long long>(n) * H * W * C;
+  for (int a = 0; a < KH; ++a) {
+    const int r = oh * SH - PH + a;
+    if (r < 0 || r >= H)
+      continue;
+    for (int b = 0; b < KW; ++b) {
+      const int c = ow * SW - PW + b;
+      if (c < 0 || c >= W)
+        continue;
+      Pack8 v;
+      v.u = __ldg(reinterpret_cast<const uint4 *>(
+          xn + (static_cast<long long>(r) * W + c) * C + c0));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __half22float2(v.h[j]);
+        acc[2 * j] = fmaf(
+            f.x, __half2float(w[(c0 + 2 * j) * (KH * KW) + a * KW + b]),
+            acc[2 * j]);
+        acc[2 * j + 1] = fmaf(
+            f.y, __half2float(w[(c0 + 2 * j + 1) * (KH * KW) + a * KW + b]),
+            acc[2 * j + 1]);
+      }
+    }
+  }
+  Pack8 o;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float v0 = round_half(acc[2 * j]);
+    float v1 = round_half(acc[2 * j + 1]);
+    if (bias) {
+      v0 = apply_act(v0 + __half2float(bias[c0 + 2 * j]), act);
+      v1 = apply_act(v1 + __half2float(bias[c0 + 2 * j + 1]), act);
+    }
+    o.h[j] = __floats2half2_rn(v0, v1);
+  }
+  *reinterpret_cast<uint4 *>(
+      y + ((static_cast<long long>(n) * OH + oh) * OW + ow) * C + c0) = o.u;
+}
+
+template <int KH, int KW, int SH, int SW>
+cudaError_t launch_dw(const half *x, const half *w, const half *bias, half *y,
+                      int batch, int C, int H, int W, int OH, int OW, int PH,
+                      int PW, int act, cudaStream_t s) {
+  constexpr int PIX = (KW >= 7) ? 2 : 4;
+  const long long total =
+      static_cast<long long>(batch) * OH * ((OW + PIX - 1) / PIX) * (C / 8);
+  depthwise_kernel<KH, KW, SH, SW, PIX><<<blocks_for(total), kBlock, 0, s>>>(
+      x, w, bias, y, batch, C, H, W, OH, OW, PH, PW, act);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------- direct conv
+// Thread = one output pixel x 8 output channels. Filter in shared memory as
+// fp32, summed in (kh, kw, ci) order.
+__global__ void __launch_bounds__(kBlock)
+    direct_conv_kernel(const half *__restrict__ x, const half *__restrict__ w,
+                       const half *__restrict__ bias, half *__restrict__ y,
+                       int batch, int Ci, int H, int W, int Co, int OH, int OW,
+                       int KH, int KW, int SH, int SW, int PH, int PW,
+                       int act) {
+  extern __shared__ float wsm[];
+  const int wn = Co * KH * KW * Ci;
+  for (int j = threadIdx.x; j < wn; j += blockDim.x)
+    wsm[j] = __half2float(w[j]);
+  __syncthreads();
+  const int groups = Co >> 3;
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(batch) * OH * OW * groups;
+  if (i >= total)
+    return;
+  const int g = static_cast<int>(i % groups);
+  long long t = i / groups;
+  const int ow = static_cast<int>(t % OW);
+  t /= OW;
+  const int oh = static_cast<int>(t % OH);
+  const int n = static_cast<int>(t / OH);
+  const int co0 = g * 8;
+  const int kstride = KH * KW * Ci;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int a = 0; a < KH; ++a) {
+    const int r = oh * SH - PH + a;
+    if (r < 0 || r >= H)
+      continue;
+    for (int b = 0; b < KW; ++b) {
+      const int c = ow * SW - PW + b;
+      if (c < 0 || c >= W)
+        continue;
+      const half *px = x + ((static_cast<long long>(n) * H + r) * W + c) * Ci;
+      const int tap = (a * KW + b) * Ci;
+      for (int ci = 0; ci < Ci; ++ci) {
+        const float xv = __half2float(px[ci]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          acc[j] = fmaf(xv, wsm[(co0 + j) * kstride + tap + ci], acc[j]);
+      }
+    }
+  }
+  Pack8 o;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float v0 = round_half(acc[2 * j]);
+    float v1 = round_half(acc[2 * j + 1]);
+    if (bias) {
+      v0 += __half2float(bias[co0 + 2 * j]);
+      v1 += __half2float(bias[co0 + 2 * j + 1]);
+    }
+    o.h[j] = __floats2half2_rn(apply_act(v0, act), apply_act(v1, act));
+  }
+  *reinterpret_cast<uint4 *>(
+      y + ((static_cast<long long>(n) * OH + oh) * OW + ow) * Co + co0) = o.u;
+}
+
+// ----------------------------------------------------------------- pool
+__global__ void __launch_bounds__(kBlock)
+    pool_nhwc_vec_kernel(const half *__restrict__ x, half *__restrict__ y,
+                         int batch, int C, int H, int W, int OH, int OW,
+                         int KH, int KW, int SH, int SW, int PH, int PW,
+                         bool maximum) {
+  const int groups = C >> 3;
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(batch) * OH * OW * groups;
+  if (i >= total)
+    return;
+  const int g = static_cast<int>(i % groups);
+  long long t = i / groups;
+  const int ow = static_cast<int>(t % OW);
+  t /= OW;
+  const int oh = static_cast<int>(t % OH);
+  const int n = static_cast<int>(t / OH);
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    acc[j] = maximum ? -INFINITY : 0.f;
+  int valid = 0;
+  const int r0 = oh * SH - PH, q0 = ow * SW - PW;
+  for (int a = 0; a < KH; ++a) {
+    for (int b = 0; b < KW; ++b) {
+      const int r = r0 + a, c = q0 + b;
+      if (r < 0 || r >= H || c < 0 || c >= W)
+        continue;
+      Pack8 v;
+      v.u = __ldg(reinterpret_cast<const uint4 *>(
+          x + ((static_cast<long long>(n) * H + r) * W + c) * C + g * 8));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __half22float2(v.h[j]);
+        acc[2 * j] = maximum ? fmaxf(acc[2 * j], f.x) : acc[2 * j] + f.x;
+        acc[2 * j + 1] =
+            maximum ? fmaxf(acc[2 * j + 1], f.y) : acc[2 * j + 1] + f.y;
+      }
+      ++valid;
+    }
+  }
+  Pack8 o;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    o.h[j] = __floats2half2_rn(maximum ? acc[2 * j] : acc[2 * j] / valid,
+                               maximum ? acc[2 * j + 1]
+                                       : acc[2 * j + 1] / valid);
+  *reinterpret_cast<uint4 *>(y + i * 8) = o.u;
+}
+
+__global__ void __launch_bounds__(kBlock)
+    pool_scalar_kernel(const half *__restrict__ x, half *__restrict__ y,
+                       long long total, int C, int H, int W, int OH, int OW,
+                       int KH, int KW, int SH, int SW, int PH, int PW,
+                       bool maximum, bool nhwc) {
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total)
+    return;
+  int c, ow, oh;
+  long long plane;
+  if (nhwc) {
+    c = static_cast<int>(i % C);
+    long long p = i / C;
+    ow = static_cast<int>(p % OW);
+    oh = static_cast<int>((p / OW) % OH);
+    plane = p / (static_cast<long long>(OW) * OH); // batch index
+  } else {
+    ow = static_cast<int>(i % OW);
+    oh = static_cast<int>((i / OW) % OH);
+    plane = i / (static_cast<long long>(OW) * OH);
+    c = 0;
+  }
+  float v = maximum ? -INFINITY : 0.f;
+  int valid = 0;
+  for (int a = 0; a < KH; ++a)
+    for (int b = 0; b < KW; ++b) {
+      const int r = oh * SH - PH + a, q = ow * SW - PW + b;
+      if (r < 0 || r >= H || q < 0 || q >= W)
+        continue;
+      const long long idx =
+          nhwc ? ((plane * H + r) * W + q) * C + c : (plane * H + r) * W + q;
+      const float z = __half2float(x[idx]);
+      v = maximum ? fmaxf(v, z) : v + z;
+      ++valid;
+    }
+  y[i] = __float2half_rn(maximum ? v : v / valid);
+}
+
+// ------------------------------------------------------------------ pad
+__global__ void __launch_bounds__(kBlock)
+    pad_kernel(const half *__restrict__ x, half *__restrict__ y,
+               long long total, int C, int H, int W, int OH, int OW, int PH,
+               int PW, bool vec) {
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total)
+    return;
+  // vec: NHWC, one 8-channel group per thread. !vec with C==1: NCHW planes.
+  const int groups = vec ? C / 8 : C;
+  const int g = static_cast<int>(i % groups);
+  long long p = i / groups;
+  const int ow = static_cast<int>(p % OW);
+  const int oh = static_cast<int>((p / OW) % OH);
+  const long long n = p / (static_cast<long long>(OW) * OH);
+  const int r = oh - PH, c = ow - PW;
+  const bool in = r >= 0 && r < H && c >= 0 && c < W;
+  const long long src = ((n * H + r) * W + c) * C;
+  if (vec) {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (in)
+      v = __ldg(reinterpret_cast<const uint4 *>(x + src + g * 8));
+    *reinterpret_cast<uint4 *>(y + i * 8) = v;
+  } else {
+    y[i] = in ? x[src + g] : __float2half_rn(0.f);
+  }
+}
+
+// --------------------------------------------------------------- resize
+__global__ void __launch_bounds__(kBlock)
+    resize_nhwc_kernel(const half *__restrict__ x,
+                       const half *__restrict__ addend, half *__restrict__ y,
+                       long long total, int C, int H, int W, int OH, int OW,
+                       float sh, float sw, bool vec) {
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total)
+    return;
+  const int groups = vec ? C / 8 : C;
+  const int g = static_cast<int>(i % groups);
+  long long p = i / groups;
+  const int ow = static_cast<int>(p % OW);
+  const int oh = static_cast<int>((p / OW) % OH);
+  const long long n = p / (static_cast<long long>(OW) * OH);
+  const int r = min(static_cast<int>(floorf(oh / sh)), H - 1);
+  const int c = min(static_cast<int>(floorf(ow / sw)), W - 1);
+  const long long src = ((n * H + r) * W + c) * C;
+  if (vec) {
+    Pack8 v;
+    v.u = __ldg(reinterpret_cast<const uint4 *>(x + src + g * 8));
+    if (addend) {
+      Pack8 a;
+      a.u = __ldg(reinterpret_cast<const uint4 *>(addend + i * 8));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __half22float2(v.h[j]), e = __half22float2(a.h[j]);
+        v.h[j] = __floats2half2_rn(f.x + e.x, f.y + e.y);
+      }
+    }
+    *reinterpret_cast<uint4 *>(y + i * 8) = v.u;
+  } else {
+    float v = __half2float(x[src + g]);
+    if (addend)
+      v += __half2float(addend[i]);
+    y[i] = __float2half_rn(v);
+  }
+}
+
+__global__ void __launch_bounds__(kBlock)
+    resize_nchw_kernel(const half *__restrict__ x, half *__restrict__ y,
+                       long long total, int H, int W, int OH, int OW, float sh,
+                       float sw) {
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total)
+    return;
+  const int ow = static_cast<int>(i % OW);
+  const int oh = static_cast<int>((i / OW) % OH);
+  const long long plane = i / (static_cast<long long>(OW) * OH);
+  const int r = min(static_cast<int>(floorf(oh / sh)), H - 1);
+  const int c = min(static_cast<int>(floorf(ow / sw)), W - 1);
+  y[i] = x[(plane * H + r) * W + c];
+}
+
+// --------------------------------------------------------------- concat
+__global__ void __launch_bounds__(kBlock)
+    concat_kernel(const half *__restrict__ a, const half *__restrict__ b,
+                  half *__restrict__ y, long long total, int na, int nb,
+                  bool vec) {
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total)
+    return;
+  const int width = na + nb;
+  const long long row = i / width;
+  const int col = static_cast<int>(i % width);
+  if (vec) {
+    const uint4 *src = col < na ? reinterpret_cast<const uint4 *>(a) + row * na + col
+                                : reinterpret_cast<const uint4 *>(b) + row * nb + (col - na);
+    reinterpret_cast<uint4 *>(y)[i] = __ldg(src);
+  } else {
+    y[i] = col < na ? a[row * na + col] : b[row * nb + col - na];
+  }
+}
+
+// ------------------------------------------------------------ transpose
+__global__ void transpose_kernel(const half *__restrict__ x,
+                                 half *__restrict__ y, int rows, int cols) {
+  __shared__ half tile[32][34];
+  const long long base = static_cast<long long>(blockIdx.z) * rows * cols;
+  int c = blockIdx.x * 32 + threadIdx.x;
+  int r = blockIdx.y * 32 + threadIdx.y;
+  for (int j = 0; j < 32; j += 8)
+    if (c < cols && r + j < rows)
+      tile[threadIdx.y + j][threadIdx.x] =
+          x[base + static_cast<long long>(r + j) * cols + c];
+  __syncthreads();
+  c = blockIdx.y * 32 + threadIdx.x;
+  r = blockIdx.x * 32 + threadIdx.y;
+  for (int j = 0; j < 32; j += 8)
+    if (c < rows && r + j < cols)
+      y[base + static_cast<long long>(r + j) * rows + c] =
+          tile[threadIdx.x][threadIdx.y + j];
+}
+
+__device__ __forceinline__ long long locate(long long i, const Gather &g) {
+  long long off = g.offset;
+  for (int d = g.rank - 1; d >= 0; --d) {
+    off += (i % g.shape[d]) * g.stride[d];
+    i /= g.shape[d];
+  }
+  return off;
+}
+
+__global__ void __launch_bounds__(kBlock)
+    gather_kernel(const half *__restrict__ x, half *__restrict__ y,
+                  long long n, Gather g) {
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n)
+    y[i] = x[locate(i, g)];
+}
+
+__device__ __forceinline__ float binop(float x, float z, int op) {
+  return op == 0   ? x + z
+         : op == 1 ? x - z
+         : op == 2 ? x * z
+         : op == 3 ? x / z
+                   : powf(x, z);
+}
+
+__global__ void __launch_bounds__(kBlock)
+    binary_kernel(const half *__restrict__ a, const half *__restrict__ b,
+                  half *__restrict__ y, long long n, Gather ga, Gather gb,
+                  int op) {
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n)
+    y[i] = __float2half_rn(binop(__half2float(a[locate(i, ga)]),
+                                 __half2float(b[locate(i, gb)]), op));
+}
+
+__device__ __forceinline__ long long flat(long long i, int d, int m) {
+  if (m == 1)
+    return 0;
+  if (d != 1)
+    i /= d;
+  if (m > 1)
+    i %= m;
+  return i;
+}
+
+__global__ void __launch_bounds__(kBlock)
+    binary_flat_kernel(const half *__restrict__ a, const half *__restrict__ b,
+                       half *__restrict__ y, long long n, int ad, int am,
+                       int bd, int bm, int op) {
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n)
+    y[i] = __float2half_rn(binop(__half2float(a[flat(i, ad, am)]),
+                                 __half2float(b[flat(i, bd, bm)]), op));
+}
+
+__global__ void __launch_bounds__(kBlock)
+    unary_kernel(const half *__restrict__ x, half *__restrict__ y, long long n,
+                 int op, float alpha, float beta) {
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n)
+    return;
+  const float v = __half2float(x[i]);
+  float r;
+  switch (op) {
+  case 0:
+    r = fmaxf(v, 0.f);
+    break;
+  case 1:
+    r = 1.f / (1.f + expf(-v));
+    break;
+  case 2:
+    r = fminf(1.f, fmaxf(0.f, alpha * v + beta));
+    break;
+  case 3:
+    r = erff(v);
+    break;
+  case 4:
+    r = sqrtf(v);
+    break;
+  default:
+    r = v;
+  }
+  y[i] = __float2half_rn(r);
+}
+
+__global__ void __launch_bounds__(kBlock)
+    copy_input_f32_kernel(const float *__restrict__ x, half *__restrict__ y,
+                          size_t valid, size_t total) {
+  size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < total)
+    y[i] = i < valid ? __float2half_rn(x[i]) : __float2half_rn(0.f);
+}
+
+// NHWC (valid images) -> NCHW, zero for images >= valid.
+__global__ void __launch_bounds__(kBlock)
+    copy_input_nhwc_kernel(const half *__restrict__ x, half *__restrict__ y,
+                           int valid, long long total, int C, int H, int W) {
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total)
+    return;
+  const int w = static_cast<int>(i % W);
+  const int h = static_cast<int>((i / W) % H);
+  const int c = static_cast<int>((i / (static_cast<long long>(W) * H)) % C);
+  const long long n = i / (static_cast<long long>(W) * H * C);
+  y[i] = n < valid ? x[((n * H + h) * W + w) * C + c] : __float2half_rn(0.f);
+}
+
+__global__ void __launch_bounds__(kBlock)
+    half_to_float_kernel(const half *__restrict__ x, float *__restrict__ y,
+                         size_t n) {
+  size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n)
+    y[i] = __half2float(x[i]);
+}
+
+bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+} // namespace
+
+cudaError_t depthwise(const half *x, const half *w, const half *bias, half *y,
+                      int batch, int C, int H, int W, int OH, int OW, int KH,
+                      int KW, int SH, int SW, int PH, int PW, int act,
+                      cudaStream_t s) {
+  if (batch <= 0 || OH <= 0 || OW <= 0)
+    return cudaSuccess;
+  if (C % 8 || !al16(x) || !al16(y))
+    return cudaErrorInvalidValue;
+#define PB2_DW(kh, kw, sh, sw)                                                 \
+  if (KH == kh && KW == kw && SH == sh && SW == sw)                            \
+    return launch_dw<kh, kw, sh, sw>(x, w, bias, y, batch, C, H, W, OH, OW,    \
+                                     PH, PW, act, s);
+  PB2_DW(3, 3, 1, 1)
+  PB2_DW(3, 3, 2, 2)
+  PB2_DW(3, 3, 2, 1)
+  PB2_DW(5, 5, 1, 1)
+  PB2_DW(5, 5, 2, 2)
+  PB2_DW(1, 7, 1, 1)
+  PB2_DW(9, 9, 1, 1)
+#undef PB2_DW
+  const long long total = static_cast<long long>(batch) * OH * OW * (C / 8);
+  depthwise_generic_kernel<<<blocks_for(total), kBlock, 0, s>>>(
+      x, w, bias, y, batch, C, H, W, OH, OW, KH, KW, SH, SW, PH, PW, act);
+  return cudaGetLastError();
+}
+
+cudaError_t direct_conv(const half *x, const half *w, const half *bias,
+                        half *y, int batch, int Ci, int H, int W, int Co,
+                        int OH, int OW, int KH, int KW, int SH, int SW, int PH,
+                        int PW, int act, cudaStream_t s) {
+  if (batch <= 0 || OH <= 0 || OW <= 0)
+    return cudaSuccess;
+  const size_t smem = sizeof(float) * static_cast<size_t>(Co) * KH * KW * Ci;
+  if (Co % 8 || !al16(y) || smem > 48 * 1024)
+    return cudaErrorInvalidValue;
+  const long long total = static_cast<long long>(batch) * OH * OW * (Co / 8);
+  direct_conv_kernel<<<blocks_for(total), kBlock, smem, s>>>(
+      x, w, bias, y, batch, Ci, H, W, Co, OH, OW, KH, KW, SH, SW, PH, PW, act);
+  return cudaGetLastError();
+}
+
+cudaError_t pool_nhwc(const half *x, half *y, int batch, int C, int H, int W,
+                      int OH, int OW, int KH, int KW, int SH, int SW, int PH,
+                      int PW, bool maximum, cudaStream_t s) {
+  if (C % 8 == 0 && al16(x) && al16(y)) {
+    const long long total = static_cast<long long>(batch) * OH * OW * (C / 8);
+    pool_nhwc_vec_kernel<<<blocks_for(total), kBlock, 0, s>>>(
+        x, y, batch, C, H, W, OH, OW, KH, KW, SH, SW, PH, PW, maximum);
+  } else {
+    const long long total = static_cast<long long>(batch) * OH * OW * C;
+    pool_scalar_kernel<<<blocks_for(total), kBlock, 0, s>>>(
+        x, y, total, C, H, W, OH, OW, KH, KW, SH, SW, PH, PW, maximum, true);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t pool_nchw(const half *x, half *y, int planes, int H, int W, int OH,
+                      int OW, int KH, int KW, int SH, int SW, int PH, int PW,
+                      bool maximum, cudaStream_t s) {
+  const long long total = static_cast<long long>(planes) * OH * OW;
+  pool_scalar_kernel<<<blocks_for(total), kBlock, 0, s>>>(
+      x, y, total, 1, H, W, OH, OW, KH, KW, SH, SW, PH, PW, maximum, false);
+  return cudaGetLastError();
+}
+
+cudaError_t pad_nhwc(const half *x, half *y, int batch, int C, int H, int W,
+                     int OH, int OW, int PH, int PW, cudaStream_t s) {
+  const bool vec = C % 8 == 0 && al16(x) && al16(y);
+  const long long total =
+      static_cast<long long>(batch) * OH * OW * (vec ? C / 8 : C);
+  pad_kernel<<<blocks_for(total), kBlock, 0, s>>>(x, y, total, C, H, W, OH, OW,
+                                                   PH, PW, vec);
+  return cudaGetLastError();
+}
+
+cudaError_t pad_nchw(const half *x, half *y, int planes, int H, int W, int OH,
+                     int OW, int PH, int PW, cudaStream_t s) {
+  const long long total = static_cast<long long>(planes) * OH * OW;
+  pad_kernel<<<blocks_for(total), kBlock, 0, s>>>(x, y, total, 1, H, W, OH, OW,
+                                                   PH, PW, false);
+  return cudaGetLastError();
+}
+
+cudaError_t resize_nearest_nhwc(const half *x, const half *addend, half *y,
+                                int batch, int C, int H, int W, int OH, int OW,
+                                float sh, float sw, cudaStream_t s) {
+  const bool vec =
+      C % 8 == 0 && al16(x) && al16(y) && (!addend || al16(addend));
+  const long long total =
+      static_cast<long long>(batch) * OH * OW * (vec ? C / 8 : C);
+  resize_nhwc_kernel<<<blocks_for(total), kBlock, 0, s>>>(
+      x, addend, y, total, C, H, W, OH, OW, sh, sw, vec);
+  return cudaGetLastError();
+}
+
+cudaError_t resize_nearest_nchw(const half *x, half *y, int planes, int H,
+                                int W, int OH, int OW, float sh, float sw,
+                                cudaStream_t s) {
+  const long long total = static_cast<long long>(planes) * OH * OW;
+  resize_nchw_kernel<<<blocks_for(total), kBlock, 0, s>>>(x, y, total, H, W,
+                                                           OH, OW, sh, sw);
+  return cudaGetLastError();
+}
+
+cudaError_t concat_rows(const half *a, const half *b, half *y, long long rows,
+                        int na, int nb, cudaStream_t s) {
+  const bool vec = na % 8 == 0 && nb % 8 == 0 && al16(a) && al16(b) && al16(y);
+  const int wa = vec ? na / 8 : na, wb = vec ? nb / 8 : nb;
+  const long long total = rows * (wa + wb);
+  concat_kernel<<<blocks_for(total), kBlock, 0, s>>>(a, b, y, total, wa, wb,
+                                                      vec);
+  return cudaGetLastError();
+}
+
+cudaError_t transpose2d(const half *x, half *y, int batch, int rows, int cols,
+                        cudaStream_t s) {
+  if (batch <= 0 || rows <= 0 || cols <= 0)
+    return cudaSuccess;
+  dim3 grid((cols + 31) / 32, (rows + 31) / 32, batch);
+  transpose_kernel<<<grid, dim3(32, 8), 0, s>>>(x, y, rows, cols);
+  return cudaGetLastError();
+}
+
+cudaError_t gather(const half *x, half *y, long long n, const Gather &g,
+                   cudaStream_t s) {
+  if (n <= 0)
+    return cudaSuccess;
+  gather_kernel<<<blocks_for(n), kBlock, 0, s>>>(x, y, n, g);
+  return cudaGetLastError();
+}
+
+cudaError_t binary(const half *a, const half *b, half *y, long long n,
+                   const Gather &ga, const Gather &gb, int op,
+                   cudaStream_t s) {
+  if (n <= 0)
+    return cudaSuccess;
+  binary_kernel<<<blocks_for(n), kBlock, 0, s>>>(a, b, y, n, ga, gb, op);
+  return cudaGetLastError();
+}
+
+cudaError_t binary_flat(const half *a, const half *b, half *y, long long n,
+                        int ad, int am, int bd, int bm, int op,
+                        cudaStream_t s) {
+  if (n <= 0)
+    return cudaSuccess;
+  binary_flat_kernel<<<blocks_for(n), kBlock, 0, s>>>(a, b, y, n, ad, am, bd,
+                                                       bm, op);
+  return cudaGetLastError();
+}
+
+cudaError_t unary(const half *x, half *y, long long n, int op, float alpha,
+                  float beta, cudaStream_t s) {
+  if (n <= 0)
+    return cudaSuccess;
+  unary_kernel<<<blocks_for(n), kBlock, 0, s>>>(x, y, n, op, alpha, beta);
+  return cudaGetLastError();
+}
+
+cudaError_t copy_input_f32(const float *x, half *y, size_t valid, size_t total,
+                           cudaStream_t s) {
+  if (!total)
+    return cudaSuccess;
+  copy_input_f32_kernel<<<blocks_for(static_cast<long long>(total)), kBlock, 0,
+                          s>>>(x, y, valid, total);
+  return cudaGetLastError();
+}
+
+cudaError_t copy_input_nhwc_f16(const half *x, half *y, int valid, int batch,
+                                int C, int H, int W, cudaStream_t s) {
+  const long long total = static_cast<long long>(batch) * C * H * W;
+  if (total <= 0)
+    return cudaSuccess;
+  copy_input_nhwc_kernel<<<blocks_for(total), kBlock, 0, s>>>(x, y, valid,
+                                                              total, C, H, W);
+  return cudaGetLastError();
+}
+
+cudaError_t half_to_float(const half *x, float *y, size_t n, cudaStream_t s) {
+  if (!n)
+    return cudaSuccess;
+  half_to_float_kernel<<<blocks_for(static_cast<long long>(n)), kBlock, 0, s>>>(
+      x, y, n);
+  return cudaGetLastError();
+}
+
+} // namespace pb2

@@ -1,0 +1,573 @@
+// tcgen05 tensor-core GEMM and stride-1 implicit-GEMM convolution for sm_100a.
+//
+// Replaces the reference's 1x1 cublasLt/CUTLASS-Sm80 GEMMs
+// (native/src/compiled/runtime.cuh:514-667, cutlass_gemm.cu:20-120), its
+// cuDNN dense convolutions (runtime.cuh:766-815) and the WMMA vocabulary
+// projection (native/src/kernels/classifier.cu:388-516).
+//
+// Design: one persistent CTA per SM, 6 warps:
+//   warp 0      TMA producer   (one thread) fills a STAGES-deep smem ring
+//   warp 1      UMMA issuer    (one thread) tcgen05.mma 128xBNx16 into TMEM
+//   warps 2..5  epilogue       tcgen05.ld -> fused bias/act/residual -> HBM
+// The TMEM accumulator is double buffered so the epilogue of tile i overlaps
+// the main loop of tile i+1. Operand tiles are K-major, 128-byte swizzled.
+//
+// Implicit GEMM: output rows are enumerated as (image, out_row, 16-pixel
+// segment); one A stage (128 rows x 64 channels of one filter tap) is eight
+// 4-D TMA boxes of 16 pixels x 64 channels at the tap-shifted coordinates.
+// TMA zero-fills out-of-range pixels (the convolution padding), channels past
+// Ci and images past the batch, so no im2col buffer exists.
+#include "kernels.h"
+#include "ptx.cuh"
+#include <cfloat>
+#include <climits>
+#include <mutex>
+#include <vector>
+
+namespace pb2 {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 192;
+
+enum Epi : int { kEpiStore = 0, kEpiVocab = 1 };
+
+struct Args {
+  int M, N;            // GEMM rows (conv: padded row space), columns
+  int num_kb;          // k-blocks per tile
+  int kb_per_tap;      // conv: ceil(Ci/64); gemm: num_kb
+  int KW, pad_h, pad_w;
+  int mt, nt;          // tile grid
+  int Wseg, OH, OW, batch; // conv geometry (Wseg = 16-pixel segments per row)
+  GemmEpilogue epi;
+  float *part_max;
+  int *part_id;
+  float *part_sum;
+  int part_ld, calc_prob;
+  int *err;
+};
+
+template <int BN> struct Cfg {
+  static constexpr uint32_t A_BYTES = kBM * kBK * 2;
+  static constexpr uint32_t B_BYTES = BN * kBK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 256;
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
+  static_assert(B_BYTES % 1024 == 0, "B tile must keep 1024-byte alignment");
+};
+
+__device__ __forceinline__ void fail(const Args &g, volatile int *abort,
+                                     int code) {
+  *abort = 1;
+  if (g.err)
+    atomicCAS(g.err, 0, code);
+}
+
+template <int BN, bool CONV, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap mapA,
+                   const __grid_constant__ CUtensorMap mapB,
+                   const __grid_constant__ Args g) {
+  using C = Cfg<BN>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t *empty = full + STAGES;
+  uint64_t *tfull = empty + STAGES;
+  uint64_t *tempty = tfull + 2;
+  uint64_t *drain = tempty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int total = g.mt * g.nt;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tensormap(&mapA);
+      prefetch_tensormap(&mapB);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;     // stages that received at least one load
+      uint32_t issued_par = 0; // parity of the last phase armed per stage
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        const int mb = tile / g.nt, nb = tile - mb * g.nt;
+        for (int kb = 0; kb < g.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort)) {
+            fail(g, abort, 1);
+            ok = false;
+            break;
+          }
+          uint8_t *sa = smem + stage * C::STAGE_BYTES;
+          uint8_t *sb = sa + C::A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          issued |= 1u << stage;
+          issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+          const int tap = kb / g.kb_per_tap;
+          const int cb = kb - tap * g.kb_per_tap;
+          if (CONV) {
+            const int kh = tap / g.KW, kw = tap - kh * g.KW;
+            const int seg0 = mb * (kBM / 16);
+#pragma unroll 1
+            for (int s = 0; s < kBM / 16; ++s) {
+              const int seg = seg0 + s;
+              const int r = seg / g.Wseg;
+              const int owseg = seg - r * g.Wseg;
+              const int n = r / g.OH;
+              const int oh = r - n * g.OH;
+              tma_load_4d(sa + s * 2048, &mapA, &full[stage], cb * kBK,
+                          owseg * 16 + kw - g.pad_w, oh + kh - g.pad_h, n);
+            }
+            tma_load_3d(sb, &mapB, &full[stage], cb * kBK, tap, nb * BN);
+          } else {
+            tma_load_2d(sa, &mapA, &full[stage], kb * kBK, mb * kBM);
+            tma_load_2d(sb, &mapB, &full[stage], kb * kBK, nb * BN);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Let every load we issued land before the CTA's smem goes away.
+        for (int s = 0; s < STAGES; ++s)
+          if (issued & (1u << s)) {
+            const uint32_t par = (issued_par >> s) & 1u;
+            long long t0 = clock64();
+            while (!mbar_try_wait(&full[s], par) &&
+                   clock64() - t0 < kWaitBudgetCycles) {
+            }
+          }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16_f32(kBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort)) {
+          fail(g, abort, 2);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * C::ACC_COLS;
+        for (int kb = 0; kb < g.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort)) {
+            fail(g, abort, 3);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t b0 = a0 + C::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_f16(d, sdesc_k_sw128(a0 + k * 32), sdesc_k_sw128(b0 + k * 32),
+                     idesc, (kb | k) != 0);
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok)
+          umma_commit(&tfull[acc]);
+      }
+      // Make sure no UMMA is still writing TMEM when it is released.
+      umma_commit(drain);
+      long long t0 = clock64();
+      while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitBudgetCycles) {
+      }
+    }
+  } else {
+    // Epilogue warps: TMEM lane quarter is fixed by warp id modulo 4.
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+      const int mb = tile / g.nt, nb = tile - mb * g.nt;
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort)) {
+        fail(g, abort, 4);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * C::ACC_COLS;
+      // Map this thread's accumulator row to an output row.
+      long long orow = -1;
+      if (CONV) {
+        const int seg = mb * (kBM / 16) + (row_in_tile >> 4);
+        const int r = seg / g.Wseg;
+        const int owseg = seg - r * g.Wseg;
+        const int n = r / g.OH;
+        const int oh = r - n * g.OH;
+        const int ow = owseg * 16 + (row_in_tile & 15);
+        if (n < g.batch && ow < g.OW)
+          orow = (static_cast<long long>(n) * g.OH + oh) * g.OW + ow;
+      } else {
+        const int m = mb * kBM + row_in_tile;
+        if (m < g.M)
+          orow = m;
+      }
+      const int n_base = nb * BN;
+      if (EPI == kEpiStore) {
+        const GemmEpilogue &e = g.epi;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(taddr + c, r);
+          tmem_ld_wait();
+          if (orow >= 0) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int n0 = n_base + c + h * 8;
+              if (n0 + 8 > g.N)
+                continue;
+              float v[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                v[j] = round_half(__uint_as_float(r[h * 8 + j]));
+              if (e.bias) {
+                uint4 bb = __ldg(reinterpret_cast<const uint4 *>(e.bias + n0));
+                const half2 *bh = reinterpret_cast<const half2 *>(&bb);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  float2 f = __half22float2(bh[j]);
+                  v[2 * j] += f.x;
+                  v[2 * j + 1] += f.y;
+                }
+              }
+              if (e.residual) {
+                uint4 rr = __ldg(reinterpret_cast<const uint4 *>(
+                    e.residual + orow * e.ldr + n0));
+                const half2 *rh = reinterpret_cast<const half2 *>(&rr);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  float2 f = __half22float2(rh[j]);
+                  v[2 * j] = round_half(v[2 * j]) + f.x;
+                  v[2 * j + 1] = round_half(v[2 * j + 1]) + f.y;
+                }
+              }
+              uint4 o;
+              half2 *oh2 = reinterpret_cast<half2 *>(&o);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                oh2[j] = __floats2half2_rn(apply_act(v[2 * j], e.act),
+                                           apply_act(v[2 * j + 1], e.act));
+              *reinterpret_cast<uint4 *>(e.out + orow * e.ldo + n0) = o;
+            }
+          }
+        }
+      } else {
+        // Vocabulary tile: fp32 logits = acc + bias, reduced to
+        // (max, lowest argmax, sum exp(l - max)) without leaving registers.
+        float best = -FLT_MAX;
+        int best_id = INT_MAX;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(taddr + c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int col = n_base + c + j;
+            if (col < g.N) {
+              const float l =
+                  __uint_as_float(r[j]) + __half2float(g.epi.bias[col]);
+              if (l > best) {
+                best = l;
+                best_id = col;
+              }
+            }
+          }
+        }
+        float sum = 0.f;
+        if (g.calc_prob) {
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 16) {
+            uint32_t r[16];
+            tmem_ld16(taddr + c, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int col = n_base + c + j;
+              if (col < g.N)
+                sum += __expf(__uint_as_float(r[j]) +
+                              __half2float(g.epi.bias[col]) - best);
+            }
+          }
+        }
+        if (orow >= 0) {
+          const long long p = static_cast<long long>(nb) * g.part_ld + orow;
+          g.part_max[p] = best;
+          g.part_id[p] = best_id;
+          g.part_sum[p] = sum;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ----------------------------------------------------------- host helpers
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t,
+                                 void *, const cuuint64_t *, const cuuint64_t *,
+                                 const cuuint32_t *, const cuuint32_t *,
+                                 CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion,
+                                 CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+  static EncodeTiled fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault,
+                                &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<EncodeTiled>(p);
+  }();
+  return fn;
+}
+
+// fp16 tensor map, innermost dimension first; strides in bytes for dims 1..
+bool encode(CUtensorMap *m, const void *base, int rank, const cuuint64_t *dims,
+            const cuuint64_t *strides, const cuuint32_t *box) {
+  EncodeTiled fn = encoder();
+  if (!fn)
+    return false;
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank,
+                  const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, bool CONV, int EPI>
+cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const Args &g,
+                   cudaStream_t stream) {
+  using C = Cfg<BN>;
+  auto kernel = tc_gemm_kernel<BN, CONV, EPI>;
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr = cudaSuccess;
+  std::call_once(once[dev & 63], [&] {
+    attr = cudaFuncSetAttribute(kernel,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(C::SMEM));
+  });
+  if (attr != cudaSuccess)
+    return attr;
+  const int total = g.mt * g.nt;
+  const int grid = total < sm_count() ? total : sm_count();
+  kernel<<<grid, kThreads, C::SMEM, stream>>>(a, b, g);
+  return cudaGetLastError();
+}
+
+// Picks the UMMA N tile that pads the column count least (ties: larger).
+int pick_bn(int N) {
+  const int cands[] = {256, 128, 64, 48};
+  int best = 256;
+  long long best_pad = -1;
+  for (int bn : cands) {
+    if (bn == 48 && N > 48)
+      continue;
+    long long padded = (static_cast<long long>(N) + bn - 1) / bn * bn;
+    if (best_pad < 0 || padded < best_pad) {
+      best_pad = padded;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+template <bool CONV, int EPI>
+cudaError_t dispatch_bn(int bn, const CUtensorMap &a, const CUtensorMap &b,
+                        const Args &g, cudaStream_t s) {
+  switch (bn) {
+  case 48:
+    return launch<48, CONV, EPI>(a, b, g, s);
+  case 64:
+    return launch<64, CONV, EPI>(a, b, g, s);
+  case 128:
+    return launch<128, CONV, EPI>(a, b, g, s);
+  default:
+    return launch<256, CONV, EPI>(a, b, g, s);
+  }
+}
+
+bool aligned16(const void *p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+}
+
+} // namespace
+
+int vocab_tiles(int V) { return (V + 255) / 256; }
+
+cudaError_t tc_gemm(const half *A, int M, int K, int lda, const half *W, int N,
+                    int ldw, const GemmEpilogue &epi, cudaStream_t stream) {
+  if (M <= 0 || N <= 0)
+    return cudaSuccess;
+  if (K <= 0 || N % 8 || lda % 8 || ldw % 8 || epi.ldo % 8 || !aligned16(A) ||
+      !aligned16(W) || !aligned16(epi.out) ||
+      (epi.bias && !aligned16(epi.bias)) ||
+      (epi.residual && (!aligned16(epi.residual) || epi.ldr % 8)))
+    return cudaErrorInvalidValue;
+  const int bn = pick_bn(N);
+  CUtensorMap ma, mb;
+  cuuint64_t da[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+  cuuint64_t sa[1] = {static_cast<cuuint64_t>(lda) * 2};
+  cuuint32_t ba[2] = {kBK, kBM};
+  cuuint64_t db[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+  cuuint64_t sb[1] = {static_cast<cuuint64_t>(ldw) * 2};
+  cuuint32_t bb[2] = {kBK, static_cast<cuuint32_t>(bn)};
+  if (!encode(&ma, A, 2, da, sa, ba) || !encode(&mb, W, 2, db, sb, bb))
+    return cudaErrorInvalidValue;
+  Args g{};
+  g.M = M;
+  g.N = N;
+  g.num_kb = (K + kBK - 1) / kBK;
+  g.kb_per_tap = g.num_kb;
+  g.KW = 1;
+  g.mt = (M + kBM - 1) / kBM;
+  g.nt = (N + bn - 1) / bn;
+  g.Wseg = g.OH = g.OW = g.batch = 1;
+  g.epi = epi;
+  g.err = device_error_word();
+  return dispatch_bn<false, kEpiStore>(bn, ma, mb, g, stream);
+}
+
+cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
+                    const GemmEpilogue &epi, cudaStream_t stream) {
+  const int OH = s.H + 2 * s.pad_h - s.KH + 1;
+  const int OW = s.W + 2 * s.pad_w - s.KW + 1;
+  if (s.batch <= 0 || OH <= 0 || OW <= 0)
+    return cudaSuccess;
+  if (s.Ci % 8 || s.Co % 8 || epi.ldo % 8 || !aligned16(x) || !aligned16(w) ||
+      !aligned16(epi.out) || (epi.bias && !aligned16(epi.bias)) ||
+      (epi.residual && (!aligned16(epi.residual) || epi.ldr % 8)) ||
+      s.KH * s.KW > 256)
+    return cudaErrorInvalidValue;
+  const int bn = pick_bn(s.Co);
+  const int taps = s.KH * s.KW;
+  CUtensorMap ma, mb;
+  cuuint64_t da[4] = {static_cast<cuuint64_t>(s.Ci), static_cast<cuuint64_t>(s.W),
+                      static_cast<cuuint64_t>(s.H),
+                      static_cast<cuuint64_t>(s.batch)};
+  cuuint64_t sa[3] = {static_cast<cuuint64_t>(s.Ci) * 2,
+                      static_cast<cuuint64_t>(s.W) * s.Ci * 2,
+                      static_cast<cuuint64_t>(s.H) * s.W * s.Ci * 2};
+  cuuint32_t ba[4] = {kBK, 16, 1, 1};
+  cuuint64_t db[3] = {static_cast<cuuint64_t>(s.Ci), static_cast<cuuint64_t>(taps),
+                      static_cast<cuuint64_t>(s.Co)};
+  cuuint64_t sb[2] = {static_cast<cuuint64_t>(s.Ci) * 2,
+                      static_cast<cuuint64_t>(taps) * s.Ci * 2};
+  cuuint32_t bb[3] = {kBK, 1, static_cast<cuuint32_t>(bn)};
+  if (!encode(&ma, x, 4, da, sa, ba) || !encode(&mb, w, 3, db, sb, bb))
+    return cudaErrorInvalidValue;
+  Args g{};
+  g.Wseg = (OW + 15) / 16;
+  g.OH = OH;
+  g.OW = OW;
+  g.batch = s.batch;
+  g.M = s.batch * OH * g.Wseg * 16;
+  g.N = s.Co;
+  g.kb_per_tap = (s.Ci + kBK - 1) / kBK;
+  g.num_kb = g.kb_per_tap * taps;
+  g.KW = s.KW;
+  g.pad_h = s.pad_h;
+  g.pad_w = s.pad_w;
+  g.mt = (g.M + kBM - 1) / kBM;
+  g.nt = (s.Co + bn - 1) / bn;
+  g.epi = epi;
+  g.err = device_error_word();
+  return dispatch_bn<true, kEpiStore>(bn, ma, mb, g, stream);
+}
+
+cudaError_t tc_vocab_partials(const half *hidden, int rows, int H,
+                              const half *wt, const half *bias, int V,
+                              float *part_max, int *part_id, float *part_sum,
+                              int calc_prob, cudaStream_t stream) {
+  if (rows <= 0)
+    return cudaSuccess;
+  if (H <= 0 || H % 8 || V <= 0 || !aligned16(hidden) || !aligned16(wt) ||
+      !bias || !part_max || !part_id || !part_sum)
+    return cudaErrorInvalidValue;
+  CUtensorMap ma, mb;
+  cuuint64_t da[2] = {static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(rows)};
+  cuuint64_t sa[1] = {static_cast<cuuint64_t>(H) * 2};
+  cuuint32_t ba[2] = {kBK, kBM};
+  cuuint64_t db[2] = {static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(V)};
+  cuuint32_t bb[2] = {kBK, 256};
+  if (!encode(&ma, hidden, 2, da, sa, ba) || !encode(&mb, wt, 2, db, sa, bb))
+    return cudaErrorInvalidValue;
+  Args g{};
+  g.M = rows;
+  g.N = V;
+  g.num_kb = (H + kBK - 1) / kBK;
+  g.kb_per_tap = g.num_kb;
+  g.KW = 1;
+  g.mt = (rows + kBM - 1) / kBM;
+  g.nt = vocab_tiles(V);
+  g.Wseg = g.OH = g.OW = g.batch = 1;
+  g.epi.bias = bias;
+  g.part_max = part_max;
+  g.part_id = part_id;
+  g.part_sum = part_sum;
+  g.part_ld = rows;
+  g.calc_prob = calc_prob;
+  g.err = device_error_word();
+  return launch<256, false, kEpiVocab>(ma, mb, g, stream);
+}
+
+} // namespace pb2

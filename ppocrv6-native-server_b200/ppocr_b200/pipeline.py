@@ -1,0 +1,131 @@
+"""Line recognizer and page pipeline over the C-ABI, one replica per GPU.
+
+Mirrors the reference's worker flow (native/src/recognition/
+recognition_worker.cpp:700-746: enqueue the compiled model, launch the
+classifier, collapse; native/src/full_page/full_page_worker.cpp:361-497 for
+pages) with every step on the device: the model graph, the fused vocabulary
+projection + argmax, and the CTC collapse. torch provides device memory and
+streams only.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from . import capi, models, modelgen
+
+
+def _p(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr())
+
+
+class CompiledModel:
+    """One compiled shape: weights (shared), scratch, a handle, CUDA graph."""
+
+    def __init__(self, name: str, device: torch.device, weights_ptr: int | None = None):
+        self.name = name
+        self.device = device
+        self.lib = capi.ModelLibrary(models.library_path(name))
+        info = self.lib.info
+        self.input_shape = tuple(info.input_shape)
+        self.output_shape = tuple(info.output_shape[: info.output_rank])
+        self.output_bytes = info.output_element_bytes
+        with torch.cuda.device(device):
+            self._owns_weights = weights_ptr is None
+            self.weights = weights_ptr or self.lib.load_weights(models.ensure_weights(name))
+            self.scratch = torch.empty(info.scratch_bytes, dtype=torch.uint8, device=device)
+            self.handle = self.lib.create(self.weights, self.scratch.data_ptr(), info.scratch_bytes)
+
+    def output_tensor(self) -> torch.Tensor:
+        dtype = torch.float16 if self.output_bytes == 2 else torch.float32
+        return torch.empty(self.output_shape, dtype=dtype, device=self.device)
+
+    def enqueue_nhwc(self, x: torch.Tensor, out: torch.Tensor, stream: torch.cuda.Stream) -> None:
+        self.lib.enqueue_nhwc_f16(self.handle, x.data_ptr(), out.data_ptr(), x.shape[0],
+                                  ctypes.c_void_p(stream.cuda_stream))
+
+    def enqueue_f32(self, x: torch.Tensor, out: torch.Tensor, stream: torch.cuda.Stream) -> None:
+        self.lib.enqueue(self.handle, x.data_ptr(), out.data_ptr(), x.shape[0],
+                         ctypes.c_void_p(stream.cuda_stream))
+
+    def close(self) -> None:
+        if self.handle:
+            self.lib.destroy(self.handle)
+            self.handle = None
+        if self._owns_weights and self.weights:
+            torch.cuda.synchronize(self.device)
+            capi.load().ppocr_b200_device_free(ctypes.c_void_p(self.weights))
+            self.weights = None
+
+
+class Classifier:
+    """CTC head weights resident on the device in the packed layout."""
+
+    def __init__(self, hidden: int, vocab: int, device: torch.device, seed: int = models.SEED):
+        init = modelgen.Init(seed + 1)
+        w = init.xavier((hidden, vocab), hidden, vocab)
+        b = init.normal((vocab,), 0.0, 0.01)
+        self.hidden, self.vocab = hidden, vocab
+        self.weight_host = w
+        self.bias_host = b
+        self.device = device
+        self.weight = torch.from_numpy(w).to(torch.float16).to(device)
+        self.bias = torch.from_numpy(b).to(torch.float16).to(device)
+        self.packed = torch.empty(vocab, hidden, dtype=torch.float16, device=device)
+        lib = capi.load()
+        capi.check(lib.ppocr_b200_classifier_pack(_p(self.weight), _p(self.packed), hidden, vocab,
+                                                  ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)))
+
+
+class LineRecognizer:
+    """Compiled recognizer shape + head + device collapse on one GPU."""
+
+    def __init__(self, name: str, device: torch.device | str = "cuda:0"):
+        self.device = torch.device(device)
+        self.model = CompiledModel(name, self.device)
+        spec = models.spec("recognizer")
+        self.batch = self.model.input_shape[0]
+        _, self.T, self.H = self.model.output_shape
+        self.vocab = spec["vocab"]
+        self.blank = spec["blank"]
+        with torch.cuda.device(self.device):
+            self.head = Classifier(self.H, self.vocab, self.device)
+            self.stream = torch.cuda.Stream(self.device)
+            rows = self.batch * self.T
+            tiles = (self.vocab + 255) // 256
+            self.hidden = self.model.output_tensor()
+            self.part_id = torch.empty(rows * tiles, dtype=torch.int32, device=self.device)
+            self.part_max = torch.empty(rows * tiles, dtype=torch.float32, device=self.device)
+            self.part_sum = torch.empty(rows * tiles, dtype=torch.float32, device=self.device)
+            self.ids = torch.empty(rows, dtype=torch.int32, device=self.device)
+            self.prob = torch.empty(rows, dtype=torch.float32, device=self.device)
+            self.maxl = torch.empty(rows, dtype=torch.float32, device=self.device)
+            self.out_ids = torch.empty(self.batch, self.T, dtype=torch.int32, device=self.device)
+            self.out_len = torch.empty(self.batch, dtype=torch.int32, device=self.device)
+            self.out_score = torch.empty(self.batch, dtype=torch.float32, device=self.device)
+        self.lib = capi.load()
+
+    def enqueue(self, x_nhwc: torch.Tensor) -> None:
+        """Full forward of an FP16 NHWC batch on self.stream (asynchronous)."""
+        s = ctypes.c_void_p(self.stream.cuda_stream)
+        self.model.enqueue_nhwc(x_nhwc, self.hidden, self.stream)
+        rows = x_nhwc.shape[0] * self.T
+        capi.check(self.lib.ppocr_b200_classifier_run_packed(
+            _p(self.hidden), _p(self.head.packed), _p(self.head.bias), _p(self.ids), _p(self.prob), _p(self.maxl),
+            rows, self.H, self.vocab, _p(self.part_id), _p(self.part_max), _p(self.part_sum), 1, s))
+        capi.check(self.lib.ppocr_b200_ctc_collapse(
+            _p(self.ids), _p(self.prob), x_nhwc.shape[0], self.T, self.blank, _p(self.out_ids), _p(self.out_len),
+            _p(self.out_score), s))
+
+    def results(self, n: int):
+        """Host copy of (ids [n,T], lengths [n], scores [n]) after synchronizing."""
+        self.stream.synchronize()
+        return (self.out_ids[:n].cpu().numpy(), self.out_len[:n].cpu().numpy(),
+                self.out_score[:n].cpu().numpy())
+
+    def close(self) -> None:
+        self.model.close()

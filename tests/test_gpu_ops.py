@@ -1,0 +1,341 @@
+"""Operator parity on the B200: every kernel through the C-ABI
+(include/ppocr_b200_ops.h, include/ppocr_b200_head.h) against the CPU oracle
+(oracle/layers.py, oracle/ctc_oracle.c) on the same seeded inputs."""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ptr, stream_handle
+from helpers import assert_close, dev, f16, host, rng
+from oracle import layers as L
+
+pytestmark = pytest.mark.gpu
+
+
+def sync():
+    torch.cuda.synchronize()
+
+
+def check_device_error(native):
+    assert native.ppocr_b200_device_error() == 0, "a kernel's bounded wait ran out"
+
+
+# ------------------------------------------------------------ tensor cores
+GEMM_CASES = [
+    # rows, ci, co, bias, residual, act
+    (256, 128, 128, True, False, 1),
+    (1000, 120, 360, True, False, 0),   # K tail (120), N tail (360), M tail
+    (333, 240, 120, True, True, 0),     # residual epilogue
+    (130, 64, 48, True, False, 1),      # N tile 48
+    (2048, 1024, 1024, True, False, 1),
+    (512, 2048, 120, True, False, 0),
+    (77, 120, 240, True, False, 5),     # swish
+    (300, 64, 128, True, False, 3),     # hardswish
+    (1, 128, 64, False, False, 0),      # single row, no bias
+]
+
+
+@pytest.mark.parametrize("rows,ci,co,bias,residual,act", GEMM_CASES)
+def test_gemm_epilogue(native, cuda, rows, ci, co, bias, residual, act):
+    r = rng(rows + ci + co)
+    x = f16(r.uniform(-1, 1, (rows, ci)))
+    w = f16(r.standard_normal((co, ci)) * np.sqrt(2.0 / ci))
+    b = f16(r.normal(0, 0.1, co)) if bias else None
+    res = f16(r.uniform(-1, 1, (rows, co))) if residual else None
+    y = torch.empty(rows, co, dtype=torch.float16, device=cuda)
+    dx, dw = dev(x), dev(w)
+    db = dev(b) if bias else None
+    dr = dev(res) if residual else None
+    rc = native.ppocr_b200_gemm_epilogue(ptr(dx), ptr(dw), ptr(db) if bias else None,
+                                         ptr(dr) if residual else None, ptr(y), rows, ci, co, act,
+                                         stream_handle())
+    assert rc == 0, native.ppocr_b200_last_error()
+    sync()
+    check_device_error(native)
+    want = L.gemm(x, w, b, res, act)
+    assert_close(host(y), want, what=f"gemm {rows}x{ci}x{co}")
+
+
+CONV_CASES = [
+    # batch, h, w, ci, co, k
+    (2, 3, 80, 64, 128, 3),
+    (2, 6, 80, 128, 256, 3),
+    (1, 24, 160, 48, 48, 3),    # Ci 48 (channel tail), N tile 48
+    (2, 30, 30, 64, 64, 3),     # width not a multiple of 16
+    (1, 12, 80, 48, 128, 3),
+    (1, 7, 9, 64, 64, 5),       # 5x5, tiny image
+    (3, 3, 80, 512, 256, 3),
+]
+
+
+@pytest.mark.parametrize("batch,h,w,ci,co,k", CONV_CASES)
+def test_implicit_conv(native, cuda, batch, h, w, ci, co, k):
+    r = rng(batch * 7 + h + w + ci + co)
+    x = f16(r.uniform(-1, 1, (batch, h, w, ci)))
+    wt = f16(r.standard_normal((co, k, k, ci)) * np.sqrt(2.0 / (ci * k * k)))
+    b = f16(r.normal(0, 0.1, co))
+    y = torch.empty(batch, h, w, co, dtype=torch.float16, device=cuda)
+    dx, dw, db = dev(x), dev(wt), dev(b)
+    p = k // 2
+    rc = native.ppocr_b200_conv_nhwc(ptr(dx), ptr(dw), ptr(db), ptr(y), batch, ci, h, w, co, k, k,
+                                     1, 1, p, p, 1, 1, stream_handle())
+    assert rc == 0, native.ppocr_b200_last_error()
+    sync()
+    check_device_error(native)
+    want = L.conv_nhwc(x, wt, b, (1, 1), (p, p), 1, 1)
+    assert_close(host(y), want, what=f"conv{k}x{k} {batch}x{h}x{w}x{ci}->{co}")
+
+
+def test_stem_direct_conv(native, cuda):
+    r = rng(3)
+    x = f16(r.uniform(-1, 1, (2, 48, 320, 3)))
+    wt = f16(r.standard_normal((48, 3, 3, 3)) * np.sqrt(2.0 / 27))
+    b = f16(r.normal(0, 0.1, 48))
+    y = torch.empty(2, 24, 160, 48, dtype=torch.float16, device=cuda)
+    dx, dw, db = dev(x), dev(wt), dev(b)
+    rc = native.ppocr_b200_conv_nhwc(ptr(dx), ptr(dw), ptr(db), ptr(y), 2, 3, 48, 320, 48, 3, 3,
+                                     2, 2, 1, 1, 1, 1, stream_handle())
+    assert rc == 0, native.ppocr_b200_last_error()
+    sync()
+    want = L.conv_nhwc(x, wt, b, (2, 2), (1, 1), 1, 1)
+    assert_close(host(y), want, what="stem")
+
+
+# ------------------------------------------------------------ depthwise
+DW_CASES = [
+    # batch, h, w, c, kh, kw, sh, sw, act
+    (2, 24, 160, 48, 3, 3, 2, 2, 1),
+    (2, 12, 80, 128, 3, 3, 2, 1, 1),
+    (2, 3, 80, 1024, 3, 3, 1, 1, 1),
+    (2, 48, 320, 64, 5, 5, 1, 1, 3),   # BASELINE config 2 depthwise 5x5
+    (1, 9, 33, 16, 1, 7, 1, 1, 0),
+    (1, 20, 20, 8, 9, 9, 1, 1, 2),
+]
+
+
+@pytest.mark.parametrize("batch,h,w,c,kh,kw,sh,sw,act", DW_CASES)
+def test_depthwise_bit_exact(native, cuda, batch, h, w, c, kh, kw, sh, sw, act):
+    """Same fp32 FMA tap order as the reference kernel, so bit-exact."""
+    r = rng(h * w + c + kh)
+    x = f16(r.uniform(-1, 1, (batch, h, w, c)))
+    wt = f16(r.standard_normal((c, kh, kw)) * np.sqrt(2.0 / (kh * kw)))
+    b = f16(r.normal(0, 0.1, c))
+    ph, pw = kh // 2, kw // 2
+    oh, ow = (h + 2 * ph - kh) // sh + 1, (w + 2 * pw - kw) // sw + 1
+    y = torch.empty(batch, oh, ow, c, dtype=torch.float16, device=cuda)
+    dx, dw, db = dev(x), dev(wt), dev(b)
+    rc = native.ppocr_b200_conv_nhwc(ptr(dx), ptr(dw), ptr(db), ptr(y), batch, c, h, w, c, kh, kw,
+                                     sh, sw, ph, pw, c, act, stream_handle())
+    assert rc == 0, native.ppocr_b200_last_error()
+    sync()
+    want = L.depthwise_exact(x, wt, b, (sh, sw), (ph, pw), act)
+    got = host(y)
+    if act in (0, 1, 3):
+        assert torch.equal(got, want), f"max diff {(got - want).abs().max().item()}"
+    else:
+        assert_close(got, want, what="depthwise gelu")
+
+
+# ------------------------------------------------------------ sequence ops
+def test_layernorm(native, cuda):
+    r = rng(11)
+    x = f16(r.standard_normal((10240, 120)) * 2 + 0.5)
+    s = f16(r.normal(1, 0.1, 120))
+    b = f16(r.normal(0, 0.1, 120))
+    y = torch.empty(10240, 120, dtype=torch.float16, device=cuda)
+    dx, ds, dbb = dev(x), dev(s), dev(b)
+    assert native.ppocr_b200_layernorm(ptr(dx), ptr(ds), ptr(dbb), ptr(y), 10240, 120, 1e-6,
+                                       stream_handle()) == 0
+    sync()
+    assert_close(host(y), L.layernorm(x, s, b, 1e-6), what="layernorm")
+
+
+def test_softmax(native, cuda):
+    r = rng(12)
+    x = f16(r.standard_normal((4096, 40)) * 3)
+    y = torch.empty(4096, 40, dtype=torch.float16, device=cuda)
+    dx = dev(x)
+    assert native.ppocr_b200_softmax(ptr(dx), ptr(y), 4096, 40, stream_handle()) == 0
+    sync()
+    assert_close(host(y), L.softmax(x), what="softmax")
+
+
+@pytest.mark.parametrize("lines,seq,heads,dh", [(4, 40, 8, 15), (3, 25, 4, 16)])
+def test_attention(native, cuda, lines, seq, heads, dh):
+    r = rng(13 + seq)
+    qkv = f16(r.standard_normal((lines, seq, 3 * heads * dh)))
+    y = torch.empty(lines, seq, heads * dh, dtype=torch.float16, device=cuda)
+    d = dev(qkv)
+    scale = float(np.float32(dh ** -0.5))
+    assert native.ppocr_b200_attention(ptr(d), ptr(y), lines, seq, heads, dh, scale, stream_handle()) == 0
+    sync()
+    assert_close(host(y), L.attention(qkv, heads, dh, scale), what="attention")
+
+
+def test_pools(native, cuda):
+    r = rng(14)
+    x = f16(r.uniform(-2, 2, (3, 3, 80, 256)))
+    y = torch.empty(3, 1, 40, 256, dtype=torch.float16, device=cuda)
+    d = dev(x)
+    assert native.ppocr_b200_pool_nhwc(ptr(d), ptr(y), 3, 256, 3, 80, 3, 2, 3, 2, 0, 0, 0, stream_handle()) == 0
+    sync()
+    assert_close(host(y), L.pool_nhwc(x, (3, 2), (3, 2), (0, 0), False), what="avgpool")
+    y2 = torch.empty(3, 2, 79, 256, dtype=torch.float16, device=cuda)
+    assert native.ppocr_b200_pool_nhwc(ptr(d), ptr(y2), 3, 256, 3, 80, 2, 2, 1, 1, 0, 0, 1, stream_handle()) == 0
+    sync()
+    assert torch.equal(host(y2), L.pool_nhwc(x, (2, 2), (1, 1), (0, 0), True))
+
+
+def test_resize_add_and_concat(native, cuda):
+    r = rng(15)
+    x = f16(r.uniform(-1, 1, (2, 15, 15, 64)))
+    a = f16(r.uniform(-1, 1, (2, 30, 30, 64)))
+    y = torch.empty(2, 30, 30, 64, dtype=torch.float16, device=cuda)
+    dx, da = dev(x), dev(a)
+    assert native.ppocr_b200_resize_nearest_nhwc(ptr(dx), ptr(da), ptr(y), 2, 64, 15, 15, 30, 30, 2.0, 2.0,
+                                                 stream_handle()) == 0
+    sync()
+    assert torch.equal(host(y), L.resize_nearest_nhwc(x, 30, 30, 2.0, 2.0, addend=a))
+    c = torch.empty(2 * 30 * 30, 128, dtype=torch.float16, device=cuda)
+    assert native.ppocr_b200_concat(ptr(da), ptr(y), ptr(c), 2 * 30 * 30, 64, 64, stream_handle()) == 0
+    sync()
+    want = torch.cat([a.reshape(-1, 64), L.resize_nearest_nhwc(x, 30, 30, 2.0, 2.0, addend=a).reshape(-1, 64)], 1)
+    assert torch.equal(host(c), want)
+
+
+@pytest.mark.parametrize("co,act", [(64, 1), (1, 4)])
+def test_deconv(native, cuda, co, act):
+    r = rng(16 + co)
+    x = f16(r.uniform(-1, 1, (2, 16, 16, 64)))
+    w = f16(r.standard_normal((64, 2, 2, co)) * np.sqrt(2.0 / 256))
+    b = f16(r.normal(0, 0.1, co))
+    y = torch.empty(2, 32, 32, co, dtype=torch.float16, device=cuda)
+    dx, dw, db = dev(x), dev(w), dev(b)
+    assert native.ppocr_b200_deconv_nhwc(ptr(dx), ptr(dw), ptr(db), ptr(y), 2, 16, 16, 64, co, 2, 2, act,
+                                         stream_handle()) == 0
+    sync()
+    assert_close(host(y), L.deconv_kxk(x, w, b, act), what="deconv")
+
+
+def test_binarize_bit_exact(native, cuda):
+    r = rng(17)
+    p = r.uniform(0, 1, 960 * 960 + 3).astype(np.float32)
+    p[:5] = [0.3, np.nextafter(np.float32(0.3), 1), np.nextafter(np.float32(0.3), 0), 0.0, 1.0]
+    d = torch.from_numpy(p).cuda()
+    m = torch.empty(p.size, dtype=torch.uint8, device=cuda)
+    assert native.ppocr_b200_binarize(ptr(d), ptr(m), p.size, 0.3, stream_handle()) == 0
+    sync()
+    assert np.array_equal(m.cpu().numpy(), L.binarize(p, 0.3))
+
+
+# ------------------------------------------------------------ CTC head
+def synthetic_logits(r, lines, T, V):
+    """N(0,1) logits, one seeded class per timestep +4,
+    30% of timesteps blank, repeats inserted."""
+    logits = r.standard_normal((lines, T, V)).astype(np.float32)
+    cls = r.integers(1, V, (lines, T))
+    blank = r.random((lines, T)) < 0.3
+    rep = r.random((lines, T)) < 0.2
+    for t in range(1, T):
+        cls[:, t] = np.where(rep[:, t], cls[:, t - 1], cls[:, t])
+    cls = np.where(blank, 0, cls)
+    np.put_along_axis(logits, cls[..., None], np.take_along_axis(logits, cls[..., None], -1) + 4.0, -1)
+    return logits.astype(np.float16)
+
+
+def test_logits_argmax_and_collapse(native, cuda, oracle_c):
+    r = rng(18)
+    lines, T, V = 32, 40, 18385
+    logits = synthetic_logits(r, lines, T, V)
+    rows = lines * T
+    d = torch.from_numpy(logits.reshape(rows, V)).cuda()
+    ids = torch.empty(rows, dtype=torch.int32, device=cuda)
+    prob = torch.empty(rows, dtype=torch.float32, device=cuda)
+    mx = torch.empty(rows, dtype=torch.float32, device=cuda)
+    assert native.ppocr_b200_logits_argmax_prob(ptr(d), rows, V, ptr(ids), ptr(prob), ptr(mx), 1,
+                                                stream_handle()) == 0
+    oid = torch.empty(lines, T, dtype=torch.int32, device=cuda)
+    olen = torch.empty(lines, dtype=torch.int32, device=cuda)
+    osc = torch.empty(lines, dtype=torch.float32, device=cuda)
+    assert native.ppocr_b200_ctc_collapse(ptr(ids), ptr(prob), lines, T, 0, ptr(oid), ptr(olen), ptr(osc),
+                                          stream_handle()) == 0
+    sync()
+    want_ids = np.empty(rows, np.int32)
+    want_prob = np.empty(rows, np.float32)
+    want_max = np.empty(rows, np.float32)
+    oracle_c.oracle_argmax_prob(logits.ctypes.data, rows, V, want_ids.ctypes.data, want_prob.ctypes.data,
+                                want_max.ctypes.data, 4)
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
+    assert np.array_equal(mx.cpu().numpy(), want_max)
+    assert np.abs(prob.cpu().numpy() - want_prob).max() <= 1e-5
+    # Collapse of the oracle's own ids/probs must match the device collapse
+    # of the device ids/probs bit for bit on ids and lengths.
+    c_ids = np.empty((lines, T), np.int32)
+    c_len = np.empty(lines, np.int32)
+    c_sc = np.empty(lines, np.float32)
+    oracle_c.oracle_ctc_collapse(want_ids.ctypes.data, want_prob.ctypes.data, lines, T, 0, c_ids.ctypes.data,
+                                 c_len.ctypes.data, c_sc.ctypes.data)
+    assert np.array_equal(oid.cpu().numpy(), c_ids)
+    assert np.array_equal(olen.cpu().numpy(), c_len)
+    assert np.abs(osc.cpu().numpy() - c_sc).max() <= 1e-5
+
+
+def test_collapse_bit_exact_on_device_inputs(native, cuda, oracle_c):
+    """Same ids/probs in: lengths, ids and float scores identical."""
+    r = rng(19)
+    lines, T = 777, 40
+    ids = r.integers(0, 6, (lines, T)).astype(np.int32)
+    probs = r.random((lines, T)).astype(np.float32)
+    d_ids, d_p = torch.from_numpy(ids).cuda(), torch.from_numpy(probs).cuda()
+    oid = torch.empty(lines, T, dtype=torch.int32, device=cuda)
+    olen = torch.empty(lines, dtype=torch.int32, device=cuda)
+    osc = torch.empty(lines, dtype=torch.float32, device=cuda)
+    assert native.ppocr_b200_ctc_collapse(ptr(d_ids), ptr(d_p), lines, T, 0, ptr(oid), ptr(olen), ptr(osc),
+                                          stream_handle()) == 0
+    sync()
+    c_ids = np.empty((lines, T), np.int32)
+    c_len = np.empty(lines, np.int32)
+    c_sc = np.empty(lines, np.float32)
+    oracle_c.oracle_ctc_collapse(ids.ctypes.data, probs.ctypes.data, lines, T, 0, c_ids.ctypes.data,
+                                 c_len.ctypes.data, c_sc.ctypes.data)
+    assert np.array_equal(oid.cpu().numpy(), c_ids)
+    assert np.array_equal(olen.cpu().numpy(), c_len)
+    assert np.array_equal(osc.cpu().numpy(), c_sc)
+
+
+@pytest.mark.parametrize("rows,H,V", [(1280, 120, 18385), (300, 128, 5000), (16, 120, 300)])
+def test_classifier_projection(native, cuda, rows, H, V):
+    """Fused tcgen05 vocabulary projection + argmax vs fp64 logits on the CPU;
+    ids must agree wherever the oracle's top-2 gap exceeds fp32 noise."""
+    r = rng(20 + V)
+    hid = f16(r.standard_normal((rows, H)))
+    w = f16(r.uniform(-1, 1, (H, V)) * np.sqrt(6.0 / (H + V)) * 4)
+    b = f16(r.normal(0, 0.1, V))
+    dh, dw, db = dev(hid), dev(w), dev(b)
+    ids = torch.empty(rows, dtype=torch.int32, device=cuda)
+    prob = torch.empty(rows, dtype=torch.float32, device=cuda)
+    mx = torch.empty(rows, dtype=torch.float32, device=cuda)
+    nrb, nvb, cnt = ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
+    assert native.ppocr_b200_classifier_workspace(rows, V, 16, 512, ctypes.byref(nrb), ctypes.byref(nvb),
+                                                  ctypes.byref(cnt)) == 0
+    pid = torch.empty(cnt.value, dtype=torch.int32, device=cuda)
+    pmax = torch.empty(cnt.value, dtype=torch.float32, device=cuda)
+    psum = torch.empty(cnt.value, dtype=torch.float32, device=cuda)
+    rc = native.ppocr_b200_linear_argmax_prob(ptr(dh), ptr(dw), ptr(db), ptr(ids), ptr(prob), ptr(mx), rows, H, V,
+                                              512, ptr(pid), ptr(pmax), ptr(psum), 1, stream_handle())
+    assert rc == 0, native.ppocr_b200_last_error()
+    sync()
+    check_device_error(native)
+    logits = hid.double() @ w.double() + b.double()
+    top2 = torch.topk(logits, 2, dim=1).values
+    clear = (top2[:, 0] - top2[:, 1]) > 1e-3
+    want_ids = logits.argmax(1)
+    got_ids = ids.cpu().long()
+    assert clear.float().mean() > 0.9
+    assert torch.equal(got_ids[clear], want_ids[clear])
+    want_prob = 1.0 / torch.exp(logits - logits.max(1, keepdim=True).values).sum(1)
+    assert (prob.cpu().double() - want_prob).abs().max().item() <= 1e-4
+    assert (mx.cpu().double() - logits.max(1).values).abs().max().item() <= 1e-3
