@@ -258,13 +258,12 @@ cudaError_t attention(const half *qkv, half *out, int lines, int seq, int heads,
                        8ull * seq * seq);
   if (smem > 200 * 1024)
     return cudaErrorInvalidValue;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(attention_kernel,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         200 * 1024);
-    configured = true;
-  }
+  // Per-device function attribute; cheap, so set on every call.
+  cudaError_t e = cudaFuncSetAttribute(
+      attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      static_cast<int>(smem));
+  if (e != cudaSuccess)
+    return e;
   attention_kernel<<<lines, 256, smem, s>>>(qkv, out, seq, heads, dh, scale);
   return cudaGetLastError();
 }
