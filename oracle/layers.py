@@ -34,14 +34,22 @@ def act(x: torch.Tensor, code: int) -> torch.Tensor:
     if code == 2:
         return (x * (torch.erf(x / 1.41421354) + 1.0)) * 0.5
     if code == 3:
-        return x * torch.clamp(np.float32(0.166666671634) * x + 0.5, 0.0, 1.0)
+        return x * _hardsigmoid(x)
     if code == 4:
         return 1.0 / (1.0 + torch.exp(-x))
     if code == 5:
         return x * (1.0 / (1.0 + torch.exp(-x)))
     if code == 6:
-        return torch.clamp(np.float32(0.166666671634) * x + 0.5, 0.0, 1.0)
+        return _hardsigmoid(x)
     raise ValueError(code)
+
+
+def _hardsigmoid(x):
+    """clamp(alpha*x + beta) with alpha = float32(1/6), beta = 0.5, the
+    multiply-add rounded once (as nvcc contracts the exporter's expression
+    `(alpha)*(x)+(beta)` into an FMA)."""
+    alpha = float(np.float32(0.166666671634))
+    return torch.clamp((alpha * x.double() + 0.5).float(), 0.0, 1.0)
 
 
 def epilogue(acc, bias=None, residual=None, code=0):

@@ -99,6 +99,38 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map,
       "r"(c2), "r"(c3)
       : "memory");
 }
+// Tiled bulk-tensor stores from this CTA's shared memory (bulk-group
+// completion). Out-of-range rows/columns of the box are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map,
+                                             const void *src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group "
+               "[%0, {%2, %3}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *map,
+                                             const void *src, int c0, int c1,
+                                             int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group "
+               "[%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until at most N of this thread's bulk groups still read smem.
+template <int N> __device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Orders this thread's generic-proxy smem writes before async-proxy reads.
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map))
                : "memory");
@@ -204,20 +236,40 @@ enum Act : int {
   kActHardSigmoid = 6,
 };
 
+__device__ __forceinline__ float apply_act(float x, int act);
+
+// Compile-time activation (ACT >= 0) keeps unrolled epilogues small; ACT < 0
+// falls back to the runtime switch.
+template <int ACT>
+__device__ __forceinline__ float act_t(float x, int act) {
+  if constexpr (ACT < 0)
+    return apply_act(x, act);
+  else if constexpr (ACT == kActNone)
+    return x;
+  else if constexpr (ACT == kActRelu)
+    return fmaxf(x, 0.f);
+  else if constexpr (ACT == kActHardSwish)
+    return x * fminf(1.f, fmaxf(0.f, __fmaf_rn(0.166666671634f, x, 0.5f)));
+  else if constexpr (ACT == kActSwish)
+    return x * (1.f / (1.f + expf(-x)));
+  else
+    return apply_act(x, ACT);
+}
+
 __device__ __forceinline__ float apply_act(float x, int act) {
   switch (act) {
   case kActRelu:
     return fmaxf(x, 0.f);
   case kActGelu:
     return (x * (erff(x / 1.41421354f) + 1.f)) * 0.5f;
-  case kActHardSwish:
-    return x * fminf(1.f, fmaxf(0.f, 0.166666671634f * x + 0.5f));
+  case kActHardSwish: // HardSigmoid(alpha=1/6, beta=1/2) * x, one FMA
+    return x * fminf(1.f, fmaxf(0.f, __fmaf_rn(0.166666671634f, x, 0.5f)));
   case kActSigmoid:
     return 1.f / (1.f + expf(-x));
   case kActSwish:
     return x * (1.f / (1.f + expf(-x)));
   case kActHardSigmoid:
-    return fminf(1.f, fmaxf(0.f, 0.166666671634f * x + 0.5f));
+    return fminf(1.f, fmaxf(0.f, __fmaf_rn(0.166666671634f, x, 0.5f)));
   default:
     return x;
   }

@@ -55,10 +55,59 @@ template <int BN> struct Cfg {
   static constexpr int ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
   static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
   static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
-  static constexpr size_t SMEM = size_t(STAGES) * STAGE_BYTES + 1024 + 256;
+  // TMA-store epilogue: each epilogue warp stages 32 rows x 64 columns
+  // (4 KB, 128-byte swizzled) in a double buffer, then one lane stores it.
+  static constexpr bool TMA_EPI = BN % 64 == 0;
+  static constexpr uint32_t EPI_BYTES = TMA_EPI ? 4 * 2 * 4096 : 0;
+  static constexpr size_t SMEM =
+      size_t(STAGES) * STAGE_BYTES + EPI_BYTES + 1024 + 256;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
   static_assert(B_BYTES % 1024 == 0, "B tile must keep 1024-byte alignment");
+  static_assert(SMEM <= 232448, "dynamic shared memory above 227 KB");
 };
+
+// Fused epilogue for 8 consecutive columns [n0, n0+8) of one accumulator
+// row: v = round(acc) + bias; v = round(v) + residual; y = round(act(v)).
+// Columns at or past N and rows without an output row (orow < 0) skip their
+// bias/residual loads; their values are never stored.
+template <int ACT>
+__device__ __forceinline__ uint4 epilogue8(const uint32_t *acc,
+                                           const GemmEpilogue &e, int n0,
+                                           int N, long long orow) {
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    v[j] = round_half(__uint_as_float(acc[j]));
+  const bool col_ok = n0 + 8 <= N;
+  if (e.bias && col_ok) {
+    uint4 bb = __ldg(reinterpret_cast<const uint4 *>(e.bias + n0));
+    const half2 *bh = reinterpret_cast<const half2 *>(&bb);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __half22float2(bh[j]);
+      v[2 * j] += f.x;
+      v[2 * j + 1] += f.y;
+    }
+  }
+  if (e.residual && col_ok && orow >= 0) {
+    uint4 rr = __ldg(
+        reinterpret_cast<const uint4 *>(e.residual + orow * e.ldr + n0));
+    const half2 *rh = reinterpret_cast<const half2 *>(&rr);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __half22float2(rh[j]);
+      v[2 * j] = round_half(v[2 * j]) + f.x;
+      v[2 * j + 1] = round_half(v[2 * j + 1]) + f.y;
+    }
+  }
+  uint4 o;
+  half2 *oh2 = reinterpret_cast<half2 *>(&o);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    oh2[j] = __floats2half2_rn(act_t<ACT>(v[2 * j], e.act),
+                               act_t<ACT>(v[2 * j + 1], e.act));
+  return o;
+}
 
 __device__ __forceinline__ void fail(const Args &g, volatile int *abort,
                                      int code) {
@@ -67,17 +116,19 @@ __device__ __forceinline__ void fail(const Args &g, volatile int *abort,
     atomicCAS(g.err, 0, code);
 }
 
-template <int BN, bool CONV, int EPI>
+template <int BN, bool CONV, int EPI, int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap mapA,
                    const __grid_constant__ CUtensorMap mapB,
+                   const __grid_constant__ CUtensorMap mapC,
                    const __grid_constant__ Args g) {
   using C = Cfg<BN>;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * C::STAGE_BYTES);
+  uint8_t *epi_smem = smem + STAGES * C::STAGE_BYTES; // 1024-aligned
+  uint64_t *full = reinterpret_cast<uint64_t *>(epi_smem + C::EPI_BYTES);
   uint64_t *empty = full + STAGES;
   uint64_t *tfull = empty + STAGES;
   uint64_t *tempty = tfull + 2;
@@ -122,6 +173,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
         const int mb = tile / g.nt, nb = tile - mb * g.nt;
+        // Implicit GEMM: the 8 pixel segments of this M tile are fixed for
+        // the whole K loop; only the filter tap and channel block move.
+        int seg_x[kBM / 16], seg_y[kBM / 16], seg_n[kBM / 16];
+        if (CONV) {
+#pragma unroll
+          for (int s = 0; s < kBM / 16; ++s) {
+            const int seg = mb * (kBM / 16) + s;
+            const int r = seg / g.Wseg;
+            seg_x[s] = (seg - r * g.Wseg) * 16 - g.pad_w;
+            seg_n[s] = r / g.OH;
+            seg_y[s] = r - seg_n[s] * g.OH - g.pad_h;
+          }
+        }
+        int cb = 0, tap = 0, kh = 0, kw = 0;
         for (int kb = 0; kb < g.num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort)) {
             fail(g, abort, 1);
@@ -133,22 +198,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
           issued |= 1u << stage;
           issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
-          const int tap = kb / g.kb_per_tap;
-          const int cb = kb - tap * g.kb_per_tap;
           if (CONV) {
-            const int kh = tap / g.KW, kw = tap - kh * g.KW;
-            const int seg0 = mb * (kBM / 16);
-#pragma unroll 1
-            for (int s = 0; s < kBM / 16; ++s) {
-              const int seg = seg0 + s;
-              const int r = seg / g.Wseg;
-              const int owseg = seg - r * g.Wseg;
-              const int n = r / g.OH;
-              const int oh = r - n * g.OH;
+#pragma unroll
+            for (int s = 0; s < kBM / 16; ++s)
               tma_load_4d(sa + s * 2048, &mapA, &full[stage], cb * kBK,
-                          owseg * 16 + kw - g.pad_w, oh + kh - g.pad_h, n);
-            }
+                          seg_x[s] + kw, seg_y[s] + kh, seg_n[s]);
             tma_load_3d(sb, &mapB, &full[stage], cb * kBK, tap, nb * BN);
+            if (++cb == g.kb_per_tap) {
+              cb = 0;
+              ++tap;
+              if (++kw == g.KW) {
+                kw = 0;
+                ++kh;
+              }
+            }
           } else {
             tma_load_2d(sa, &mapA, &full[stage], kb * kBK, mb * kBM);
             tma_load_2d(sb, &mapB, &full[stage], kb * kBK, nb * BN);
@@ -221,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int row_in_tile = q * 32 + lane;
     int it = 0;
+    int epi_buf = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
       const int mb = tile / g.nt, nb = tile - mb * g.nt;
       const int acc = it & 1;
@@ -249,7 +313,54 @@ __global__ void __launch_bounds__(kThreads, 1)
           orow = m;
       }
       const int n_base = nb * BN;
-      if (EPI == kEpiStore) {
+      if (EPI == kEpiStore && C::TMA_EPI) {
+        // 64-column chunks: TMEM -> registers -> fused epilogue -> swizzled
+        // smem row (this thread's row) -> one TMA store per warp. TMA drops
+        // rows past M / past the image width and columns past N.
+        const GemmEpilogue &e = g.epi;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 64) {
+          uint32_t r[64];
+          tmem_ld16(taddr + c, *reinterpret_cast<uint32_t(*)[16]>(r));
+          tmem_ld16(taddr + c + 16, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
+          tmem_ld16(taddr + c + 32, *reinterpret_cast<uint32_t(*)[16]>(r + 32));
+          tmem_ld16(taddr + c + 48, *reinterpret_cast<uint32_t(*)[16]>(r + 48));
+          tmem_ld_wait();
+          uint4 packed[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            packed[j] = epilogue8<ACT>(r + 8 * j, e, n_base + c + 8 * j, g.N, orow);
+          // The store issued from this buffer two chunks ago must have read
+          // its source before the buffer is overwritten.
+          if (lane == 0)
+            bulk_wait_read<1>();
+          __syncwarp();
+          uint8_t *buf = epi_smem + (q * 2 + epi_buf) * 4096;
+          uint8_t *row = buf + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4 *>(row + ((j ^ (lane & 7)) << 4)) =
+                packed[j];
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (CONV) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int seg = mb * (kBM / 16) + q * 2 + h;
+                const int rr = seg / g.Wseg;
+                const int n = rr / g.OH;
+                tma_store_4d(&mapC, buf + h * 2048, n_base + c,
+                             (seg - rr * g.Wseg) * 16, rr - n * g.OH, n);
+              }
+            } else {
+              tma_store_2d(&mapC, buf, n_base + c, mb * kBM + q * 32);
+            }
+            bulk_commit();
+          }
+          epi_buf ^= 1;
+        }
+      } else if (EPI == kEpiStore) {
         const GemmEpilogue &e = g.epi;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 16) {
@@ -262,38 +373,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int n0 = n_base + c + h * 8;
               if (n0 + 8 > g.N)
                 continue;
-              float v[8];
-#pragma unroll
-              for (int j = 0; j < 8; ++j)
-                v[j] = round_half(__uint_as_float(r[h * 8 + j]));
-              if (e.bias) {
-                uint4 bb = __ldg(reinterpret_cast<const uint4 *>(e.bias + n0));
-                const half2 *bh = reinterpret_cast<const half2 *>(&bb);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  float2 f = __half22float2(bh[j]);
-                  v[2 * j] += f.x;
-                  v[2 * j + 1] += f.y;
-                }
-              }
-              if (e.residual) {
-                uint4 rr = __ldg(reinterpret_cast<const uint4 *>(
-                    e.residual + orow * e.ldr + n0));
-                const half2 *rh = reinterpret_cast<const half2 *>(&rr);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  float2 f = __half22float2(rh[j]);
-                  v[2 * j] = round_half(v[2 * j]) + f.x;
-                  v[2 * j + 1] = round_half(v[2 * j + 1]) + f.y;
-                }
-              }
-              uint4 o;
-              half2 *oh2 = reinterpret_cast<half2 *>(&o);
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                oh2[j] = __floats2half2_rn(apply_act(v[2 * j], e.act),
-                                           apply_act(v[2 * j + 1], e.act));
-              *reinterpret_cast<uint4 *>(e.out + orow * e.ldo + n0) = o;
+              *reinterpret_cast<uint4 *>(e.out + orow * e.ldo + n0) =
+                  epilogue8<ACT>(r + 8 * h, e, n0, g.N, orow);
             }
           }
         }
@@ -346,6 +427,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }
+    // Output tiles must be fully written before the CTA exits.
+    if (C::TMA_EPI && lane == 0)
+      bulk_wait_all();
   }
 
   tc_fence_before();
@@ -392,11 +476,12 @@ bool encode(CUtensorMap *m, const void *base, int rank, const cuuint64_t *dims,
   return r == CUDA_SUCCESS;
 }
 
-template <int BN, bool CONV, int EPI>
-cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const Args &g,
+template <int BN, bool CONV, int EPI, int ACT>
+cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &c,
+                   const Args &g,
                    cudaStream_t stream) {
   using C = Cfg<BN>;
-  auto kernel = tc_gemm_kernel<BN, CONV, EPI>;
+  auto kernel = tc_gemm_kernel<BN, CONV, EPI, ACT>;
   static std::once_flag once[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -410,7 +495,7 @@ cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const Args &g,
     return attr;
   const int total = g.mt * g.nt;
   const int grid = total < sm_count() ? total : sm_count();
-  kernel<<<grid, kThreads, C::SMEM, stream>>>(a, b, g);
+  kernel<<<grid, kThreads, C::SMEM, stream>>>(a, b, c, g);
   return cudaGetLastError();
 }
 
@@ -431,18 +516,38 @@ int pick_bn(int N) {
   return best;
 }
 
+// Activations used by the generated graphs get their own instantiation; the
+// rest share one with a runtime switch.
+template <int BN, bool CONV, int EPI>
+cudaError_t dispatch_act(const CUtensorMap &a, const CUtensorMap &b,
+                         const CUtensorMap &c, const Args &g, cudaStream_t s) {
+  switch (g.epi.act) {
+  case kActNone:
+    return launch<BN, CONV, EPI, kActNone>(a, b, c, g, s);
+  case kActRelu:
+    return launch<BN, CONV, EPI, kActRelu>(a, b, c, g, s);
+  case kActHardSwish:
+    return launch<BN, CONV, EPI, kActHardSwish>(a, b, c, g, s);
+  case kActSwish:
+    return launch<BN, CONV, EPI, kActSwish>(a, b, c, g, s);
+  default:
+    return launch<BN, CONV, EPI, -1>(a, b, c, g, s);
+  }
+}
+
 template <bool CONV, int EPI>
 cudaError_t dispatch_bn(int bn, const CUtensorMap &a, const CUtensorMap &b,
+                        const CUtensorMap &c,
                         const Args &g, cudaStream_t s) {
   switch (bn) {
   case 48:
-    return launch<48, CONV, EPI>(a, b, g, s);
+    return dispatch_act<48, CONV, EPI>(a, b, c, g, s);
   case 64:
-    return launch<64, CONV, EPI>(a, b, g, s);
+    return dispatch_act<64, CONV, EPI>(a, b, c, g, s);
   case 128:
-    return launch<128, CONV, EPI>(a, b, g, s);
+    return dispatch_act<128, CONV, EPI>(a, b, c, g, s);
   default:
-    return launch<256, CONV, EPI>(a, b, g, s);
+    return dispatch_act<256, CONV, EPI>(a, b, c, g, s);
   }
 }
 
@@ -471,7 +576,13 @@ cudaError_t tc_gemm(const half *A, int M, int K, int lda, const half *W, int N,
   cuuint64_t db[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
   cuuint64_t sb[1] = {static_cast<cuuint64_t>(ldw) * 2};
   cuuint32_t bb[2] = {kBK, static_cast<cuuint32_t>(bn)};
-  if (!encode(&ma, A, 2, da, sa, ba) || !encode(&mb, W, 2, db, sb, bb))
+  // Output map for the TMA-store epilogue: box of 64 columns x 32 rows.
+  CUtensorMap mc;
+  cuuint64_t dc[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
+  cuuint64_t sc[1] = {static_cast<cuuint64_t>(epi.ldo) * 2};
+  cuuint32_t bc[2] = {64, 32};
+  if (!encode(&ma, A, 2, da, sa, ba) || !encode(&mb, W, 2, db, sb, bb) ||
+      !encode(&mc, epi.out, 2, dc, sc, bc))
     return cudaErrorInvalidValue;
   Args g{};
   g.M = M;
@@ -484,7 +595,7 @@ cudaError_t tc_gemm(const half *A, int M, int K, int lda, const half *W, int N,
   g.Wseg = g.OH = g.OW = g.batch = 1;
   g.epi = epi;
   g.err = device_error_word();
-  return dispatch_bn<false, kEpiStore>(bn, ma, mb, g, stream);
+  return dispatch_bn<false, kEpiStore>(bn, ma, mb, mc, g, stream);
 }
 
 cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
@@ -513,7 +624,18 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   cuuint64_t sb[2] = {static_cast<cuuint64_t>(s.Ci) * 2,
                       static_cast<cuuint64_t>(taps) * s.Ci * 2};
   cuuint32_t bb[3] = {kBK, 1, static_cast<cuuint32_t>(bn)};
-  if (!encode(&ma, x, 4, da, sa, ba) || !encode(&mb, w, 3, db, sb, bb))
+  // Output map (NHWC y) for the TMA-store epilogue: one 16-pixel segment of
+  // one output row, 64 channels. Pixels past OW are not written.
+  CUtensorMap mc;
+  cuuint64_t dc[4] = {static_cast<cuuint64_t>(s.Co), static_cast<cuuint64_t>(OW),
+                      static_cast<cuuint64_t>(OH),
+                      static_cast<cuuint64_t>(s.batch)};
+  cuuint64_t sc[3] = {static_cast<cuuint64_t>(epi.ldo) * 2,
+                      static_cast<cuuint64_t>(OW) * epi.ldo * 2,
+                      static_cast<cuuint64_t>(OH) * OW * epi.ldo * 2};
+  cuuint32_t bc[4] = {64, 16, 1, 1};
+  if (!encode(&ma, x, 4, da, sa, ba) || !encode(&mb, w, 3, db, sb, bb) ||
+      !encode(&mc, epi.out, 4, dc, sc, bc))
     return cudaErrorInvalidValue;
   Args g{};
   g.Wseg = (OW + 15) / 16;
@@ -531,7 +653,7 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   g.nt = (s.Co + bn - 1) / bn;
   g.epi = epi;
   g.err = device_error_word();
-  return dispatch_bn<true, kEpiStore>(bn, ma, mb, g, stream);
+  return dispatch_bn<true, kEpiStore>(bn, ma, mb, mc, g, stream);
 }
 
 cudaError_t tc_vocab_partials(const half *hidden, int rows, int H,
@@ -567,7 +689,7 @@ cudaError_t tc_vocab_partials(const half *hidden, int rows, int H,
   g.part_ld = rows;
   g.calc_prob = calc_prob;
   g.err = device_error_word();
-  return launch<256, false, kEpiVocab>(ma, mb, g, stream);
+  return launch<256, false, kEpiVocab, 0>(ma, mb, ma, g, stream);
 }
 
 } // namespace pb2

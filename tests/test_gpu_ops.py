@@ -306,14 +306,31 @@ def test_collapse_bit_exact_on_device_inputs(native, cuda, oracle_c):
     assert np.array_equal(osc.cpu().numpy(), c_sc)
 
 
-@pytest.mark.parametrize("rows,H,V", [(1280, 120, 18385), (300, 128, 5000), (16, 120, 300)])
-def test_classifier_projection(native, cuda, rows, H, V):
-    """Fused tcgen05 vocabulary projection + argmax vs fp64 logits on the CPU;
-    ids must agree wherever the oracle's top-2 gap exceeds fp32 noise."""
-    r = rng(20 + V)
+def _classifier_case(rows, H, V):
+    r = rng(20 + V + H)
     hid = f16(r.standard_normal((rows, H)))
     w = f16(r.uniform(-1, 1, (H, V)) * np.sqrt(6.0 / (H + V)) * 4)
     b = f16(r.normal(0, 0.1, V))
+    return hid, w, b
+
+
+def _check_classifier(hid, w, b, ids, prob, mx):
+    logits = hid.double() @ w.double() + b.double()
+    top2 = torch.topk(logits, 2, dim=1).values
+    clear = (top2[:, 0] - top2[:, 1]) > 1e-3
+    want_ids = logits.argmax(1)
+    got_ids = ids.cpu().long()
+    assert clear.float().mean() > 0.9
+    assert torch.equal(got_ids[clear], want_ids[clear])
+    want_prob = 1.0 / torch.exp(logits - logits.max(1, keepdim=True).values).sum(1)
+    assert (prob.cpu().double() - want_prob).abs().max().item() <= 1e-4
+    assert (mx.cpu().double() - logits.max(1).values).abs().max().item() <= 1e-3
+
+
+@pytest.mark.parametrize("rows,H,V", [(300, 128, 5000), (1280, 128, 18385)])
+def test_classifier_reference_signature(native, cuda, rows, H, V):
+    """Reference-signature entry (weight [H][V] as the worker holds it)."""
+    hid, w, b = _classifier_case(rows, H, V)
     dh, dw, db = dev(hid), dev(w), dev(b)
     ids = torch.empty(rows, dtype=torch.int32, device=cuda)
     prob = torch.empty(rows, dtype=torch.float32, device=cuda)
@@ -329,13 +346,29 @@ def test_classifier_projection(native, cuda, rows, H, V):
     assert rc == 0, native.ppocr_b200_last_error()
     sync()
     check_device_error(native)
-    logits = hid.double() @ w.double() + b.double()
-    top2 = torch.topk(logits, 2, dim=1).values
-    clear = (top2[:, 0] - top2[:, 1]) > 1e-3
-    want_ids = logits.argmax(1)
-    got_ids = ids.cpu().long()
-    assert clear.float().mean() > 0.9
-    assert torch.equal(got_ids[clear], want_ids[clear])
-    want_prob = 1.0 / torch.exp(logits - logits.max(1, keepdim=True).values).sum(1)
-    assert (prob.cpu().double() - want_prob).abs().max().item() <= 1e-4
-    assert (mx.cpu().double() - logits.max(1).values).abs().max().item() <= 1e-3
+    _check_classifier(hid, w, b, ids, prob, mx)
+    # The reference rejects hidden sizes that are not multiples of 16.
+    assert native.ppocr_b200_linear_argmax_prob(ptr(dh), ptr(dw), ptr(db), ptr(ids), ptr(prob), ptr(mx), rows, 120,
+                                                V, 512, ptr(pid), ptr(pmax), ptr(psum), 1, stream_handle()) == -1
+
+
+@pytest.mark.parametrize("rows,H,V", [(20480, 120, 18385), (16, 120, 300), (129, 64, 257)])
+def test_classifier_packed(native, cuda, rows, H, V):
+    """Packed-weight entry used by the pipeline (hidden 120, BASELINE)."""
+    hid, w, b = _classifier_case(rows, H, V)
+    dh, dw, db = dev(hid), dev(w), dev(b)
+    packed = torch.empty(V, H, dtype=torch.float16, device=cuda)
+    assert native.ppocr_b200_classifier_pack(ptr(dw), ptr(packed), H, V, stream_handle()) == 0
+    tiles = (V + 255) // 256
+    pid = torch.empty(rows * tiles, dtype=torch.int32, device=cuda)
+    pmax = torch.empty(rows * tiles, dtype=torch.float32, device=cuda)
+    psum = torch.empty(rows * tiles, dtype=torch.float32, device=cuda)
+    ids = torch.empty(rows, dtype=torch.int32, device=cuda)
+    prob = torch.empty(rows, dtype=torch.float32, device=cuda)
+    mx = torch.empty(rows, dtype=torch.float32, device=cuda)
+    rc = native.ppocr_b200_classifier_run_packed(ptr(dh), ptr(packed), ptr(db), ptr(ids), ptr(prob), ptr(mx), rows,
+                                                 H, V, ptr(pid), ptr(pmax), ptr(psum), 1, stream_handle())
+    assert rc == 0, native.ppocr_b200_last_error()
+    sync()
+    check_device_error(native)
+    _check_classifier(hid, w, b, ids, prob, mx)
