@@ -57,6 +57,23 @@ int ppocr_b200_classifier_run_packed(
     int vocab_size, int *partial_ids, float *partial_max, float *partial_sum,
     int calculate_probability, cudaStream_t stream);
 
+// No counterpart in the reference. Allocation-free form of
+// ppocr_b200_classifier_run_packed for callers that must not call cudaMalloc
+// (their device memory is owned by their own pool allocator, or an
+// allocation would stall a latency-bound request loop). Same arguments and
+// results minus the partial buffers: the partials live in a file-scope
+// device array of this library (about 24 MB per GPU that loads the library,
+// held until the process exits). Limit: rows * ceil(vocab_size/256) must not
+// exceed 2,097,152 (e.g. 29,127 rows at vocab 18,385); larger calls fail with
+// a message. All calls on a device share the array, so calls whose kernels
+// may overlap on the GPU race; order them on one stream. The first call on
+// each device performs a one-time set-up (array lookup and a synchronous
+// clear), so make it before any stream capture on that device.
+int ppocr_b200_classifier_run_packed_noalloc(
+    const void *hidden, const void *packed, const void *bias, int *out_indices,
+    float *out_prob, float *out_max_logits, int rows, int hidden_size,
+    int vocab_size, int calculate_probability, cudaStream_t stream);
+
 // Replaces cuda_selected_class_vs_max_probability (classifier.h:45-49,
 // classifier.cu:111-143): p(class) / (p(class) + p(max)) per row.
 int ppocr_b200_selected_class_vs_max_probability(

@@ -50,6 +50,8 @@ half *pack_buffer(size_t bytes) {
 }
 } // namespace
 
+void pb2::set_last_error(const std::string &message) { g_error = message; }
+
 extern "C" {
 
 const char *ppocr_b200_last_error(void) { return g_error.c_str(); }

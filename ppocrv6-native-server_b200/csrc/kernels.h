@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
+#include <string>
 
 namespace pb2 {
 
@@ -15,6 +16,8 @@ int *device_error_word();
 // Reads and clears the error word of the current device (synchronizes).
 int take_device_error();
 int sm_count();
+// Sets the calling thread's message returned by ppocr_b200_last_error().
+void set_last_error(const std::string &message);
 
 // ------------------------------------------------------------ tensor cores
 // Implicit-GEMM / GEMM on tcgen05. Weights are K-major: [N][taps][Ci].
@@ -45,10 +48,13 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
 // logits[r][v] = hidden[r][:] . wt[v][:] + bias[v] (fp32), reduced over v to
 // (max, lowest argmax, sum exp(l - max)) per vocabulary tile of 256 columns.
 // Partials are laid out [tile][rows]. hidden [rows][H], wt [V][H] (K-major).
+// `err_word` receives a code if a bounded wait runs out; null means the
+// per-device word of device_error_word().
 cudaError_t tc_vocab_partials(const half *hidden, int rows, int H,
                               const half *wt, const half *bias, int V,
                               float *part_max, int *part_id, float *part_sum,
-                              int calc_prob, cudaStream_t stream);
+                              int calc_prob, cudaStream_t stream,
+                              int *err_word = nullptr);
 int vocab_tiles(int V);
 // Merges the per-tile partials into ids/prob/max_logit per row.
 cudaError_t vocab_merge(const float *part_max, const int *part_id,

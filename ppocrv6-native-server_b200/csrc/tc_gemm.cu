@@ -659,7 +659,8 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
 cudaError_t tc_vocab_partials(const half *hidden, int rows, int H,
                               const half *wt, const half *bias, int V,
                               float *part_max, int *part_id, float *part_sum,
-                              int calc_prob, cudaStream_t stream) {
+                              int calc_prob, cudaStream_t stream,
+                              int *err_word) {
   if (rows <= 0)
     return cudaSuccess;
   if (H <= 0 || H % 8 || V <= 0 || !aligned16(hidden) || !aligned16(wt) ||
@@ -688,7 +689,7 @@ cudaError_t tc_vocab_partials(const half *hidden, int rows, int H,
   g.part_sum = part_sum;
   g.part_ld = rows;
   g.calc_prob = calc_prob;
-  g.err = device_error_word();
+  g.err = err_word ? err_word : device_error_word();
   return launch<256, false, kEpiVocab, 0>(ma, mb, ma, g, stream);
 }
 
