@@ -133,6 +133,11 @@ cudaError_t copy_input_nhwc_f16(const half *x, half *y, int valid, int batch,
                                 int C, int H, int W, cudaStream_t stream);
 cudaError_t half_to_float(const half *x, float *y, size_t n,
                           cudaStream_t stream);
+// NCHW f32 (valid images) -> NHWC fp16 with zero images past `valid`: the
+// ABI input copy fused with the exporter's channels-last transpose.
+cudaError_t nchw_f32_to_nhwc_f16(const float *x, half *y, int valid,
+                                 int batch, int C, int H, int W,
+                                 cudaStream_t stream);
 
 // ------------------------------------------------------ sequence kernels
 cudaError_t layernorm(const half *x, const half *scale, const half *bias,

@@ -268,6 +268,8 @@ void Runtime::transpose(int a, int y, Shape xs, Shape ys, Shape perm) {
   } else if (xs.size() == 4 && perm == Shape{0, 1, 3, 2}) {
     batch = xs[0] * xs[1], rows = xs[2], cols = xs[3];
   }
+  if (ops.empty() && a == 0 && xs.size() == 4 && perm == Shape{0, 2, 3, 1})
+    input_nhwc_id = y;
   if (batch) {
     add("transpose", [=] {
       check(transpose2d(t[a], t[y], batch, rows, cols, stream), "transpose");
@@ -405,7 +407,7 @@ void Runtime::run() {
       p();
     prepared = true;
   }
-  for (auto &op : ops)
-    op();
+  for (size_t i = static_cast<size_t>(first_op); i < ops.size(); ++i)
+    ops[i]();
   CU(cudaGetLastError());
 }

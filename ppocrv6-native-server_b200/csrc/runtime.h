@@ -120,9 +120,14 @@ struct Runtime {
   void resize_nearest_add_nhwc(int a, int addend, int y, Shape xs, Shape ys,
                                float sh, float sw);
 
-  // Runs `prepare` once, then every op in order on `stream`.
+  // Runs `prepare` once, then ops[first_op..] in order on `stream`.
   void run();
   bool prepared = false;
+  // When the graph opens with the exporter's channels-last transpose of the
+  // model input (t[0] NCHW -> t[input_nhwc_id] NHWC), the ABI shell writes
+  // t[input_nhwc_id] directly and starts the launch list at first_op = 1.
+  int input_nhwc_id = -1;
+  int first_op = 0;
 
 private:
   std::vector<void *> owned_; // device buffers owned by this runtime

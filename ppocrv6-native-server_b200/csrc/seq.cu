@@ -201,6 +201,79 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Register-resident form for seq <= 64, head_dim <= 16: one block per text
+// line, K and V of every head staged in shared memory as fp32, and each
+// thread owning one (head, query row) at a time with its 64 scores, softmax
+// and output row in registers. Same rounding points as attention_kernel.
+template <int MAXSEQ, int MAXDH>
+__global__ void __launch_bounds__(256)
+    attention_rows_kernel(const half *__restrict__ qkv, half *__restrict__ out,
+                          int seq, int heads, int dh, float scale) {
+  extern __shared__ float sm[];
+  const int hd = heads * dh;
+  const int width = 3 * hd;
+  float *ks = sm;                  // [heads][seq][dh]
+  float *vs = sm + heads * seq * dh;
+  const long long line = blockIdx.x;
+  const half *src = qkv + line * seq * width;
+  for (int j = threadIdx.x; j < seq * hd; j += blockDim.x) {
+    const int i = j / hd, rem = j - i * hd;
+    const int h = rem / dh, d = rem - h * dh;
+    ks[(h * seq + i) * dh + d] = __half2float(src[i * width + hd + rem]);
+    vs[(h * seq + i) * dh + d] = __half2float(src[i * width + 2 * hd + rem]);
+  }
+  __syncthreads();
+  half *dst = out + line * seq * hd;
+  for (int task = threadIdx.x; task < heads * seq; task += blockDim.x) {
+    const int h = task / seq, i = task - h * seq;
+    float q[MAXDH];
+#pragma unroll
+    for (int d = 0; d < MAXDH; ++d)
+      q[d] = d < dh ? round_half(__half2float(src[i * width + h * dh + d]) * scale)
+                    : 0.f;
+    const float *kh = ks + h * seq * dh;
+    float s[MAXSEQ];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < MAXSEQ; ++j) {
+      float acc = 0.f;
+      if (j < seq) {
+#pragma unroll
+        for (int d = 0; d < MAXDH; ++d)
+          if (d < dh)
+            acc = fmaf(q[d], kh[j * dh + d], acc);
+        acc = round_half(acc);
+        m = fmaxf(m, acc);
+      }
+      s[j] = acc;
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < MAXSEQ; ++j)
+      if (j < seq)
+        sum += expf(s[j] - m);
+    const float *vh = vs + h * seq * dh;
+    float o[MAXDH];
+#pragma unroll
+    for (int d = 0; d < MAXDH; ++d)
+      o[d] = 0.f;
+#pragma unroll
+    for (int j = 0; j < MAXSEQ; ++j) {
+      if (j < seq) {
+        const float p = round_half(expf(s[j] - m) / sum);
+#pragma unroll
+        for (int d = 0; d < MAXDH; ++d)
+          if (d < dh)
+            o[d] = fmaf(p, vh[j * dh + d], o[d]);
+      }
+    }
+#pragma unroll
+    for (int d = 0; d < MAXDH; ++d)
+      if (d < dh)
+        dst[i * hd + h * dh + d] = __float2half_rn(o[d]);
+  }
+}
+
 unsigned rows_blocks(int rows) { return static_cast<unsigned>((rows + 7) / 8); }
 
 } // namespace
@@ -253,6 +326,19 @@ cudaError_t attention(const half *qkv, half *out, int lines, int seq, int heads,
                       int dh, float scale, cudaStream_t s) {
   if (lines <= 0)
     return cudaSuccess;
+  if (seq <= 64 && dh <= 16) {
+    const size_t kv = sizeof(float) * 2ull * heads * seq * dh;
+    if (kv <= 200 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(
+          attention_rows_kernel<64, 16>,
+          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kv));
+      if (e != cudaSuccess)
+        return e;
+      attention_rows_kernel<64, 16><<<lines, 256, kv, s>>>(qkv, out, seq, heads,
+                                                            dh, scale);
+      return cudaGetLastError();
+    }
+  }
   const size_t smem =
       sizeof(float) * (static_cast<size_t>(seq) * 3 * heads * dh +
                        8ull * seq * seq);

@@ -33,88 +33,112 @@ inline unsigned blocks_for(long long n, int per_block = kBlock) {
 }
 
 // ------------------------------------------------------------- depthwise
-// Thread = 8 channels x PIX consecutive output columns of one output row.
-// Threads of a warp walk the channel groups of the same pixels, so every
-// 16-byte load and store is coalesced across the warp.
-template <int KH, int KW, int SH, int SW, int PIX>
+// Work item = 8 channels x PIX consecutive output columns of one output row;
+// consecutive threads take consecutive channel groups of the same pixels, so
+// every 16-byte load and store is coalesced across the warp. Per filter row
+// the item loads its input strip ((PIX-1)*SW + KW pixels) once into
+// registers. The filter is staged in shared memory tap-major ([tap][C]) so a
+// tap's 8 weights are one 16-byte load. Blocks loop over items (grid sized
+// to the SM count) so the filter is staged once per block. Sums follow the
+// reference's tap order (row a, then column b) with fp32 FMAs.
+template <int KH, int KW, int SH, int SW, int PIX, int ACT>
 __global__ void __launch_bounds__(kBlock)
     depthwise_kernel(const half *__restrict__ x, const half *__restrict__ w,
                      const half *__restrict__ bias, half *__restrict__ y,
                      int batch, int C, int H, int W, int OH, int OW, int PH,
                      int PW, int act) {
+  extern __shared__ uint4 dw_smem[];
+  half *ws = reinterpret_cast<half *>(dw_smem);
+  constexpr int TAPS = KH * KW;
+  for (int j = threadIdx.x; j < C * TAPS; j += blockDim.x) {
+    const int c = j / TAPS, tap = j - c * TAPS; // w is [C][KH][KW]
+    ws[tap * C + c] = w[j];
+  }
+  __syncthreads();
+  constexpr int NCOL = (PIX - 1) * SW + KW;
   const int groups = C >> 3;
   const int tiles = (OW + PIX - 1) / PIX;
-  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(batch) * OH * tiles * groups;
-  if (i >= total)
-    return;
-  const int g = static_cast<int>(i % groups);
-  long long t = i / groups;
-  const int tile = static_cast<int>(t % tiles);
-  t /= tiles;
-  const int oh = static_cast<int>(t % OH);
-  const int n = static_cast<int>(t / OH);
-  const int c0 = g * 8;
-  const int ow0 = tile * PIX;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < total; i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int g = static_cast<int>(i % groups);
+    long long t = i / groups;
+    const int tile = static_cast<int>(t % tiles);
+    t /= tiles;
+    const int oh = static_cast<int>(t % OH);
+    const int n = static_cast<int>(t / OH);
+    const int c0 = g * 8;
+    const int ow0 = tile * PIX;
+    const int col0 = ow0 * SW - PW;
 
-  float acc[PIX][8];
+    float acc[PIX][8];
 #pragma unroll
-  for (int p = 0; p < PIX; ++p)
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      acc[p][j] = 0.f;
-
-  const half *xn = x + static_cast<long long>(n) * H * W * C;
-#pragma unroll
-  for (int a = 0; a < KH; ++a) {
-    const int r = oh * SH - PH + a;
-    if (r < 0 || r >= H)
-      continue;
-#pragma unroll
-    for (int b = 0; b < KW; ++b) {
-      float wv[8];
+    for (int p = 0; p < PIX; ++p)
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        wv[j] = __half2float(w[(c0 + j) * (KH * KW) + a * KW + b]);
+        acc[p][j] = 0.f;
+
+    const half *xn = x + static_cast<long long>(n) * H * W * C + c0;
 #pragma unroll
-      for (int p = 0; p < PIX; ++p) {
-        const int c = (ow0 + p) * SW - PW + b;
-        if (c < 0 || c >= W)
-          continue;
-        Pack8 v;
-        v.u = __ldg(reinterpret_cast<const uint4 *>(
-            xn + (static_cast<long long>(r) * W + c) * C + c0));
+    for (int a = 0; a < KH; ++a) {
+      const int r = oh * SH - PH + a;
+      if (r < 0 || r >= H)
+        continue;
+      Pack8 strip[NCOL];
+#pragma unroll
+      for (int k = 0; k < NCOL; ++k) {
+        const int c = col0 + k;
+        strip[k].u = (c >= 0 && c < W)
+                         ? __ldg(reinterpret_cast<const uint4 *>(
+                               xn + (static_cast<long long>(r) * W + c) * C))
+                         : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int b = 0; b < KW; ++b) {
+        Pack8 wt;
+        wt.u = *reinterpret_cast<const uint4 *>(ws + (a * KW + b) * C + c0);
+        float wv[8];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          float2 f = __half22float2(v.h[j]);
-          acc[p][2 * j] = fmaf(f.x, wv[2 * j], acc[p][2 * j]);
-          acc[p][2 * j + 1] = fmaf(f.y, wv[2 * j + 1], acc[p][2 * j + 1]);
+          float2 f = __half22float2(wt.h[j]);
+          wv[2 * j] = f.x;
+          wv[2 * j + 1] = f.y;
+        }
+#pragma unroll
+        for (int p = 0; p < PIX; ++p) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float2 f = __half22float2(strip[p * SW + b].h[j]);
+            acc[p][2 * j] = fmaf(f.x, wv[2 * j], acc[p][2 * j]);
+            acc[p][2 * j + 1] = fmaf(f.y, wv[2 * j + 1], acc[p][2 * j + 1]);
+          }
         }
       }
     }
-  }
-  float bv[8];
+    float bv[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j)
-    bv[j] = bias ? __half2float(bias[c0 + j]) : 0.f;
+    for (int j = 0; j < 8; ++j)
+      bv[j] = bias ? __half2float(bias[c0 + j]) : 0.f;
 #pragma unroll
-  for (int p = 0; p < PIX; ++p) {
-    const int ow = ow0 + p;
-    if (ow >= OW)
-      break;
-    Pack8 o;
+    for (int p = 0; p < PIX; ++p) {
+      const int ow = ow0 + p;
+      if (ow >= OW)
+        break;
+      Pack8 o;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float v0 = round_half(acc[p][2 * j]);
-      float v1 = round_half(acc[p][2 * j + 1]);
-      if (bias) {
-        v0 = apply_act(v0 + bv[2 * j], act);
-        v1 = apply_act(v1 + bv[2 * j + 1], act);
+      for (int j = 0; j < 4; ++j) {
+        float v0 = round_half(acc[p][2 * j]);
+        float v1 = round_half(acc[p][2 * j + 1]);
+        if (bias) {
+          v0 = act_t<ACT>(v0 + bv[2 * j], act);
+          v1 = act_t<ACT>(v1 + bv[2 * j + 1], act);
+        }
+        o.h[j] = __floats2half2_rn(v0, v1);
       }
-      o.h[j] = __floats2half2_rn(v0, v1);
+      *reinterpret_cast<uint4 *>(
+          y + ((static_cast<long long>(n) * OH + oh) * OW + ow) * C + c0) =
+          o.u;
     }
-    *reinterpret_cast<uint4 *>(
-        y + ((static_cast<long long>(n) * OH + oh) * OW + ow) * C + c0) = o.u;
   }
 }
 
@@ -185,7 +209,23 @@ cudaError_t launch_dw(const half *x, const half *w, const half *bias, half *y,
   constexpr int PIX = (KW >= 7) ? 2 : 4;
   const long long total =
       static_cast<long long>(batch) * OH * ((OW + PIX - 1) / PIX) * (C / 8);
-  depthwise_kernel<KH, KW, SH, SW, PIX><<<blocks_for(total), kBlock, 0, s>>>(
+  const size_t smem = static_cast<size_t>(C) * KH * KW * sizeof(half);
+  if (smem > 200 * 1024)
+    return cudaErrorInvalidValue;
+  long long blocks = (total + kBlock - 1) / kBlock;
+  const long long cap = static_cast<long long>(sm_count()) * 8;
+  if (blocks > cap)
+    blocks = cap;
+  auto kernel = act == kActRelu ? depthwise_kernel<KH, KW, SH, SW, PIX, kActRelu>
+                                : depthwise_kernel<KH, KW, SH, SW, PIX, -1>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(
+        kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        static_cast<int>(smem));
+    if (e != cudaSuccess)
+      return e;
+  }
+  kernel<<<static_cast<unsigned>(blocks), kBlock, smem, s>>>(
       x, w, bias, y, batch, C, H, W, OH, OW, PH, PW, act);
   return cudaGetLastError();
 }
@@ -251,6 +291,74 @@ __global__ void __launch_bounds__(kBlock)
       y + ((static_cast<long long>(n) * OH + oh) * OW + ow) * Co + co0) = o.u;
 }
 
+// Stem form: thread = one output pixel x all CO output channels. The filter
+// sits in shared memory tap-major ([kh][kw][ci][co], fp32) so each tap's
+// CO weights are read as broadcast float4s; 16-byte output stores.
+template <int CO, int ACT>
+__global__ void __launch_bounds__(kBlock)
+    stem_conv_kernel(const half *__restrict__ x, const half *__restrict__ w,
+                     const half *__restrict__ bias, half *__restrict__ y,
+                     int batch, int Ci, int H, int W, int OH, int OW, int KH,
+                     int KW, int SH, int SW, int PH, int PW, int act) {
+  extern __shared__ float wsm[];
+  const int taps = KH * KW * Ci;
+  for (int j = threadIdx.x; j < taps * CO; j += blockDim.x) {
+    const int co = j / taps, k = j - co * taps; // w is [co][kh][kw][ci]
+    wsm[k * CO + co] = __half2float(w[j]);
+  }
+  __syncthreads();
+  const long long p = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(batch) * OH * OW;
+  if (p >= total)
+    return;
+  const int ow = static_cast<int>(p % OW);
+  const int oh = static_cast<int>((p / OW) % OH);
+  const long long n = p / (static_cast<long long>(OW) * OH);
+  float acc[CO];
+#pragma unroll
+  for (int c = 0; c < CO; ++c)
+    acc[c] = 0.f;
+  for (int a = 0; a < KH; ++a) {
+    const int r = oh * SH - PH + a;
+    if (r < 0 || r >= H)
+      continue;
+    for (int b = 0; b < KW; ++b) {
+      const int c = ow * SW - PW + b;
+      if (c < 0 || c >= W)
+        continue;
+      const half *px = x + ((n * H + r) * W + c) * Ci;
+      const float4 *wt = reinterpret_cast<const float4 *>(wsm + (a * KW + b) * Ci * CO);
+      for (int ci = 0; ci < Ci; ++ci) {
+        const float xv = __half2float(px[ci]);
+#pragma unroll
+        for (int q = 0; q < CO / 4; ++q) {
+          const float4 wv = wt[ci * (CO / 4) + q];
+          acc[4 * q] = fmaf(xv, wv.x, acc[4 * q]);
+          acc[4 * q + 1] = fmaf(xv, wv.y, acc[4 * q + 1]);
+          acc[4 * q + 2] = fmaf(xv, wv.z, acc[4 * q + 2]);
+          acc[4 * q + 3] = fmaf(xv, wv.w, acc[4 * q + 3]);
+        }
+      }
+    }
+  }
+  half *dst = y + p * CO;
+#pragma unroll
+  for (int g = 0; g < CO / 8; ++g) {
+    Pack8 o;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c0 = g * 8 + 2 * j;
+      float v0 = round_half(acc[c0]), v1 = round_half(acc[c0 + 1]);
+      if (bias) {
+        v0 += __half2float(bias[c0]);
+        v1 += __half2float(bias[c0 + 1]);
+      }
+      o.h[j] = __floats2half2_rn(act_t<ACT>(v0, act), act_t<ACT>(v1, act));
+    }
+    *reinterpret_cast<uint4 *>(dst + g * 8) = o.u;
+  }
+}
+
 // ----------------------------------------------------------------- pool
 __global__ void __launch_bounds__(kBlock)
     pool_nhwc_vec_kernel(const half *__restrict__ x, half *__restrict__ y,
@@ -298,6 +406,50 @@ __global__ void __launch_bounds__(kBlock)
     o.h[j] = __floats2half2_rn(maximum ? acc[2 * j] : acc[2 * j] / valid,
                                maximum ? acc[2 * j + 1]
                                        : acc[2 * j + 1] / valid);
+  *reinterpret_cast<uint4 *>(y + i * 8) = o.u;
+}
+
+// Unpadded fixed-window form (the recognizer's 3x2/3x2 average and the
+// stem's 2x2/1 max): every tap is in bounds, so all loads issue together.
+template <int KH, int KW, int SH, int SW, bool MAXIMUM>
+__global__ void __launch_bounds__(kBlock)
+    pool_fixed_kernel(const half *__restrict__ x, half *__restrict__ y,
+                      int batch, int C, int H, int W, int OH, int OW) {
+  const int groups = C >> 3;
+  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(batch) * OH * OW * groups;
+  if (i >= total)
+    return;
+  const int g = static_cast<int>(i % groups);
+  long long t = i / groups;
+  const int ow = static_cast<int>(t % OW);
+  t /= OW;
+  const int oh = static_cast<int>(t % OH);
+  const long long n = t / OH;
+  const half *base = x + ((n * H + oh * SH) * W + ow * SW) * C + g * 8;
+  Pack8 v[KH * KW];
+#pragma unroll
+  for (int a = 0; a < KH; ++a)
+#pragma unroll
+    for (int b = 0; b < KW; ++b)
+      v[a * KW + b].u = __ldg(reinterpret_cast<const uint4 *>(
+          base + (static_cast<long long>(a) * W + b) * C));
+  Pack8 o;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float2 acc = __half22float2(v[0].h[j]);
+#pragma unroll
+    for (int k = 1; k < KH * KW; ++k) {
+      const float2 f = __half22float2(v[k].h[j]);
+      acc.x = MAXIMUM ? fmaxf(acc.x, f.x) : acc.x + f.x;
+      acc.y = MAXIMUM ? fmaxf(acc.y, f.y) : acc.y + f.y;
+    }
+    if (!MAXIMUM) {
+      acc.x /= KH * KW;
+      acc.y /= KH * KW;
+    }
+    o.h[j] = __floats2half2_rn(acc.x, acc.y);
+  }
   *reinterpret_cast<uint4 *>(y + i * 8) = o.u;
 }
 
@@ -576,9 +728,40 @@ __global__ void __launch_bounds__(kBlock)
     y[i] = __half2float(x[i]);
 }
 
+// Thread = one pixel: reads its C values from the C planes (coalesced per
+// plane across the warp), writes C consecutive halves.
+__global__ void __launch_bounds__(kBlock)
+    nchw_to_nhwc_kernel(const float *__restrict__ x, half *__restrict__ y,
+                        int valid, long long pixels, int C, int HW) {
+  long long p = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (p >= pixels)
+    return;
+  const long long n = p / HW;
+  const int s = static_cast<int>(p - n * HW);
+  half *dst = y + p * C;
+  if (n >= valid) {
+    for (int c = 0; c < C; ++c)
+      dst[c] = __float2half_rn(0.f);
+    return;
+  }
+  const float *src = x + n * C * HW + s;
+  for (int c = 0; c < C; ++c)
+    dst[c] = __float2half_rn(__ldg(src + static_cast<long long>(c) * HW));
+}
+
 bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 } // namespace
+
+cudaError_t nchw_f32_to_nhwc_f16(const float *x, half *y, int valid, int batch,
+                                 int C, int H, int W, cudaStream_t s) {
+  const long long pixels = static_cast<long long>(batch) * H * W;
+  if (pixels <= 0)
+    return cudaSuccess;
+  nchw_to_nhwc_kernel<<<blocks_for(pixels), kBlock, 0, s>>>(x, y, valid, pixels,
+                                                             C, H * W);
+  return cudaGetLastError();
+}
 
 cudaError_t depthwise(const half *x, const half *w, const half *bias, half *y,
                       int batch, int C, int H, int W, int OH, int OW, int KH,
@@ -615,6 +798,20 @@ cudaError_t direct_conv(const half *x, const half *w, const half *bias,
   const size_t smem = sizeof(float) * static_cast<size_t>(Co) * KH * KW * Ci;
   if (Co % 8 || !al16(y) || smem > 48 * 1024)
     return cudaErrorInvalidValue;
+  if (Ci <= 4 && (Co == 16 || Co == 32 || Co == 48 || Co == 64)) {
+    const long long pixels = static_cast<long long>(batch) * OH * OW;
+#define PB2_STEM(co)                                                           \
+  if (Co == co) {                                                              \
+    (act == kActRelu ? stem_conv_kernel<co, kActRelu> : stem_conv_kernel<co, -1>)<<<blocks_for(pixels), kBlock, smem, s>>>(             \
+        x, w, bias, y, batch, Ci, H, W, OH, OW, KH, KW, SH, SW, PH, PW, act);  \
+    return cudaGetLastError();                                                 \
+  }
+    PB2_STEM(16)
+    PB2_STEM(32)
+    PB2_STEM(48)
+    PB2_STEM(64)
+#undef PB2_STEM
+  }
   const long long total = static_cast<long long>(batch) * OH * OW * (Co / 8);
   direct_conv_kernel<<<blocks_for(total), kBlock, smem, s>>>(
       x, w, bias, y, batch, Ci, H, W, Co, OH, OW, KH, KW, SH, SW, PH, PW, act);
@@ -624,6 +821,20 @@ cudaError_t direct_conv(const half *x, const half *w, const half *bias,
 cudaError_t pool_nhwc(const half *x, half *y, int batch, int C, int H, int W,
                       int OH, int OW, int KH, int KW, int SH, int SW, int PH,
                       int PW, bool maximum, cudaStream_t s) {
+  if (C % 8 == 0 && al16(x) && al16(y) && PH == 0 && PW == 0 &&
+      (OH - 1) * SH + KH <= H && (OW - 1) * SW + KW <= W) {
+    const long long total = static_cast<long long>(batch) * OH * OW * (C / 8);
+    if (!maximum && KH == 3 && KW == 2 && SH == 3 && SW == 2) {
+      pool_fixed_kernel<3, 2, 3, 2, false><<<blocks_for(total), kBlock, 0, s>>>(
+          x, y, batch, C, H, W, OH, OW);
+      return cudaGetLastError();
+    }
+    if (maximum && KH == 2 && KW == 2 && SH == 1 && SW == 1) {
+      pool_fixed_kernel<2, 2, 1, 1, true><<<blocks_for(total), kBlock, 0, s>>>(
+          x, y, batch, C, H, W, OH, OW);
+      return cudaGetLastError();
+    }
+  }
   if (C % 8 == 0 && al16(x) && al16(y)) {
     const long long total = static_cast<long long>(batch) * OH * OW * (C / 8);
     pool_nhwc_vec_kernel<<<blocks_for(total), kBlock, 0, s>>>(

@@ -168,7 +168,8 @@ class Graph:
                 lines.append(f"r.t[{i}] = r.weights + {offset};")
                 offset += t.const.size
             else:
-                lines.append(f"r.t[{i}] = r.arena + {offsets[self._storage(i)]};")
+                # Tensors no op produces (a truncated graph) get offset 0.
+                lines.append(f"r.t[{i}] = r.arena + {offsets.get(self._storage(i), 0)};")
         for _, _, code in self.ops:
             lines.append(code)
         lines.append("}")

@@ -70,6 +70,22 @@ def test_recognizer_replay_bit_identical_and_nhwc_entry(rec2):
     assert torch.equal(out, a)
 
 
+def test_first_enqueue_equals_replay(cuda):
+    """The first enqueue (eager warm-up + capture + launch) of a fresh handle
+    must give the same output as later graph replays, even though the staged
+    channels-last input shares arena storage with later tensors."""
+    from ppocr_b200 import pipeline
+
+    m = pipeline.CompiledModel("rec_b2", cuda)
+    try:
+        x = _input(2, 48, 320, 9)
+        first = _run_f32(m, x).clone()
+        second = _run_f32(m, x).clone()
+        assert torch.equal(first, second)
+    finally:
+        m.close()
+
+
 def test_recognizer_partial_batch(rec2):
     x = _input(2, 48, 320, 3)
     full = _run_f32(rec2, x).clone()
