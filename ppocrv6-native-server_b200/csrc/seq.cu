@@ -201,76 +201,96 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Register-resident form for seq <= 64, head_dim <= 16: one block per text
-// line, K and V of every head staged in shared memory as fp32, and each
-// thread owning one (head, query row) at a time with its 64 scores, softmax
-// and output row in registers. Same rounding points as attention_kernel.
-template <int MAXSEQ, int MAXDH>
+// Staged form: one block per text line. q' = round(q*scale), k, v, the
+// scores and the probabilities are all fp16-representable (the reference
+// stores each of them as fp16), so they are staged in shared memory as fp16:
+// 72 KB per line at 8 heads x 40 tokens, three resident blocks per SM. Rows
+// are RS = DP + 8 halves apart so 16-byte reads of consecutive key rows hit
+// distinct banks. Three parallel phases: every score (one (head, i, j) per
+// thread step), row softmax (one warp per row), every output (one
+// (head, i, d) per step). Same rounding points and summation order as
+// attention_kernel.
+template <int DP>
 __global__ void __launch_bounds__(256)
-    attention_rows_kernel(const half *__restrict__ qkv, half *__restrict__ out,
-                          int seq, int heads, int dh, float scale) {
-  extern __shared__ float sm[];
+    attention_staged_kernel(const half *__restrict__ qkv,
+                            half *__restrict__ out, int seq, int heads, int dh,
+                            float scale) {
+  constexpr int RS = DP + 8;
+  extern __shared__ uint4 att_smem[];
+  half *qs = reinterpret_cast<half *>(att_smem); // [heads][seq][RS]
+  half *ks = qs + heads * seq * RS;
+  half *vs = ks + heads * seq * RS;
+  half *ss = vs + heads * seq * RS;               // [heads][seq][seq]
   const int hd = heads * dh;
   const int width = 3 * hd;
-  float *ks = sm;                  // [heads][seq][dh]
-  float *vs = sm + heads * seq * dh;
   const long long line = blockIdx.x;
   const half *src = qkv + line * seq * width;
-  for (int j = threadIdx.x; j < seq * hd; j += blockDim.x) {
-    const int i = j / hd, rem = j - i * hd;
-    const int h = rem / dh, d = rem - h * dh;
-    ks[(h * seq + i) * dh + d] = __half2float(src[i * width + hd + rem]);
-    vs[(h * seq + i) * dh + d] = __half2float(src[i * width + 2 * hd + rem]);
+  for (int j = threadIdx.x; j < heads * seq * DP; j += blockDim.x) {
+    const int d = j % DP, hi = j / DP;
+    const int h = hi / seq, i = hi - h * seq;
+    half q = __float2half_rn(0.f), k = q, v = q;
+    if (d < dh) {
+      const half *row = src + i * width + h * dh + d;
+      q = __float2half_rn(__half2float(row[0]) * scale);
+      k = row[hd];
+      v = row[2 * hd];
+    }
+    qs[hi * RS + d] = q;
+    ks[hi * RS + d] = k;
+    vs[hi * RS + d] = v;
   }
   __syncthreads();
-  half *dst = out + line * seq * hd;
-  for (int task = threadIdx.x; task < heads * seq; task += blockDim.x) {
-    const int h = task / seq, i = task - h * seq;
-    float q[MAXDH];
+  // Scores S[h][i][j] = round(q'_i . k_j), d ascending.
+  const int nscore = heads * seq * seq;
+  for (int e = threadIdx.x; e < nscore; e += blockDim.x) {
+    const int j = e % seq, hi = e / seq;
+    const int h = hi / seq;
+    const uint4 *q8 = reinterpret_cast<const uint4 *>(qs + hi * RS);
+    const uint4 *k8 = reinterpret_cast<const uint4 *>(ks + (h * seq + j) * RS);
+    float acc = 0.f;
 #pragma unroll
-    for (int d = 0; d < MAXDH; ++d)
-      q[d] = d < dh ? round_half(__half2float(src[i * width + h * dh + d]) * scale)
-                    : 0.f;
-    const float *kh = ks + h * seq * dh;
-    float s[MAXSEQ];
+    for (int c = 0; c < DP / 8; ++c) {
+      uint4 a = q8[c], b = k8[c];
+      const half2 *a2 = reinterpret_cast<const half2 *>(&a);
+      const half2 *b2 = reinterpret_cast<const half2 *>(&b);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 x = __half22float2(a2[t]), y = __half22float2(b2[t]);
+        acc = fmaf(x.x, y.x, acc);
+        acc = fmaf(x.y, y.y, acc);
+      }
+    }
+    ss[e] = __float2half_rn(acc);
+  }
+  __syncthreads();
+  // Row softmax, one warp per (h, i) row: P = round(exp(s - max) / sum).
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int row = warp; row < heads * seq; row += blockDim.x >> 5) {
+    half *sr = ss + row * seq;
     float m = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < MAXSEQ; ++j) {
-      float acc = 0.f;
-      if (j < seq) {
-#pragma unroll
-        for (int d = 0; d < MAXDH; ++d)
-          if (d < dh)
-            acc = fmaf(q[d], kh[j * dh + d], acc);
-        acc = round_half(acc);
-        m = fmaxf(m, acc);
-      }
-      s[j] = acc;
-    }
+    for (int j = lane; j < seq; j += 32)
+      m = fmaxf(m, __half2float(sr[j]));
+    m = warp_max(m);
     float sum = 0.f;
-#pragma unroll
-    for (int j = 0; j < MAXSEQ; ++j)
-      if (j < seq)
-        sum += expf(s[j] - m);
-    const float *vh = vs + h * seq * dh;
-    float o[MAXDH];
-#pragma unroll
-    for (int d = 0; d < MAXDH; ++d)
-      o[d] = 0.f;
-#pragma unroll
-    for (int j = 0; j < MAXSEQ; ++j) {
-      if (j < seq) {
-        const float p = round_half(expf(s[j] - m) / sum);
-#pragma unroll
-        for (int d = 0; d < MAXDH; ++d)
-          if (d < dh)
-            o[d] = fmaf(p, vh[j * dh + d], o[d]);
-      }
-    }
-#pragma unroll
-    for (int d = 0; d < MAXDH; ++d)
-      if (d < dh)
-        dst[i * hd + h * dh + d] = __float2half_rn(o[d]);
+    for (int j = lane; j < seq; j += 32)
+      sum += expf(__half2float(sr[j]) - m);
+    sum = warp_sum(sum);
+    __syncwarp();
+    for (int j = lane; j < seq; j += 32)
+      sr[j] = __float2half_rn(expf(__half2float(sr[j]) - m) / sum);
+  }
+  __syncthreads();
+  // Outputs O[h][i][d] = round(sum_j P[h][i][j] v[h][j][d]), j ascending.
+  half *dst = out + line * seq * hd;
+  for (int e = threadIdx.x; e < heads * seq * dh; e += blockDim.x) {
+    const int d = e % dh, hi = e / dh;
+    const int h = hi / seq, i = hi - h * seq;
+    const half *pr = ss + hi * seq;
+    const half *vc = vs + h * seq * RS + d;
+    float acc = 0.f;
+    for (int j = 0; j < seq; ++j)
+      acc = fmaf(__half2float(pr[j]), __half2float(vc[j * RS]), acc);
+    dst[i * hd + h * dh + d] = __float2half_rn(acc);
   }
 }
 
@@ -326,16 +346,19 @@ cudaError_t attention(const half *qkv, half *out, int lines, int seq, int heads,
                       int dh, float scale, cudaStream_t s) {
   if (lines <= 0)
     return cudaSuccess;
-  if (seq <= 64 && dh <= 16) {
-    const size_t kv = sizeof(float) * 2ull * heads * seq * dh;
-    if (kv <= 200 * 1024) {
+  if (dh <= 32) {
+    const int dp = dh <= 16 ? 16 : 32;
+    const size_t staged =
+        sizeof(half) * (3ull * heads * seq * (dp + 8) + 1ull * heads * seq * seq);
+    if (staged <= 200 * 1024) {
+      auto kernel = dp == 16 ? attention_staged_kernel<16>
+                             : attention_staged_kernel<32>;
       cudaError_t e = cudaFuncSetAttribute(
-          attention_rows_kernel<64, 16>,
-          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kv));
+          kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+          static_cast<int>(staged));
       if (e != cudaSuccess)
         return e;
-      attention_rows_kernel<64, 16><<<lines, 256, kv, s>>>(qkv, out, seq, heads,
-                                                            dh, scale);
+      kernel<<<lines, 256, staged, s>>>(qkv, out, seq, heads, dh, scale);
       return cudaGetLastError();
     }
   }

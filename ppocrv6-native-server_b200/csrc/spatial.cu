@@ -42,7 +42,7 @@ inline unsigned blocks_for(long long n, int per_block = kBlock) {
 // to the SM count) so the filter is staged once per block. Sums follow the
 // reference's tap order (row a, then column b) with fp32 FMAs.
 template <int KH, int KW, int SH, int SW, int PIX, int ACT>
-__global__ void __launch_bounds__(kBlock)
+__global__ void __launch_bounds__(kBlock, 4)
     depthwise_kernel(const half *__restrict__ x, const half *__restrict__ w,
                      const half *__restrict__ bias, half *__restrict__ y,
                      int batch, int C, int H, int W, int OH, int OW, int PH,
@@ -206,18 +206,23 @@ template <int KH, int KW, int SH, int SW>
 cudaError_t launch_dw(const half *x, const half *w, const half *bias, half *y,
                       int batch, int C, int H, int W, int OH, int OW, int PH,
                       int PW, int act, cudaStream_t s) {
-  constexpr int PIX = (KW >= 7) ? 2 : 4;
+  // Two output columns per item keeps the kernel at <= 64 registers (four
+  // resident blocks per SM) so enough loads are in flight to cover latency.
+  constexpr int PIX = 2;
   const long long total =
       static_cast<long long>(batch) * OH * ((OW + PIX - 1) / PIX) * (C / 8);
   const size_t smem = static_cast<size_t>(C) * KH * KW * sizeof(half);
   if (smem > 200 * 1024)
     return cudaErrorInvalidValue;
   long long blocks = (total + kBlock - 1) / kBlock;
-  const long long cap = static_cast<long long>(sm_count()) * 8;
+  const long long cap = static_cast<long long>(sm_count()) * 16;
   if (blocks > cap)
     blocks = cap;
-  auto kernel = act == kActRelu ? depthwise_kernel<KH, KW, SH, SW, PIX, kActRelu>
-                                : depthwise_kernel<KH, KW, SH, SW, PIX, -1>;
+  auto kernel = act == kActRelu
+                    ? depthwise_kernel<KH, KW, SH, SW, PIX, kActRelu>
+                : act == kActHardSwish
+                    ? depthwise_kernel<KH, KW, SH, SW, PIX, kActHardSwish>
+                    : depthwise_kernel<KH, KW, SH, SW, PIX, -1>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(
         kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -5,16 +5,18 @@
 // cuDNN dense convolutions (runtime.cuh:766-815) and the WMMA vocabulary
 // projection (native/src/kernels/classifier.cu:388-516).
 //
-// Design: one persistent CTA per SM, 6 warps:
+// Design: one persistent CTA per SM:
 //   warp 0      TMA producer   (one thread) fills a STAGES-deep smem ring
 //   warp 1      UMMA issuer    (one thread) tcgen05.mma 128xBNx16 into TMEM
-//   warps 2..5  epilogue       tcgen05.ld -> fused bias/act/residual -> HBM
+//   warps 2..   epilogue       tcgen05.ld -> fused bias/act/residual -> HBM
+//               (4 warps; 16 for the vocabulary argmax/exp reduction)
 // The TMEM accumulator is double buffered so the epilogue of tile i overlaps
 // the main loop of tile i+1. Operand tiles are K-major, 128-byte swizzled.
 //
-// Implicit GEMM: output rows are enumerated as (image, out_row, 16-pixel
-// segment); one A stage (128 rows x 64 channels of one filter tap) is eight
-// 4-D TMA boxes of 16 pixels x 64 channels at the tap-shifted coordinates.
+// Implicit GEMM: output rows are enumerated as (image, out_row, pixel
+// segment of 16 or 32); one A stage (128 rows x 64 channels of one filter
+// tap) is eight (or four) 4-D TMA boxes of one segment x 64 channels at the
+// tap-shifted coordinates.
 // TMA zero-fills out-of-range pixels (the convolution padding), channels past
 // Ci and images past the batch, so no im2col buffer exists.
 #include "kernels.h"
@@ -29,9 +31,16 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
-
 enum Epi : int { kEpiStore = 0, kEpiVocab = 1 };
+
+// Epilogue warps: 4 (one per TMEM lane quarter) for stores; 16 for the
+// exp-heavy vocabulary reduction (four warps per quarter, 64 columns each).
+template <int EPI> struct EpiWarps {
+  static constexpr int value = EPI == kEpiVocab ? 16 : 4;
+};
+template <int EPI> constexpr int threads_for() {
+  return 64 + 32 * EpiWarps<EPI>::value;
+}
 
 struct Args {
   int M, N;            // GEMM rows (conv: padded row space), columns
@@ -39,7 +48,8 @@ struct Args {
   int kb_per_tap;      // conv: ceil(Ci/64); gemm: num_kb
   int KW, pad_h, pad_w;
   int mt, nt;          // tile grid
-  int Wseg, OH, OW, batch; // conv geometry (Wseg = 16-pixel segments per row)
+  int Wseg, OH, OW, batch; // conv geometry (Wseg = pixel segments per row)
+  int seg_log2;            // conv: log2 of the segment length (16 or 32)
   GemmEpilogue epi;
   float *part_max;
   int *part_id;
@@ -117,7 +127,7 @@ __device__ __forceinline__ void fail(const Args &g, volatile int *abort,
 }
 
 template <int BN, bool CONV, int EPI, int ACT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_for<EPI>(), 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap mapA,
                    const __grid_constant__ CUtensorMap mapB,
                    const __grid_constant__ CUtensorMap mapC,
@@ -133,7 +143,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *tfull = empty + STAGES;
   uint64_t *tempty = tfull + 2;
   uint64_t *drain = tempty + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  // [2][4] vocab hand-off (parts 1..3 -> part 0) per (tile parity, lane
+  // quarter). One barrier per parity: a part can run one tile ahead of part
+  // 0 (the other accumulator), but never two, so a parity wait cannot alias.
+  uint64_t *pair = drain + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pair + 8);
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -147,9 +161,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], 32 * EpiWarps<EPI>::value);
     }
     mbar_init(drain, 1);
+    for (int p = 0; p < 8; ++p)
+      mbar_init(&pair[p], 96);
     *abort = 0;
     fence_barrier_init();
   }
@@ -173,15 +189,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
         const int mb = tile / g.nt, nb = tile - mb * g.nt;
-        // Implicit GEMM: the 8 pixel segments of this M tile are fixed for
-        // the whole K loop; only the filter tap and channel block move.
+        // Implicit GEMM: the pixel segments of this M tile (8 of 16 pixels or
+        // 4 of 32) are fixed for the whole K loop; only the filter tap and
+        // channel block move.
+        const int nbox = kBM >> g.seg_log2;
         int seg_x[kBM / 16], seg_y[kBM / 16], seg_n[kBM / 16];
         if (CONV) {
 #pragma unroll
           for (int s = 0; s < kBM / 16; ++s) {
-            const int seg = mb * (kBM / 16) + s;
+            const int seg = (mb << (7 - g.seg_log2)) + s;
             const int r = seg / g.Wseg;
-            seg_x[s] = (seg - r * g.Wseg) * 16 - g.pad_w;
+            seg_x[s] = ((seg - r * g.Wseg) << g.seg_log2) - g.pad_w;
             seg_n[s] = r / g.OH;
             seg_y[s] = r - seg_n[s] * g.OH - g.pad_h;
           }
@@ -201,8 +219,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (CONV) {
 #pragma unroll
             for (int s = 0; s < kBM / 16; ++s)
-              tma_load_4d(sa + s * 2048, &mapA, &full[stage], cb * kBK,
-                          seg_x[s] + kw, seg_y[s] + kh, seg_n[s]);
+              if (s < nbox)
+                tma_load_4d(sa + (s << (g.seg_log2 + 7)), &mapA, &full[stage],
+                            cb * kBK, seg_x[s] + kw, seg_y[s] + kh, seg_n[s]);
             tma_load_3d(sb, &mapB, &full[stage], cb * kBK, tap, nb * BN);
             if (++cb == g.kb_per_tap) {
               cb = 0;
@@ -281,7 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // Epilogue warps: TMEM lane quarter is fixed by warp id modulo 4.
-    const int q = warp & 3;
+    const int q = warp & 3;          // TMEM lane quarter
+    const int hf = (warp - 2) >> 2;  // vocab: column quarter of the tile
     const int row_in_tile = q * 32 + lane;
     int it = 0;
     int epi_buf = 0;
@@ -299,12 +319,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Map this thread's accumulator row to an output row.
       long long orow = -1;
       if (CONV) {
-        const int seg = mb * (kBM / 16) + (row_in_tile >> 4);
+        const int seg = (mb << (7 - g.seg_log2)) + (row_in_tile >> g.seg_log2);
         const int r = seg / g.Wseg;
         const int owseg = seg - r * g.Wseg;
         const int n = r / g.OH;
         const int oh = r - n * g.OH;
-        const int ow = owseg * 16 + (row_in_tile & 15);
+        const int ow = (owseg << g.seg_log2) +
+                       (row_in_tile & ((1 << g.seg_log2) - 1));
         if (n < g.batch && ow < g.OW)
           orow = (static_cast<long long>(n) * g.OH + oh) * g.OW + ow;
       } else {
@@ -345,13 +366,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) {
             if (CONV) {
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int seg = mb * (kBM / 16) + q * 2 + h;
+              // This warp's 32 rows are 32 >> seg_log2 whole segments.
+              for (int h = 0; h < (32 >> g.seg_log2); ++h) {
+                const int seg = (mb << (7 - g.seg_log2)) +
+                                ((q * 32) >> g.seg_log2) + h;
                 const int rr = seg / g.Wseg;
                 const int n = rr / g.OH;
-                tma_store_4d(&mapC, buf + h * 2048, n_base + c,
-                             (seg - rr * g.Wseg) * 16, rr - n * g.OH, n);
+                tma_store_4d(&mapC, buf + (h << (g.seg_log2 + 7)), n_base + c,
+                             (seg - rr * g.Wseg) << g.seg_log2, rr - n * g.OH,
+                             n);
               }
             } else {
               tma_store_2d(&mapC, buf, n_base + c, mb * kBM + q * 32);
@@ -381,47 +404,124 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         // Vocabulary tile: fp32 logits = acc + bias, reduced to
         // (max, lowest argmax, sum exp(l - max)) without leaving registers.
-        float best = -FLT_MAX;
-        int best_id = INT_MAX;
+        // Four warps share each TMEM lane quarter, each reducing 64 of the
+        // tile's 256 columns with 4 independent accumulator lanes (breaks the
+        // compare/add dependency chains). Parts 1..3 hand their result to
+        // part 0 through shared memory (double-buffered by tile parity) and
+        // the per-parity hand-off mbarrier; part 0 merges in column order and
+        // writes the tile's partial.
+        constexpr int PART = BN / 4;
+        const int c_lo = hf * PART;
+        const bool vec_bias =
+            (reinterpret_cast<uintptr_t>(g.epi.bias) & 15) == 0;
+        // Bias for columns [n0, n0+16): two 16-byte loads when aligned and
+        // in range (L1-resident across the warp), guarded scalars otherwise.
+        auto load_bias = [&](int n0, float (&bf)[16]) {
+          if (vec_bias && n0 + 16 <= g.N) {
+            const uint4 b0 = __ldg(reinterpret_cast<const uint4 *>(g.epi.bias + n0));
+            const uint4 b1 = __ldg(reinterpret_cast<const uint4 *>(g.epi.bias + n0 + 8));
+            const half2 *h0 = reinterpret_cast<const half2 *>(&b0);
+            const half2 *h1 = reinterpret_cast<const half2 *>(&b1);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f0 = __half22float2(h0[j]), f1 = __half22float2(h1[j]);
+              bf[2 * j] = f0.x;
+              bf[2 * j + 1] = f0.y;
+              bf[8 + 2 * j] = f1.x;
+              bf[8 + 2 * j + 1] = f1.y;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              bf[j] = n0 + j < g.N ? __half2float(g.epi.bias[n0 + j]) : 0.f;
+          }
+        };
+        float bm[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX};
+        int bi[4] = {INT_MAX, INT_MAX, INT_MAX, INT_MAX};
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
+        for (int c = c_lo; c < c_lo + PART; c += 16) {
+          const int n0 = n_base + c;
           uint32_t r[16];
+          float bf[16];
           tmem_ld16(taddr + c, r);
+          load_bias(n0, bf);
           tmem_ld_wait();
+          const bool full_chunk = n0 + 16 <= g.N;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const int col = n_base + c + j;
-            if (col < g.N) {
-              const float l =
-                  __uint_as_float(r[j]) + __half2float(g.epi.bias[col]);
-              if (l > best) {
-                best = l;
-                best_id = col;
-              }
+            const float l = __uint_as_float(r[j]) + bf[j];
+            if ((full_chunk || n0 + j < g.N) && l > bm[j & 3]) {
+              bm[j & 3] = l;
+              bi[j & 3] = n0 + j;
             }
           }
         }
+        float best = bm[0];
+        int best_id = bi[0];
+#pragma unroll
+        for (int k = 1; k < 4; ++k)
+          if (bm[k] > best || (bm[k] == best && bi[k] < best_id)) {
+            best = bm[k];
+            best_id = bi[k];
+          }
         float sum = 0.f;
         if (g.calc_prob) {
+          float sp[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
-          for (int c = 0; c < BN; c += 16) {
+          for (int c = c_lo; c < c_lo + PART; c += 16) {
+            const int n0 = n_base + c;
             uint32_t r[16];
+            float bf[16];
             tmem_ld16(taddr + c, r);
+            load_bias(n0, bf);
             tmem_ld_wait();
+            const bool full_chunk = n0 + 16 <= g.N;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int col = n_base + c + j;
-              if (col < g.N)
-                sum += __expf(__uint_as_float(r[j]) +
-                              __half2float(g.epi.bias[col]) - best);
+            for (int j = 0; j < 16; ++j)
+              if (full_chunk || n0 + j < g.N)
+                sp[j & 3] += __expf(__uint_as_float(r[j]) + bf[j] - best);
+          }
+          sum = (sp[0] + sp[1]) + (sp[2] + sp[3]);
+        }
+        // Hand-off buffer: [parity][quarter][part 1..3][max | id | sum][lane].
+        float *xb = reinterpret_cast<float *>(epi_smem) + ((it & 1) * 4 + q) * 3 * 96;
+        if (hf > 0) {
+          float *mine = xb + (hf - 1) * 96;
+          mine[lane] = best;
+          reinterpret_cast<int *>(mine)[32 + lane] = best_id;
+          mine[64 + lane] = sum;
+          mbar_arrive(&pair[(it & 1) * 4 + q]);
+        } else {
+          if (!mbar_wait(&pair[(it & 1) * 4 + q], (it >> 1) & 1, abort)) {
+            fail(g, abort, 5);
+            break;
+          }
+          float m = best;
+          int id = best_id;
+          float ms[4], ss[4];
+          ms[0] = best;
+          ss[0] = sum;
+#pragma unroll
+          for (int p = 1; p < 4; ++p) {
+            const float *theirs = xb + (p - 1) * 96;
+            ms[p] = theirs[lane];
+            ss[p] = theirs[64 + lane];
+            const int pid = reinterpret_cast<const int *>(theirs)[32 + lane];
+            if (ms[p] > m) { // parts are in column order: ties keep the lower id
+              m = ms[p];
+              id = pid;
             }
           }
-        }
-        if (orow >= 0) {
-          const long long p = static_cast<long long>(nb) * g.part_ld + orow;
-          g.part_max[p] = best;
-          g.part_id[p] = best_id;
-          g.part_sum[p] = sum;
+          float total_sum = 0.f;
+#pragma unroll
+          for (int p = 0; p < 4; ++p)
+            total_sum += ss[p] == 0.f ? 0.f : ss[p] * __expf(ms[p] - m);
+          if (orow >= 0) {
+            const long long pidx = static_cast<long long>(nb) * g.part_ld + orow;
+            g.part_max[pidx] = m;
+            g.part_id[pidx] = id;
+            g.part_sum[pidx] = total_sum;
+          }
         }
       }
       tc_fence_before();
@@ -495,7 +595,7 @@ cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap
     return attr;
   const int total = g.mt * g.nt;
   const int grid = total < sm_count() ? total : sm_count();
-  kernel<<<grid, kThreads, C::SMEM, stream>>>(a, b, c, g);
+  kernel<<<grid, threads_for<EPI>(), C::SMEM, stream>>>(a, b, c, g);
   return cudaGetLastError();
 }
 
@@ -593,6 +693,7 @@ cudaError_t tc_gemm(const half *A, int M, int K, int lda, const half *W, int N,
   g.mt = (M + kBM - 1) / kBM;
   g.nt = (N + bn - 1) / bn;
   g.Wseg = g.OH = g.OW = g.batch = 1;
+  g.seg_log2 = 4;
   g.epi = epi;
   g.err = device_error_word();
   return dispatch_bn<false, kEpiStore>(bn, ma, mb, mc, g, stream);
@@ -611,6 +712,10 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
     return cudaErrorInvalidValue;
   const int bn = pick_bn(s.Co);
   const int taps = s.KH * s.KW;
+  // Segment length: 32 pixels when it divides the output width (fewer TMA
+  // boxes per stage), else 16.
+  const int seg_log2 = OW % 32 == 0 ? 5 : 4;
+  const cuuint32_t seg = 1u << seg_log2;
   CUtensorMap ma, mb;
   cuuint64_t da[4] = {static_cast<cuuint64_t>(s.Ci), static_cast<cuuint64_t>(s.W),
                       static_cast<cuuint64_t>(s.H),
@@ -618,13 +723,13 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   cuuint64_t sa[3] = {static_cast<cuuint64_t>(s.Ci) * 2,
                       static_cast<cuuint64_t>(s.W) * s.Ci * 2,
                       static_cast<cuuint64_t>(s.H) * s.W * s.Ci * 2};
-  cuuint32_t ba[4] = {kBK, 16, 1, 1};
+  cuuint32_t ba[4] = {kBK, seg, 1, 1};
   cuuint64_t db[3] = {static_cast<cuuint64_t>(s.Ci), static_cast<cuuint64_t>(taps),
                       static_cast<cuuint64_t>(s.Co)};
   cuuint64_t sb[2] = {static_cast<cuuint64_t>(s.Ci) * 2,
                       static_cast<cuuint64_t>(taps) * s.Ci * 2};
   cuuint32_t bb[3] = {kBK, 1, static_cast<cuuint32_t>(bn)};
-  // Output map (NHWC y) for the TMA-store epilogue: one 16-pixel segment of
+  // Output map (NHWC y) for the TMA-store epilogue: one pixel segment of
   // one output row, 64 channels. Pixels past OW are not written.
   CUtensorMap mc;
   cuuint64_t dc[4] = {static_cast<cuuint64_t>(s.Co), static_cast<cuuint64_t>(OW),
@@ -633,16 +738,17 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   cuuint64_t sc[3] = {static_cast<cuuint64_t>(epi.ldo) * 2,
                       static_cast<cuuint64_t>(OW) * epi.ldo * 2,
                       static_cast<cuuint64_t>(OH) * OW * epi.ldo * 2};
-  cuuint32_t bc[4] = {64, 16, 1, 1};
+  cuuint32_t bc[4] = {64, seg, 1, 1};
   if (!encode(&ma, x, 4, da, sa, ba) || !encode(&mb, w, 3, db, sb, bb) ||
       !encode(&mc, epi.out, 4, dc, sc, bc))
     return cudaErrorInvalidValue;
   Args g{};
-  g.Wseg = (OW + 15) / 16;
+  g.seg_log2 = seg_log2;
+  g.Wseg = (OW + static_cast<int>(seg) - 1) / static_cast<int>(seg);
   g.OH = OH;
   g.OW = OW;
   g.batch = s.batch;
-  g.M = s.batch * OH * g.Wseg * 16;
+  g.M = s.batch * OH * g.Wseg * static_cast<int>(seg);
   g.N = s.Co;
   g.kb_per_tap = (s.Ci + kBK - 1) / kBK;
   g.num_kb = g.kb_per_tap * taps;
@@ -683,6 +789,7 @@ cudaError_t tc_vocab_partials(const half *hidden, int rows, int H,
   g.mt = (rows + kBM - 1) / kBM;
   g.nt = vocab_tiles(V);
   g.Wseg = g.OH = g.OW = g.batch = 1;
+  g.seg_log2 = 4;
   g.epi.bias = bias;
   g.part_max = part_max;
   g.part_id = part_id;

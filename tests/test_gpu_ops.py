@@ -163,7 +163,8 @@ def test_softmax(native, cuda):
     assert_close(host(y), L.softmax(x), what="softmax")
 
 
-@pytest.mark.parametrize("lines,seq,heads,dh", [(4, 40, 8, 15), (3, 25, 4, 16), (2, 20, 2, 24), (2, 70, 2, 8)])
+@pytest.mark.parametrize("lines,seq,heads,dh", [(4, 40, 8, 15), (3, 25, 4, 16), (2, 20, 2, 24), (2, 70, 2, 8),
+                                               (1, 10, 2, 40)])
 def test_attention(native, cuda, lines, seq, heads, dh):
     r = rng(13 + seq)
     qkv = f16(r.standard_normal((lines, seq, 3 * heads * dh)))
