@@ -44,6 +44,12 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--model", default=MODEL, choices=["rec_b512", "rec_b256", "rec_b64"],
+                   help="compiled recognizer shape of the c4 run (rec_b512 = the benchmark; the smaller "
+                        "shapes exist for profiling captures and are named in the output's config)")
+    p.add_argument("--config", default="c4", choices=["c1", "c2", "c3", "c4", "c5"],
+                   help="c4 (default) is the headline recognizer benchmark; c1/c2/c3/c5 measure the other "
+                        "BASELINE configurations (CTC head, conv block, neck, page pipeline) on one GPU")
     return p.parse_args()
 
 
@@ -70,8 +76,14 @@ class ClockSampler:
                  "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # The sampler takes a moment to start: wait for its first line so
+            # the timed region is covered even when it is short.
+            t_end = time.monotonic() + 3.0
+            while not self.lines and time.monotonic() < t_end and self.proc.poll() is None:
+                time.sleep(0.01)
         except OSError:
             self.proc = None
+        self.n0 = len(self.lines)
         return self
 
     def _read(self):
@@ -80,6 +92,10 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.proc:
+            # at least one sample taken after the timed work was issued
+            t_end = time.monotonic() + 1.0
+            while len(self.lines) <= self.n0 and time.monotonic() < t_end and self.proc.poll() is None:
+                time.sleep(0.01)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -115,30 +131,66 @@ def peaks():
     return 1590.0, 6650.0, "fallback"
 
 
+class CpuRecognizer:
+    """The oracle's CPU restatement of one recognizer step on two lines:
+    graph forward (torch fp32 with the same fp16 storage points), vocabulary
+    projection with the head's weights, argmax / softmax-max, and the CTC
+    collapse (oracle C restatement)."""
+
+    def __init__(self):
+        import ctypes
+
+        import numpy as np
+        import torch
+
+        from ppocr_b200 import modelgen, models
+        from oracle import layers as L
+
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        self.g, self.out = models.graph("rec_b2")
+        self.x = np.random.default_rng(SEED).uniform(-1, 1, (2, 3, H, W)).astype(np.float32)
+        spec = models.spec("recognizer")
+        hidden, vocab = spec["neck"]["dim"], spec["vocab"]
+        init = modelgen.Init(models.SEED + 1)  # the device head's weights (pipeline.Classifier)
+        self.w = L.rh(torch.from_numpy(init.xavier((hidden, vocab), hidden, vocab)))
+        self.b = L.rh(torch.from_numpy(init.normal((vocab,), 0.0, 0.01)))
+        self.lib = ctypes.CDLL(str(REPO / "oracle" / "_build" / "liboracle.so"))
+        Pv = ctypes.c_void_p
+        self.lib.oracle_ctc_collapse.argtypes = [Pv, Pv, ctypes.c_long, ctypes.c_int, ctypes.c_int, Pv, Pv, Pv]
+        self.T = 40
+
+    def step(self):
+        import numpy as np
+        import torch
+
+        from oracle import models as om
+
+        hid, _ = om.run_graph(self.g, self.x, self.out)
+        logits = hid.reshape(-1, hid.shape[-1]) @ self.w + self.b
+        mx, ids = logits.max(dim=1)
+        prob = (1.0 / torch.exp(logits - mx[:, None]).sum(dim=1)).float().numpy()
+        ids = ids.to(torch.int32).numpy()
+        o_ids = np.empty((2, self.T), np.int32)
+        o_len = np.empty(2, np.int32)
+        o_sc = np.empty(2, np.float32)
+        self.lib.oracle_ctc_collapse(ids.ctypes.data, prob.ctypes.data, 2, self.T, 0, o_ids.ctypes.data,
+                                     o_len.ctypes.data, o_sc.ctypes.data)
+        return 2
+
+
 def cpu_port_forward(lines_needed: int, budget_s: float = 20.0):
-    """Times the oracle's CPU restatement of the recognizer (torch fp32 with
-    the same fp16 storage points) on a bounded sample of the batch; returns
-    (lines/s, lines timed, threads)."""
-    import numpy as np
-    import torch
-
-    from ppocr_b200 import models
-    from oracle import models as om
-
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    g, out = models.graph("rec_b2")
-    x = np.random.default_rng(SEED).uniform(-1, 1, (2, 3, H, W)).astype(np.float32)
+    """Times the oracle's CPU restatement of the recognizer step on a
+    bounded sample of the batch; returns (lines/s, lines timed, threads)."""
+    cpu = CpuRecognizer()
     t0 = time.perf_counter()
-    om.run_graph(g, x, out)
-    one = time.perf_counter() - t0  # 2 lines, includes first-touch costs
-    done, elapsed = 2, one
+    done = cpu.step()  # includes first-touch costs
+    elapsed = time.perf_counter() - t0
     while elapsed < budget_s and done < lines_needed:
         t0 = time.perf_counter()
-        om.run_graph(g, x, out)
+        done += cpu.step()
         elapsed += time.perf_counter() - t0
-        done += 2
-    return done / elapsed, done, threads
+    return done / elapsed, done, cpu.threads
 
 
 def reference_arm(args):
@@ -147,21 +199,13 @@ def reference_arm(args):
         return
     per_step = []
     lines_per_step = 4
-    threads = os.cpu_count() or 1
     total = args.warmup + args.steps
-    import numpy as np
-    import torch
-
-    from ppocr_b200 import models
-    from oracle import models as om
-
-    torch.set_num_threads(threads)
-    g, out = models.graph("rec_b2")
-    x = np.random.default_rng(SEED).uniform(-1, 1, (2, 3, H, W)).astype(np.float32)
+    cpu = CpuRecognizer()
+    threads = cpu.threads
     for i in range(total):
         t0 = time.perf_counter()
         for _ in range(lines_per_step // 2):
-            om.run_graph(g, x, out)
+            cpu.step()
         dt = time.perf_counter() - t0
         if i >= args.warmup:
             per_step.append(dt)
@@ -172,8 +216,9 @@ def reference_arm(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * t / len(per_step), 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded U(-1,1) line images, random-init weights)",
-        "config": {"workload": "config 4 recognizer forward (same graph and weights), CPU restatement "
-                               "(oracle/ port; the reference has no CPU layer path)",
+        "config": {"workload": "config 4 recognizer step (same graph and weights: forward, vocabulary "
+                               "projection, argmax/softmax-max, CTC collapse), CPU restatement (oracle/ port; "
+                               "the reference has no CPU layer path)",
                    "lines_per_step": lines_per_step},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"{lines_per_step} lines per step (a bounded sample of the 512-line batch)"},
@@ -209,14 +254,18 @@ def b200_arm(args):
         return t.item()
 
     lib = capi.load()
-    rec = pipeline.LineRecognizer(MODEL, dev)
+    model_name = args.model
+    rec = pipeline.LineRecognizer(model_name, dev)
+    LINES = rec.batch
     rng = np.random.default_rng(SEED + rank)
     x_host = torch.from_numpy(rng.uniform(-1, 1, (LINES, H, W, 3)).astype(np.float16)).pin_memory()
     x_dev = x_host.to(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
     stream = rec.stream
     op_names = rec.model.lib.op_names(rec.model.handle)
-    launches_per_step = len(op_names) + 1 + 2 + 1  # graph ops + input staging + head (2) + collapse
+    # graph ops after the leading NCHW->NHWC transpose (replaced by a staging
+    # copy, no kernel) + vocabulary projection (2 kernels) + collapse (1)
+    launches_per_step = len(op_names) - 1 + 2 + 1
 
     # ---- device-resident timing
     for _ in range(args.warmup):
@@ -273,13 +322,22 @@ def b200_arm(args):
     h2d = x_host.numel() * x_host.element_size()
     d2h = out_ids.numel() * 4 + out_len.numel() * 4 + out_sc.numel() * 4
 
+    # ---- replicas decode one common check batch to identical tokens
+    from ppocr_b200.replicas import all_equal_over_ranks, tokens_digest
+
+    x_chk = torch.from_numpy(np.random.default_rng(SEED).uniform(-1, 1, (LINES, H, W, 3))
+                             .astype(np.float16)).to(dev)
+    rec.enqueue(x_chk)
+    digest = tokens_digest(*rec.results(LINES))
+    identical = all_equal_over_ranks(digest)
+
     # ---- roofline of the dominant kernel (stage-4 3x3 implicit GEMM)
     prof = [rec.model.lib.profile(rec.model.handle) for _ in range(3)]
     per_op = [min(p[i] for p in prof) for i in range(len(op_names))]
     dom = max(range(len(per_op)), key=lambda i: per_op[i])
     # algorithmic flops of that op, from the graph's layer table
     from ppocr_b200 import models
-    g, _ = models.graph(MODEL)
+    g, _ = models.graph(model_name)
     flops = op_flops(g, dom)
     peak_tf, peak_hbm, peak_kind = peaks()
     achieved = flops / (per_op[dom] / 1e3) / 1e12 if flops else None
@@ -293,7 +351,7 @@ def b200_arm(args):
         cpu_value, cpu_lines, cores = cpu_port_forward(8)
         cpu = {"value": round(cpu_value, 3), "unit": UNIT, "cores": cores, "kind": "port",
                "sample": f"{cpu_lines} lines of the batch through the oracle's CPU restatement "
-                         f"(torch fp32, same graph and weights)"}
+                         f"(torch fp32, same graph and weights, vocabulary projection, argmax, collapse)"}
     gpu_launches = launches_per_step * args.steps
     if world > 1:
         dist.barrier()
@@ -303,10 +361,10 @@ def b200_arm(args):
             "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded U(-1,1) FP16 NHWC line images, seeded random-init weights)",
-            "config": {"workload": "BASELINE config 4: full recognizer forward, 512 lines/GPU of 48x320, "
+            "config": {"workload": f"BASELINE config 4: full recognizer forward, {LINES} lines/GPU of 48x320, "
                                    "HGNet-style backbone 48-128-512-1024-2048 + SVTR neck dim 120 x2 + CTC "
                                    "projection V=18385 with fused argmax + device collapse",
-                       "lines_per_gpu": LINES, "parallelism": f"replicas x{world} (no collective)",
+                       "model": model_name, "lines_per_gpu": LINES, "parallelism": f"replicas x{world} (no collective)",
                        "l2": "flushed between timed steps (256 MB write outside the timed events)"},
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
@@ -318,6 +376,7 @@ def b200_arm(args):
             "cpu_baseline": cpu,
             "gpu_launches": gpu_launches,
             "clocks": clocks.summary(),
+            "replica_tokens": {"sha256": digest[:16], "identical_across_ranks": identical},
         }
         print(json.dumps(line), flush=True)
     rec.close()
@@ -336,6 +395,10 @@ def op_flops(g, index: int) -> float | None:
         if layer["groups"] != 1:
             return 2.0 * out[0] * out[1] * out[2] * out[3] * w[1] * w[2]
         return 2.0 * out[0] * out[1] * out[2] * out[3] * w[1] * w[2] * w[3]
+    if layer["op"] == "deconv":  # kernel == stride: one tap per output pixel
+        out = g.tensors[layer["out"]].shape
+        w = g.tensors[layer["w"]].const.shape  # [Ci, KH, KW, Co]
+        return 2.0 * out[0] * out[1] * out[2] * out[3] * w[0]
     if layer["op"] == "gemm":
         out = g.tensors[layer["out"]].shape
         w = g.tensors[layer["w"]].const.shape
@@ -346,10 +409,426 @@ def op_flops(g, index: int) -> float | None:
     return None
 
 
+# --------------------------------------------------------------------------
+# The other BASELINE configurations (one GPU, rank 0). Same timing rules as
+# the headline: >= 3 warm-up steps, CUDA events on the launching stream, L2
+# flushed (256 MB write) outside the timed events, clocks sampled meanwhile.
+
+CONFIGS = {
+    "c1": ("CTC-decoded lines/sec (C1: [32,40,18385] FP16 logits, argmax + softmax-max + collapse)",
+           "lines/s", True),
+    "c2": ("conv-block images/sec (C2: dw5x5 + pw 64->128 hardswish, [16,48,320,64] FP16 NHWC)",
+           "images/s", True),
+    "c3": ("neck lines/sec (C3: SVTR neck, 2 blocks, [256,40,120] FP16)", "lines/s", True),
+    "c5": ("page p50 latency ms @960^2 (C5: 8 pages -> detector + binarize, 512 line crops -> recognizer)",
+           "ms", False),
+}
+
+
+def _event_steps(stream, steps, body, flush):
+    """Per-step device time (ms) of body(i) on `stream`, flush outside."""
+    import torch
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        with torch.cuda.stream(stream):
+            if flush is not None:
+                flush.zero_()
+            starts[i].record(stream)
+        body(i)
+        ends[i].record(stream)
+    stream.synchronize()
+    return [a.elapsed_time(b) for a, b in zip(starts, ends)]
+
+
+def op_bytes(g, index: int) -> float:
+    """Algorithmic HBM bytes of one graph layer: every distinct tensor it
+    reads (activations and constants) plus the one it writes, FP16."""
+    import math
+
+    layer = g.layers[index]
+    ids = set()
+    for k, v in layer.items():
+        if k in ("in", "w", "b", "scale", "bias", "add", "a") or (k == "res" and v >= 0):
+            if isinstance(v, int) and v >= 0:
+                ids.add(v)
+    ids.add(layer["out"])
+    total = 0
+    for i in ids:
+        t = g.tensors[i]
+        shape = t.const.shape if t.const is not None else t.shape
+        total += 2 * math.prod(shape)
+    return float(total)
+
+
+def _per_op(model, reps=3):
+    prof = [model.lib.profile(model.handle) for _ in range(reps)]
+    return [min(p[i] for p in prof) for i in range(len(prof[0]))]
+
+
+def _dominant(model, name, bound_hint=None):
+    """(index, name, ms, bytes, flops) of the slowest op of a compiled graph."""
+    from ppocr_b200 import models
+
+    per = _per_op(model)
+    names = model.lib.op_names(model.handle)
+    dom = max(range(len(per)), key=lambda i: per[i])
+    g, _ = models.graph(name)
+    return dom, names[dom], per[dom], op_bytes(g, dom), op_flops(g, dom), per, names
+
+
+def _roofline_for(kind, ms, bytes_, flops, key, peak_tf, peak_hbm, peak_kind):
+    if kind == "tensor" and not flops:
+        kind = "hbm"  # not a contraction: bounded by its bytes
+    traffic = None
+    tf = REPO / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(key)
+    if kind == "hbm":
+        achieved = bytes_ / (ms / 1e3) / 1e9
+        return {"bound": "hbm", "kernel": key, "achieved": round(achieved, 1), "peak": peak_hbm, "unit": "GB/s",
+                "frac": round(achieved / peak_hbm, 4), "peak_source": f"hbm_gbs of {peak_kind} peaks",
+                "traffic": traffic, "launch_ms": round(ms, 5), "bytes": bytes_}
+    achieved = flops / (ms / 1e3) / 1e12
+    return {"bound": "tensor", "kernel": key, "achieved": round(achieved, 1), "peak": peak_tf, "unit": "TFLOP/s",
+            "frac": round(achieved / peak_tf, 4), "peak_source": f"bf16_tflops of {peak_kind} peaks",
+            "traffic": traffic, "launch_ms": round(ms, 5), "flops": flops}
+
+
+def config_arm(args):
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    from ppocr_b200 import capi, models, pipeline, workloads
+
+    rank, world, local = dist_env()
+    if rank != 0:
+        return  # the secondary configurations run on one GPU
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lib = capi.load()
+    metric, unit, hib = CONFIGS[args.config]
+    peak_tf, peak_hbm, peak_kind = peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    r = workloads.rng(SEED)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    warm = max(args.warmup, 3)
+    args.steps = max(args.steps, 200)  # sub-millisecond steps: a longer timed region
+    extra = {}
+
+    if args.config == "c1":
+        lines, T, V = 32, workloads.SEQ, workloads.VOCAB
+        rows = lines * T
+        logits_h = torch.from_numpy(workloads.c1_logits(r, lines, T, V).reshape(rows, V)).pin_memory()
+        logits = logits_h.to(dev)
+        ids = torch.empty(rows, dtype=torch.int32, device=dev)
+        prob = torch.empty(rows, dtype=torch.float32, device=dev)
+        mx = torch.empty(rows, dtype=torch.float32, device=dev)
+        oid = torch.empty(lines, T, dtype=torch.int32, device=dev)
+        olen = torch.empty(lines, dtype=torch.int32, device=dev)
+        osc = torch.empty(lines, dtype=torch.float32, device=dev)
+        h_oid, h_olen, h_osc = (torch.empty_like(t, device="cpu").pin_memory() for t in (oid, olen, osc))
+        stream = torch.cuda.Stream(dev)
+        s = ctypes.c_void_p(stream.cuda_stream)
+        kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+
+        def head(i=None, src=logits):
+            if i is not None:
+                kev[i][0].record(stream)
+            capi.check(lib.ppocr_b200_logits_argmax_prob(P(src), rows, V, P(ids), P(prob), P(mx), 1, s))
+            if i is not None:
+                kev[i][1].record(stream)
+            capi.check(lib.ppocr_b200_ctc_collapse(P(ids), P(prob), lines, T, 0, P(oid), P(olen), P(osc), s))
+
+        for _ in range(warm):
+            head()
+        stream.synchronize()
+        with ClockSampler(local) as clocks:
+            step_ms = _event_steps(stream, args.steps, head, flush)
+        kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+        units = lines
+        # e2e: pinned logits in, decoded ids/lengths/scores out, every step
+        stage = torch.empty_like(logits)
+
+        def e2e_body(i):
+            with torch.cuda.stream(stream):
+                stage.copy_(logits_h, non_blocking=True)
+            head(src=stage)
+            with torch.cuda.stream(stream):
+                h_oid.copy_(oid, non_blocking=True)
+                h_olen.copy_(olen, non_blocking=True)
+                h_osc.copy_(osc, non_blocking=True)
+
+        e2e_ms = _event_steps(stream, args.steps, e2e_body, None)
+        h2d = logits_h.numel() * 2
+        d2h = h_oid.numel() * 4 + h_olen.numel() * 4 + h_osc.numel() * 4
+        roof = _roofline_for("hbm", kernel_ms, rows * V * 2.0 + rows * 12.0, None, "c1:logits_argmax",
+                             peak_tf, peak_hbm, peak_kind)
+        launches = 2
+        cpu = _cpu_c1(logits_h.numpy(), lines, T, V)
+        workload = "BASELINE config 1: CTC head on materialised FP16 logits [32,40,18385] (seeded N(0,1), +4 " \
+                   "boost, 30% blank, repeats), device argmax/softmax-max + greedy collapse"
+    elif args.config in ("c2", "c3"):
+        name = "block_b16" if args.config == "c2" else "neck_b256"
+        model = pipeline.CompiledModel(name, dev)
+        if args.config == "c2":
+            x_np = workloads.c2_input(r, 16)
+            units = 16
+        else:
+            x_np = workloads.c3_tokens(r, 256).reshape(256, 1, workloads.SEQ, 120)
+            units = 256
+        x_h = torch.from_numpy(x_np).pin_memory()
+        x = x_h.to(dev)
+        out = model.output_tensor()
+        out_h = torch.empty_like(out, device="cpu").pin_memory()
+        stream = torch.cuda.Stream(dev)
+        for _ in range(warm):
+            model.enqueue_nhwc(x, out, stream)
+        stream.synchronize()
+        with ClockSampler(local) as clocks:
+            step_ms = _event_steps(stream, args.steps, lambda i: model.enqueue_nhwc(x, out, stream), flush)
+        stage = torch.empty_like(x)
+
+        def e2e_body(i):
+            with torch.cuda.stream(stream):
+                stage.copy_(x_h, non_blocking=True)
+            model.enqueue_nhwc(stage, out, stream)
+            with torch.cuda.stream(stream):
+                out_h.copy_(out, non_blocking=True)
+
+        e2e_ms = _event_steps(stream, args.steps, e2e_body, None)
+        h2d = x_h.numel() * 2
+        d2h = out_h.numel() * 2
+        dom, dname, dms, dbytes, dflops, per, names = _dominant(model, name)
+        roof = _roofline_for("hbm", dms, dbytes, dflops, f"{args.config}:{dname}#{dom}", peak_tf, peak_hbm,
+                             peak_kind)
+        g, _ = models.graph(name)
+        extra["ops"] = [{"op": f"{names[i]}#{i}", "ms": round(per[i], 5),
+                         "gbs": round(op_bytes(g, i) / (per[i] / 1e3) / 1e9, 1) if per[i] > 0 else None}
+                        for i in range(len(per)) if per[i] > 0]
+        if args.config == "c2":
+            fused_min = (16 * 48 * 320 * 64 + 16 * 48 * 320 * 128) * 2.0
+            extra["block_vs_fused_minimum"] = {
+                "bytes": fused_min, "gbs": round(fused_min / (statistics.mean(step_ms) / 1e3) / 1e9, 1),
+                "frac": round(fused_min / (statistics.mean(step_ms) / 1e3) / 1e9 / peak_hbm, 4)}
+        # c2: the leading NCHW->NHWC op is replaced by a copy (no kernel);
+        # c3: every op runs, after one input-staging kernel.
+        launches = len(names) - 1 if args.config == "c2" else len(names) + 1
+        cpu = _cpu_graph(name, units)
+        model.close()
+        workload = ("BASELINE config 2: depthwise 5x5 s1 p2 (+folded BN, hardswish) -> pointwise 64->128 "
+                    "(+folded BN, hardswish) on FP16 NHWC [16,48,320,64] through the Model ABI v2 shell"
+                    if args.config == "c2" else
+                    "BASELINE config 3: SVTR neck (2 x [LN -> 8-head MHSA dh 15 -> residual -> LN -> MLP "
+                    "120-240-120 swish -> residual]) on FP16 [256,40,120] through the Model ABI v2 shell")
+    else:  # c5
+        pp = pipeline.PagePipeline(device=dev)
+        pages_np, crops_np = workloads.c5_pages(r)
+        pages_h = torch.from_numpy(pages_np).pin_memory()
+        crops_h = torch.from_numpy(crops_np).pin_memory()
+        pages, crops = pages_h.to(dev), crops_h.to(dev)
+        stream = pp.stream
+        for _ in range(warm):
+            pp.enqueue(pages, crops)
+        stream.synchronize()
+        assert lib.ppocr_b200_device_error() == 0
+        runs = max(args.steps, 100)
+        with ClockSampler(local) as clocks:
+            step_ms = _event_steps(stream, runs, lambda i: pp.enqueue(pages, crops), flush)
+        bm_h = torch.empty_like(pp.bitmap, device="cpu").pin_memory()
+        ids_h = torch.empty_like(pp.rec.out_ids, device="cpu").pin_memory()
+        len_h = torch.empty_like(pp.rec.out_len, device="cpu").pin_memory()
+        sc_h = torch.empty_like(pp.rec.out_score, device="cpu").pin_memory()
+        st_p, st_c = torch.empty_like(pages), torch.empty_like(crops)
+
+        def e2e_body(i):
+            with torch.cuda.stream(stream):
+                st_p.copy_(pages_h, non_blocking=True)
+                st_c.copy_(crops_h, non_blocking=True)
+            pp.enqueue(st_p, st_c)
+            with torch.cuda.stream(stream):
+                bm_h.copy_(pp.bitmap, non_blocking=True)
+                ids_h.copy_(pp.rec.out_ids, non_blocking=True)
+                len_h.copy_(pp.rec.out_len, non_blocking=True)
+                sc_h.copy_(pp.rec.out_score, non_blocking=True)
+
+        e2e_ms = _event_steps(stream, runs, e2e_body, None)
+        h2d = (pages_h.numel() + crops_h.numel()) * 2
+        d2h = bm_h.numel() + ids_h.numel() * 4 + len_h.numel() * 4 + sc_h.numel() * 4
+        dom, dname, dms, dbytes, dflops, per, names = _dominant(pp.det, "det_b8")
+        roof = _roofline_for("tensor", dms, dbytes, dflops, f"c5:det:{dname}#{dom}", peak_tf, peak_hbm, peak_kind)
+        gdet, _ = models.graph("det_b8")
+        top = sorted(range(len(per)), key=lambda i: -per[i])[:10]
+        extra["detector_top_ops"] = []
+        for i in top:
+            f = op_flops(gdet, i)
+            b = op_bytes(gdet, i)
+            extra["detector_top_ops"].append({
+                "op": f"{names[i]}#{i}", "ms": round(per[i], 5),
+                "tflops": round(f / (per[i] / 1e3) / 1e12, 1) if f and per[i] > 0 else None,
+                "gbs": round(b / (per[i] / 1e3) / 1e9, 1) if per[i] > 0 else None})
+        # binarize alone: 5 B/pixel (f32 read + u8 write)
+        n = pp.prob.numel()
+        s = ctypes.c_void_p(stream.cuda_stream)
+        bin_ms = _event_steps(stream, 20, lambda i: capi.check(lib.ppocr_b200_binarize(
+            P(pp.prob), P(pp.bitmap), n, pp.thresh, s)), flush)
+        extra["binarize"] = _roofline_for("hbm", statistics.mean(bin_ms), 5.0 * n, None, "c5:binarize",
+                                          peak_tf, peak_hbm, peak_kind)
+        det_ms = sum(_per_op(pp.det))
+        extra["detector_eager_ms"] = round(det_ms, 4)
+        extra["p90_ms"] = round(float(np.percentile(step_ms, 90)), 4)
+        extra["runs"] = runs
+        # detector ops after the staged transpose, binarize, recognizer ops
+        # after its staged transpose, vocabulary projection (2), collapse (1)
+        launches = (len(names) - 1) + 1 + (len(pp.rec.model.lib.op_names(pp.rec.model.handle)) - 1) + 3
+        cpu = _cpu_c5()
+        pp.close()
+        units = None
+        workload = ("BASELINE config 5: 8 FP16 NHWC pages 960x960 -> DB detector (backbone strides 2..32, FPN "
+                    "256, head 3x3 -> deconv x2 -> sigmoid) -> binarize 0.3, plus 64 synthetic 48x320 crops per "
+                    "page (512) -> recognizer + CTC head + collapse; one batch per run, p50 over runs")
+
+    if args.config == "c5":
+        value = float(np.percentile(step_ms, 50))
+        e2e_value = float(np.percentile(e2e_ms, 50))
+        ms_per_step = value
+    else:
+        value = units * len(step_ms) / (sum(step_ms) / 1e3)
+        e2e_value = units * len(e2e_ms) / (sum(e2e_ms) / 1e3)
+        ms_per_step = sum(step_ms) / len(step_ms)
+    line = {
+        "metric": metric, "value": round(value, 4 if args.config == "c5" else 1), "unit": unit, "n_gpus": 1,
+        "steps": len(step_ms), "warmup": warm, "ms_per_step": round(ms_per_step, 4), "higher_is_better": hib,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+        "data": "synthetic (seeded, BASELINE distributions; seeded random-init weights)",
+        "config": {"workload": workload, "l2": "flushed between timed steps (256 MB write outside the events)"},
+        "e2e": {"value": round(e2e_value, 4 if args.config == "c5" else 1), "unit": unit,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": roof, "cpu_baseline": cpu, "gpu_launches": launches * len(step_ms),
+        "clocks": clocks.summary(),
+    }
+    line.update(extra)
+    print(json.dumps(line), flush=True)
+
+
+def _cpu_c1(logits_f16: np.ndarray, lines: int, T: int, V: int):
+    """Oracle C argmax/softmax-max (OpenMP, all cores) + the reference's own
+    ctc_decode.cpp (oracle/_ref, when built) on all 32 lines."""
+    import ctypes
+
+    import numpy as np
+
+    rows = lines * T
+    lib = ctypes.CDLL(str(REPO / "oracle" / "_build" / "liboracle.so"))
+    Pv = ctypes.c_void_p
+    lib.oracle_argmax_prob.argtypes = [Pv, ctypes.c_long, ctypes.c_int, Pv, Pv, Pv, ctypes.c_int]
+    lib.oracle_ctc_collapse.argtypes = [Pv, Pv, ctypes.c_long, ctypes.c_int, ctypes.c_int, Pv, Pv, Pv]
+    ref_path = REPO / "oracle" / "_ref" / "libref_ctc.so"
+    ref = ctypes.CDLL(str(ref_path)) if ref_path.exists() else None
+    if ref is not None:
+        ref.ref_ctc_decode_batch.argtypes = [Pv, Pv, ctypes.c_int, ctypes.c_int, ctypes.c_int, Pv, Pv, Pv]
+    threads = os.cpu_count() or 1
+    lg = np.ascontiguousarray(logits_f16.view(np.uint16))
+    ids = np.empty(rows, np.int32)
+    prob = np.empty(rows, np.float32)
+    mx = np.empty(rows, np.float32)
+    o_ids = np.empty((lines, T), np.int32)
+    o_len = np.empty(lines, np.int32)
+    o_sc = np.empty(lines, np.float32)
+    times = []
+    t_end = time.perf_counter() + 10.0
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        lib.oracle_argmax_prob(lg.ctypes.data, rows, V, ids.ctypes.data, prob.ctypes.data, mx.ctypes.data, threads)
+        if ref is not None:
+            ref.ref_ctc_decode_batch(ids.ctypes.data, prob.ctypes.data, lines, T, 0, o_ids.ctypes.data,
+                                     o_len.ctypes.data, o_sc.ctypes.data)
+        else:
+            lib.oracle_ctc_collapse(ids.ctypes.data, prob.ctypes.data, lines, T, 0, o_ids.ctypes.data,
+                                    o_len.ctypes.data, o_sc.ctypes.data)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": round(lines / med, 1), "unit": "lines/s", "cores": threads,
+            "kind": "reference" if ref is not None else "port",
+            "sample": f"all {lines} lines per call, median of {len(times)} calls: argmax/softmax-max by the "
+                      f"oracle's C restatement (OpenMP), collapse by "
+                      + ("the reference's own ctc_decode.cpp compiled as-is" if ref is not None else
+                         "the oracle's C restatement")}
+
+
+def _cpu_graph(name: str, units: int):
+    """Oracle torch-CPU restatement of a compiled graph on a bounded sample."""
+    import numpy as np
+    import torch
+
+    from ppocr_b200 import modelgen, models
+    from oracle import models as om
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    family = models.SHAPES[name][0]
+    spec = models.spec(family)
+    sample = 2 if family == "block" else 64
+    g, out = (modelgen.build_block(spec, sample, models.SEED) if family == "block"
+              else modelgen.build_neck(spec, sample, models.SEED))
+    x = np.random.default_rng(SEED).standard_normal(g.tensors[0].shape).astype(np.float32)
+    om.run_graph(g, x, out)
+    times = []
+    t_end = time.perf_counter() + 10.0
+    while time.perf_counter() < t_end or len(times) < 2:
+        t0 = time.perf_counter()
+        om.run_graph(g, x, out)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    unit = "images/s" if family == "block" else "lines/s"
+    return {"value": round(sample / med, 2), "unit": unit, "cores": threads, "kind": "port",
+            "sample": f"{sample} of the {units} {unit.split('/')[0]} per call, median of {len(times)} calls "
+                      f"(oracle torch-CPU fp32 restatement of the same graph and weights; the reference has no "
+                      f"CPU layer path)"}
+
+
+def _cpu_c5():
+    """Page latency on the host cores, from a bounded sample: one 960^2 page
+    through the oracle's detector + binarize and 8 line crops through its
+    recognizer, scaled to the 8-page, 512-line batch of one run."""
+    import numpy as np
+    import torch
+
+    from ppocr_b200 import modelgen, models
+    from oracle import layers as L
+    from oracle import models as om
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rg = np.random.default_rng(SEED)
+    gd, od = modelgen.build_detector(models.spec("detector"), 1, 960, models.SEED)
+    gr, orr = modelgen.build_recognizer(models.spec("recognizer"), 8, models.SEED)
+    page = rg.uniform(-1, 1, (1, 3, 960, 960)).astype(np.float32)
+    lines8 = rg.uniform(-1, 1, (8, 3, H, W)).astype(np.float32)
+    t0 = time.perf_counter()
+    prob, _ = om.run_graph(gd, page, od)
+    L.binarize(prob.numpy().ravel(), 0.3)
+    t_page = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    om.run_graph(gr, lines8, orr)
+    t_line = (time.perf_counter() - t0) / 8
+    batch_ms = 8 * (t_page + 64 * t_line) * 1e3
+    return {"value": round(batch_ms, 1), "unit": "ms", "cores": threads, "kind": "port",
+            "sample": f"1 page (detector + binarize, {t_page * 1e3:.0f} ms) and 8 lines "
+                      f"({t_line * 1e3:.1f} ms/line) through the oracle's torch-CPU restatement, scaled to one "
+                      f"run's 8 pages + 512 lines (the reference has no CPU layer path)"}
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
+    elif args.config != "c4":
+        config_arm(args)
     else:
         b200_arm(args)
 

@@ -32,3 +32,20 @@ extern "C" int ref_linear_argmax_prob_wmma(
     return -1;
   }
 }
+
+extern "C" int ref_selected_class_vs_max(const void *hidden, const void *weight,
+                                         const void *bias,
+                                         const float *max_logits,
+                                         float *out_probability, int rows,
+                                         int hidden_size, int vocab,
+                                         int class_id, void *stream) {
+  try {
+    ppocrv6_native::kernels::cuda_selected_class_vs_max_probability(
+        static_cast<const half *>(hidden), static_cast<const half *>(weight),
+        static_cast<const half *>(bias), max_logits, out_probability, rows,
+        hidden_size, vocab, class_id, static_cast<cudaStream_t>(stream));
+    return 0;
+  } catch (...) {
+    return -1;
+  }
+}

@@ -376,6 +376,29 @@ def build_recognizer(spec: dict, batch: int, seed: int):
     return g, x
 
 
+def build_block(spec: dict, batch: int, seed: int):
+    """Depthwise-separable NHWC block: dw KxK (+BN, act) -> 1x1 (+BN, act)."""
+    g = Graph((batch, spec["channels"], spec["height"], spec["width"]))
+    bd = Builder(g, Init(seed))
+    x = bd.to_nhwc(0)
+    c = spec["channels"]
+    x = bd.conv_bn_act(x, c, spec["kernel"], act=spec["act"], depthwise=True)
+    x = bd.pointwise(x, spec["out"], act=spec["act"])
+    return g, x
+
+
+def build_neck(spec: dict, batch: int, seed: int):
+    """SVTR neck alone on [B, seq, dim] FP16 tokens (input viewed as
+    [B, 1, seq, dim], where NCHW and NHWC coincide)."""
+    seq, dim = spec["seq"], spec["dim"]
+    g = Graph((batch, 1, seq, dim))
+    bd = Builder(g, Init(seed))
+    x = g.view(0, "tokens", (batch, seq, dim))
+    for _ in range(spec["blocks"]):
+        x = svtr_block(bd, x, spec["heads"], dim // spec["heads"], spec.get("mlp_ratio", 2))
+    return g, x
+
+
 def build_detector(spec: dict, batch: int, size: int, seed: int):
     """Backbone at strides 2..32 + FPN(256) + DB head -> sigmoid map [B,1,S,S]."""
     g = Graph((batch, 3, size, size))

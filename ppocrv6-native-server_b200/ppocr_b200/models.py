@@ -26,6 +26,10 @@ SHAPES = {
     "rec_b2": ("recognizer", 2, None),
     "det_b8": ("detector", 8, 960),
     "det_b1_s128": ("detector", 1, 128),
+    "block_b16": ("block", 16, None),
+    "block_b2": ("block", 2, None),
+    "neck_b256": ("neck", 256, None),
+    "neck_b4": ("neck", 4, None),
 }
 
 
@@ -38,6 +42,10 @@ def graph(name: str):
     s = spec(family)
     if family == "recognizer":
         return modelgen.build_recognizer(s, batch, SEED)
+    if family == "block":
+        return modelgen.build_block(s, batch, SEED)
+    if family == "neck":
+        return modelgen.build_neck(s, batch, SEED)
     return modelgen.build_detector(s, batch, size, SEED)
 
 

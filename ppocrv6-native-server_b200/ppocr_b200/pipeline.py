@@ -129,3 +129,37 @@ class LineRecognizer:
 
     def close(self) -> None:
         self.model.close()
+
+
+class PagePipeline:
+    """Full-page path on one GPU: detector graph -> DB binarize -> recognizer
+    over the page's line crops -> fused head -> device collapse, all on one
+    stream (reference: full_page_worker.cpp:361-497 runs detection, then
+    recognition of the warped crops; the crops here are given, the ROI warp
+    being outside this path)."""
+
+    def __init__(self, detector: str = "det_b8", recognizer: str = "rec_b512",
+                 device: torch.device | str = "cuda:0", thresh: float | None = None):
+        self.device = torch.device(device)
+        self.rec = LineRecognizer(recognizer, self.device)
+        self.det = CompiledModel(detector, self.device)
+        self.stream = self.rec.stream
+        self.thresh = models.spec("detector")["thresh"] if thresh is None else thresh
+        self.pages = self.det.input_shape[0]
+        self.size = self.det.input_shape[2]
+        with torch.cuda.device(self.device):
+            self.prob = self.det.output_tensor()
+            self.bitmap = torch.empty(self.prob.shape, dtype=torch.uint8, device=self.device)
+        self.lib = capi.load()
+
+    def enqueue(self, pages_nhwc: torch.Tensor, crops_nhwc: torch.Tensor) -> None:
+        """pages FP16 NHWC [<=pages, S, S, 3], crops FP16 NHWC [<=lines, 48, 320, 3]."""
+        self.det.enqueue_nhwc(pages_nhwc, self.prob, self.stream)
+        n = pages_nhwc.shape[0] * self.size * self.size
+        capi.check(self.lib.ppocr_b200_binarize(_p(self.prob), _p(self.bitmap), n, self.thresh,
+                                                ctypes.c_void_p(self.stream.cuda_stream)))
+        self.rec.enqueue(crops_nhwc)
+
+    def close(self) -> None:
+        self.det.close()
+        self.rec.close()

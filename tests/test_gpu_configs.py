@@ -1,0 +1,128 @@
+"""Parity at the BASELINE configurations' own sizes, through the Model ABI v2
+shell and the head C-ABI, against the CPU oracle (oracle/models.py running
+the same generated graph on the same FP16 weights).
+
+C1 (CTC head on [32, 40, 18385] logits) is covered at full size in
+test_gpu_ops.py::test_logits_argmax_and_collapse. Here: C2 (the
+depthwise-separable block, full [16, 48, 320, 64] input), C3 (the SVTR neck,
+full [256, 40, 120] tokens), C4 (the recognizer compiled for B=512, checked
+on lines at both ends of the batch), C5 (the page pipeline at 8 x 960^2:
+detector map of one page against the oracle, binarize bit-exact over every
+page, batch-position independence, replay determinism).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_close, rel_l2, rng
+from oracle import layers as L
+from oracle import models as OM
+
+pytestmark = pytest.mark.gpu
+
+
+def _enqueue_nhwc(model, x_nhwc: torch.Tensor) -> torch.Tensor:
+    stream = torch.cuda.Stream()
+    out = model.output_tensor()
+    model.enqueue_nhwc(x_nhwc, out, stream)
+    stream.synchronize()
+    return out
+
+
+def test_c2_block_full_size(native, cuda):
+    from ppocr_b200 import models, pipeline, workloads
+
+    m = pipeline.CompiledModel("block_b16", cuda)
+    try:
+        x = workloads.c2_input(rng(40), 16)
+        got = _enqueue_nhwc(m, torch.from_numpy(x).cuda()).float().cpu()
+        assert native.ppocr_b200_device_error() == 0
+        g, out_id = models.graph("block_b16")
+        want, _ = OM.run_graph(g, x.astype(np.float32).transpose(0, 3, 1, 2), out_id)
+        assert_close(got, want, what="C2 dw5x5+pw block")
+    finally:
+        m.close()
+
+
+def test_c3_neck_full_size(native, cuda):
+    from ppocr_b200 import models, pipeline, workloads
+
+    m = pipeline.CompiledModel("neck_b256", cuda)
+    try:
+        tok = workloads.c3_tokens(rng(41), 256)
+        got = _enqueue_nhwc(m, torch.from_numpy(tok).cuda().reshape(256, 1, 40, 120)).float().cpu()
+        assert native.ppocr_b200_device_error() == 0
+        g, out_id = models.graph("neck_b256")
+        want, _ = OM.run_graph(g, tok.astype(np.float32).reshape(256, 1, 40, 120), out_id)
+        assert_close(got, want, what="C3 SVTR neck")
+    finally:
+        m.close()
+
+
+def test_c3_neck_partial_batch_rows_match(cuda):
+    """A partial batch gives the same rows as the full batch (zero tail)."""
+    from ppocr_b200 import pipeline, workloads
+
+    m = pipeline.CompiledModel("neck_b256", cuda)
+    try:
+        tok = torch.from_numpy(workloads.c3_tokens(rng(42), 256)).cuda().reshape(256, 1, 40, 120)
+        full = _enqueue_nhwc(m, tok).clone()
+        part = _enqueue_nhwc(m, tok[:37].contiguous())
+        assert torch.equal(part[:37], full[:37])
+    finally:
+        m.close()
+
+
+def test_c4_recognizer_b512_ends_of_batch(native, cuda):
+    """The B=512 bench shape: lines at both ends of the batch against the
+    oracle (graph built for 4 lines, same seeded weights)."""
+    from ppocr_b200 import models, modelgen, pipeline, workloads
+
+    m = pipeline.CompiledModel("rec_b512", cuda)
+    try:
+        x = workloads.c4_lines(rng(43), 512)
+        got = _enqueue_nhwc(m, torch.from_numpy(x).cuda()).float().cpu()
+        assert native.ppocr_b200_device_error() == 0
+        pick = [0, 1, 510, 511]
+        g, out_id = modelgen.build_recognizer(models.spec("recognizer"), 4, models.SEED)
+        want, _ = OM.run_graph(g, x[pick].astype(np.float32).transpose(0, 3, 1, 2), out_id)
+        r = rel_l2(got[pick], want)
+        assert r < 1e-2, f"rel_l2 {r}"
+    finally:
+        m.close()
+
+
+def test_c5_page_pipeline_full_size(native, cuda):
+    from ppocr_b200 import models, modelgen, pipeline, workloads
+
+    pp = pipeline.PagePipeline(device=cuda)
+    try:
+        pages, crops = workloads.c5_pages(rng(44))
+        dp, dc = torch.from_numpy(pages).cuda(), torch.from_numpy(crops).cuda()
+        pp.enqueue(dp, dc)
+        pp.stream.synchronize()
+        assert native.ppocr_b200_device_error() == 0
+        prob = pp.prob.cpu().clone()
+        bitmap = pp.bitmap.cpu().clone()
+        ids, lens, scores = pp.rec.results(512)
+        assert prob.shape == (8, 1, 960, 960) and prob.dtype == torch.float32
+        assert torch.isfinite(prob).all() and prob.min() >= 0 and prob.max() <= 1
+        # DB binarize over all eight maps, bit-exact (cv::compare CMP_GT).
+        assert np.array_equal(bitmap.numpy().ravel(), L.binarize(prob.numpy().ravel(), pp.thresh))
+        # Page 3's map against the oracle (detector graph built for one page,
+        # same seeded weights).
+        g, out_id = modelgen.build_detector(models.spec("detector"), 1, 960, models.SEED)
+        want, _ = OM.run_graph(g, pages[3:4].astype(np.float32).transpose(0, 3, 1, 2), out_id)
+        assert (prob[3:4] - want).abs().max().item() < 2e-2
+        away = (want - pp.thresh).abs() > 2e-3
+        assert torch.equal(bitmap[3:4][away], torch.from_numpy(L.binarize(want.numpy(), pp.thresh))[away])
+        # Page order reversed: every map moves with its page, bit for bit;
+        # the recognizer output replays identically.
+        pp.enqueue(dp.flip(0).contiguous(), dc)
+        pp.stream.synchronize()
+        assert torch.equal(pp.prob.cpu(), prob.flip(0))
+        ids2, lens2, scores2 = pp.rec.results(512)
+        assert np.array_equal(ids, ids2) and np.array_equal(lens, lens2) and np.array_equal(scores, scores2)
+    finally:
+        pp.close()

@@ -233,24 +233,13 @@ def test_binarize_bit_exact(native, cuda):
 
 
 # ------------------------------------------------------------ CTC head
-def synthetic_logits(r, lines, T, V):
-    """N(0,1) logits, one seeded class per timestep +4,
-    30% of timesteps blank, repeats inserted."""
-    logits = r.standard_normal((lines, T, V)).astype(np.float32)
-    cls = r.integers(1, V, (lines, T))
-    blank = r.random((lines, T)) < 0.3
-    rep = r.random((lines, T)) < 0.2
-    for t in range(1, T):
-        cls[:, t] = np.where(rep[:, t], cls[:, t - 1], cls[:, t])
-    cls = np.where(blank, 0, cls)
-    np.put_along_axis(logits, cls[..., None], np.take_along_axis(logits, cls[..., None], -1) + 4.0, -1)
-    return logits.astype(np.float16)
-
-
 def test_logits_argmax_and_collapse(native, cuda, oracle_c):
+    """BASELINE config 1 at its full size: [32, 40, 18385] FP16 logits."""
+    from ppocr_b200 import workloads
+
     r = rng(18)
     lines, T, V = 32, 40, 18385
-    logits = synthetic_logits(r, lines, T, V)
+    logits = workloads.c1_logits(r, lines, T, V)
     rows = lines * T
     d = torch.from_numpy(logits.reshape(rows, V)).cuda()
     ids = torch.empty(rows, dtype=torch.int32, device=cuda)
