@@ -377,6 +377,8 @@ def b200_arm(args):
             "gpu_launches": gpu_launches,
             "clocks": clocks.summary(),
             "replica_tokens": {"sha256": digest[:16], "identical_across_ranks": identical},
+            "ops_ms": {f"{op_names[i]}#{i}": round(per_op[i], 4)
+                       for i in sorted(range(len(per_op)), key=lambda i: -per_op[i])[:16]},
         }
         print(json.dumps(line), flush=True)
     rec.close()

@@ -348,6 +348,26 @@ int ppocr_b200_deconv_nhwc(const void *x, const void *w, const void *bias,
   g_error.clear();
   if (!x || !w || !y || batch < 0 || ci <= 0 || co <= 0 || kh <= 0 || kw <= 0)
     return fail("invalid deconv arguments");
+  if (co % 64 == 0 && ci % 8 == 0) {
+    // Tensor-core path: pack the filter (and repeat the bias) into
+    // stream-ordered temporaries, released on the same stream.
+    const size_t wn = static_cast<size_t>(ci) * kh * kw * co;
+    void *wp = nullptr, *bp = nullptr;
+    cudaError_t e = cudaMallocAsync(&wp, wn * 2, stream);
+    if (e == cudaSuccess && bias)
+      e = cudaMallocAsync(&bp, static_cast<size_t>(kh) * kw * co * 2, stream);
+    if (e == cudaSuccess)
+      e = deconv_pack(H(w), H(bias), static_cast<half *>(wp), static_cast<half *>(bp), ci, co,
+                      kh, kw, stream);
+    if (e == cudaSuccess)
+      e = tc_deconv(H(x), static_cast<half *>(wp), static_cast<half *>(bp), Hm(y), batch, h,
+                    w_, ci, co, kh, kw, act, stream);
+    if (wp)
+      cudaFreeAsync(wp, stream);
+    if (bp)
+      cudaFreeAsync(bp, stream);
+    return status(e, "deconv");
+  }
   return status(deconv_kxk(H(x), H(w), H(bias), Hm(y), batch, h, w_, ci, co,
                            kh, kw, act, stream),
                 "deconv");

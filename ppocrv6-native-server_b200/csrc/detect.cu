@@ -74,6 +74,74 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Few outputs per input pixel (KH*KW*Co <= NMAX, e.g. the DB head's last
+// 64 -> 1 upsampling): thread = one input pixel computing all its taps'
+// outputs, the input read once with 16-byte loads, the filter [Ci][taps*Co]
+// in shared memory as fp32. Sums run over ci in order with fp32 FMAs.
+template <int NMAX>
+__global__ void __launch_bounds__(256)
+    deconv_small_kernel(const half *__restrict__ x, const half *__restrict__ w,
+                        const half *__restrict__ bias, half *__restrict__ y,
+                        uint32_t pixels, FastDiv by_w, FastDiv by_h, int Ci,
+                        int Co, int KH, int KW, int act) {
+  extern __shared__ float dsm[];
+  const int nout = KH * KW * Co;
+  for (int j = threadIdx.x; j < Ci * nout; j += blockDim.x)
+    dsm[j] = __half2float(w[j]); // w is [Ci][KH][KW][Co] = [Ci][nout]
+  __syncthreads();
+  const uint32_t p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= pixels)
+    return;
+  const uint32_t r = by_w.div(p);
+  const int iw = static_cast<int>(p - r * by_w.d);
+  const uint32_t n = by_h.div(r);
+  const int ih = static_cast<int>(r - n * by_h.d);
+  const int W = static_cast<int>(by_w.d), H = static_cast<int>(by_h.d);
+  float acc[NMAX];
+#pragma unroll
+  for (int o = 0; o < NMAX; ++o)
+    acc[o] = 0.f;
+  const half *px = x + static_cast<long long>(p) * Ci;
+  if ((Ci & 7) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    for (int c8 = 0; c8 < Ci; c8 += 8) {
+      uint4 v = __ldg(reinterpret_cast<const uint4 *>(px + c8));
+      const half2 *h2 = reinterpret_cast<const half2 *>(&v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float2 f = __half22float2(h2[j >> 1]);
+        const float xv = (j & 1) ? f.y : f.x;
+        const float *wr = dsm + (c8 + j) * nout;
+#pragma unroll
+        for (int o = 0; o < NMAX; ++o)
+          if (o < nout)
+            acc[o] = fmaf(xv, wr[o], acc[o]);
+      }
+    }
+  } else {
+    for (int ci = 0; ci < Ci; ++ci) {
+      const float xv = __half2float(px[ci]);
+#pragma unroll
+      for (int o = 0; o < NMAX; ++o)
+        if (o < nout)
+          acc[o] = fmaf(xv, dsm[ci * nout + o], acc[o]);
+    }
+  }
+  const long long OW = static_cast<long long>(W) * KW;
+  const long long OH = static_cast<long long>(H) * KH;
+#pragma unroll
+  for (int o = 0; o < NMAX; ++o) {
+    if (o >= nout)
+      break;
+    const int co = o % Co, tap = o / Co;
+    const int a = tap / KW, b = tap - a * KW;
+    float v = round_half(acc[o]);
+    if (bias)
+      v += __half2float(bias[co]);
+    y[((static_cast<long long>(n) * OH + ih * KH + a) * OW + iw * KW + b) * Co + co] =
+        __float2half_rn(apply_act(v, act));
+  }
+}
+
 __global__ void __launch_bounds__(256)
     binarize_kernel(const float *__restrict__ prob, uint8_t *__restrict__ map,
                     size_t n, float thresh) {
@@ -107,11 +175,42 @@ cudaError_t binarize(const float *prob, uint8_t *map, size_t n, float thresh,
   return cudaGetLastError();
 }
 
+cudaError_t deconv_pack(const half *w, const half *bias, half *wpacked,
+                        half *bias_rep, int Ci, int Co, int KH, int KW,
+                        cudaStream_t s) {
+  const int N = KH * KW * Co;
+  cudaError_t e = transpose2d(w, wpacked, 1, Ci, N, s);
+  if (e != cudaSuccess || !bias || !bias_rep)
+    return e;
+  for (int t = 0; t < KH * KW; ++t) {
+    e = cudaMemcpyAsync(bias_rep + static_cast<size_t>(t) * Co, bias,
+                        sizeof(half) * Co, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess)
+      return e;
+  }
+  return cudaSuccess;
+}
+
 cudaError_t deconv_kxk(const half *x, const half *w, const half *bias, half *y,
                        int batch, int H, int W, int Ci, int Co, int KH, int KW,
                        int act, cudaStream_t s) {
   if (batch <= 0)
     return cudaSuccess;
+  const long long pixels = static_cast<long long>(batch) * H * W;
+  const int nout = KH * KW * Co;
+  const size_t smem = sizeof(float) * static_cast<size_t>(Ci) * nout;
+  if (nout <= 16 && pixels < (1LL << 31) && smem <= 48 * 1024) {
+    const unsigned blocks = static_cast<unsigned>((pixels + 255) / 256);
+    if (nout <= 4)
+      deconv_small_kernel<4><<<blocks, 256, smem, s>>>(
+          x, w, bias, y, static_cast<uint32_t>(pixels), FastDiv(W), FastDiv(H),
+          Ci, Co, KH, KW, act);
+    else
+      deconv_small_kernel<16><<<blocks, 256, smem, s>>>(
+          x, w, bias, y, static_cast<uint32_t>(pixels), FastDiv(W), FastDiv(H),
+          Ci, Co, KH, KW, act);
+    return cudaGetLastError();
+  }
   const bool vec = Co % 8 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(y) & 15) == 0;
   const long long total = static_cast<long long>(batch) * H * KH * W * KW *

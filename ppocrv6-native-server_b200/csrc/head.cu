@@ -14,66 +14,215 @@
 #include "ptx.cuh"
 #include <cfloat>
 #include <climits>
+#include <mutex>
 
 namespace pb2 {
 namespace {
 
-struct Best {
-  float m;
-  int id;
-  float s;
-};
+// Row argmax / softmax-max over fp16 logits, one 128-thread block per row,
+// two passes: (1) the row max with packed fp16 max instructions (exact:
+// fp16 -> fp32 is exact, so the fp16 max is the fp32 max); (2) sum
+// exp(l - max) as ex2(l*log2e - max*log2e) on the special-function unit,
+// and the lowest column holding the max (the argmax, ties -> lowest id),
+// found by checking each 8-value vector's packed max against it.
+//
+// The row is staged in shared memory by bulk copies (cp.async.bulk, 8 KB
+// each, one mbarrier): the 16-byte-aligned span of the row (rows of an odd
+// vocabulary start at any 2-byte offset), so a block has the whole 36 KB row
+// in flight with one instruction per 8 KB. The up to 7 logits before the
+// first aligned vector inside the span and after its end are handled one
+// by one (the latter read from global memory).
+constexpr int kArgmaxThreads = 128;
+constexpr uint32_t kBulkChunk = 8192;
 
-__device__ __forceinline__ Best merge(Best a, Best b) {
-  // (max, lowest id) plus rescaled exp-sums.
-  Best r;
-  const bool take_b = b.m > a.m || (b.m == a.m && b.id < a.id);
-  r.m = take_b ? b.m : a.m;
-  r.id = take_b ? b.id : a.id;
-  const float sa = a.s == 0.f ? 0.f : a.s * __expf(a.m - r.m);
-  const float sb = b.s == 0.f ? 0.f : b.s * __expf(b.m - r.m);
-  r.s = sa + sb;
-  return r;
+__device__ __forceinline__ half2 vec_max(const uint4 &u) {
+  const half2 a = __hmax2(*reinterpret_cast<const half2 *>(&u.x),
+                          *reinterpret_cast<const half2 *>(&u.y));
+  const half2 b = __hmax2(*reinterpret_cast<const half2 *>(&u.z),
+                          *reinterpret_cast<const half2 *>(&u.w));
+  return __hmax2(a, b);
 }
 
-// One 256-thread block per row of fp16 logits.
-__global__ void __launch_bounds__(256)
+// The two passes over one row: elements [0, head) at hs[k], whole vectors
+// vp[0..nvec) covering elements [head, head + 8*nvec), elements
+// [head + 8*nvec, V) at gt[k] (global row pointer).
+__device__ __forceinline__ void argmax_row(const half *hs, int head,
+                                           const uint4 *vp, int nvec,
+                                           const half *gt, int V,
+                                           long long row, int *ids,
+                                           float *prob, float *max_logit,
+                                           int calc_prob) {
+  __shared__ float red_f[kArgmaxThreads / 32];
+  __shared__ int red_i[kArgmaxThreads / 32];
+  __shared__ float row_max;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int t_idx = head + (nvec << 3) + tid; // this thread's tail element
+
+  // ---- pass 1: max
+  const half neg = __ushort_as_half(0xFC00); // -inf
+  half2 m2 = __halves2half2(neg, neg);
+  if (tid < head)
+    m2 = __hmax2(m2, __halves2half2(hs[tid], neg));
+  int v = tid;
+  for (; v + 3 * kArgmaxThreads < nvec; v += 4 * kArgmaxThreads) {
+    const uint4 u0 = vp[v], u1 = vp[v + kArgmaxThreads];
+    const uint4 u2 = vp[v + 2 * kArgmaxThreads], u3 = vp[v + 3 * kArgmaxThreads];
+    m2 = __hmax2(m2, __hmax2(__hmax2(vec_max(u0), vec_max(u1)), __hmax2(vec_max(u2), vec_max(u3))));
+  }
+  for (; v < nvec; v += kArgmaxThreads)
+    m2 = __hmax2(m2, vec_max(vp[v]));
+  if (t_idx < V)
+    m2 = __hmax2(m2, __halves2half2(gt[t_idx], neg));
+  float m = fmaxf(__low2float(m2), __high2float(m2));
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0)
+    red_f[warp] = m;
+  __syncthreads();
+  if (tid == 0) {
+    float r = red_f[0];
+    for (int w = 1; w < kArgmaxThreads / 32; ++w)
+      r = fmaxf(r, red_f[w]);
+    row_max = r;
+  }
+  __syncthreads();
+  const float M = row_max;
+  const half Mh = __float2half_rn(M); // exact: M is an fp16 value
+  const float mL = M * kLog2e;
+
+  // ---- pass 2: sum of exponentials and the first column holding the max
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+  int best = INT_MAX;
+  auto one = [&](float l, int idx) {
+    s[0] += ex2_ftz(fmaf(l, kLog2e, -mL));
+    if (l == M && idx < best)
+      best = idx;
+  };
+  if (tid < head)
+    one(__half2float(hs[tid]), tid);
+  auto vec = [&](const uint4 &u, int vi) {
+    if (calc_prob) {
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(*reinterpret_cast<const half2 *>(&w[j]));
+        s[j] += ex2_ftz(fmaf(f.x, kLog2e, -mL)) + ex2_ftz(fmaf(f.y, kLog2e, -mL));
+      }
+    }
+    const half2 vm = vec_max(u);
+    if (__heq(__high2half(vm), Mh) || __heq(__low2half(vm), Mh)) {
+      const half *hv = reinterpret_cast<const half *>(&u);
+      for (int j = 0; j < 8; ++j)
+        if (__heq(hv[j], Mh)) {
+          best = min(best, head + (vi << 3) + j);
+          break;
+        }
+    }
+  };
+  v = tid;
+  for (; v + 3 * kArgmaxThreads < nvec; v += 4 * kArgmaxThreads) {
+    const uint4 u0 = vp[v], u1 = vp[v + kArgmaxThreads];
+    const uint4 u2 = vp[v + 2 * kArgmaxThreads], u3 = vp[v + 3 * kArgmaxThreads];
+    vec(u0, v);
+    vec(u1, v + kArgmaxThreads);
+    vec(u2, v + 2 * kArgmaxThreads);
+    vec(u3, v + 3 * kArgmaxThreads);
+  }
+  for (; v < nvec; v += kArgmaxThreads)
+    vec(vp[v], v);
+  if (t_idx < V)
+    one(__half2float(gt[t_idx]), t_idx);
+  float sum = (s[0] + s[1]) + (s[2] + s[3]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
+  }
+  __syncthreads();
+  if (lane == 0) {
+    red_f[warp] = sum;
+    red_i[warp] = best;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float t = 0.f;
+    int b = INT_MAX;
+    for (int w = 0; w < kArgmaxThreads / 32; ++w) {
+      t += red_f[w];
+      b = min(b, red_i[w]);
+    }
+    ids[row] = b;
+    max_logit[row] = M;
+    prob[row] = calc_prob ? 1.f / t : 1.f;
+  }
+}
+
+// Rows staged in shared memory (logits base 16-byte aligned).
+__global__ void __launch_bounds__(kArgmaxThreads)
+    logits_argmax_bulk_kernel(const half *__restrict__ logits, int V,
+                              int *__restrict__ ids, float *__restrict__ prob,
+                              float *__restrict__ max_logit, int calc_prob,
+                              int *err) {
+  extern __shared__ uint4 row_smem[];
+  __shared__ uint64_t bar;
+  __shared__ int failed;
+  const long long row = blockIdx.x;
+  const uint64_t start_b = static_cast<uint64_t>(row) * V * 2; // bytes
+  const uint64_t a0 = start_b & ~uint64_t(15);
+  const uint64_t a1 = (start_b + 2ull * V) & ~uint64_t(15);
+  const uint32_t nbytes = a1 > a0 ? static_cast<uint32_t>(a1 - a0) : 0;
+  const char *base = reinterpret_cast<const char *>(logits);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    failed = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && nbytes) {
+    mbar_arrive_expect_tx(&bar, nbytes);
+    for (uint32_t off = 0; off < nbytes; off += kBulkChunk)
+      bulk_load(reinterpret_cast<char *>(row_smem) + off, base + a0 + off,
+                min(kBulkChunk, nbytes - off), &bar);
+  }
+  volatile int no_abort = 0;
+  const bool ok = nbytes == 0 || mbar_wait(&bar, 0, &no_abort);
+  if (!ok)
+    failed = 1;
+  __syncthreads();
+  if (failed) {
+    // Bounded wait ran out: report, give the copies one more budget to land
+    // before this block's shared memory goes away, and leave the row.
+    if (!ok)
+      mbar_wait(&bar, 0, &no_abort);
+    if (threadIdx.x == 0 && err)
+      atomicCAS(err, 0, 6);
+    return;
+  }
+  // Row element k is at shared half (k + off); the vector holding element 0
+  // also holds the previous row's tail when off > 0.
+  const int off = static_cast<int>((start_b - a0) >> 1);
+  const half *rs = reinterpret_cast<const half *>(row_smem) + off;
+  const int in_smem = static_cast<int>((a1 > start_b ? a1 - start_b : 0) >> 1);
+  const int head = min(in_smem, off ? 8 - off : 0);
+  const int nvec = (in_smem - head) >> 3;
+  argmax_row(rs, head, row_smem + (off ? 1 : 0), nvec,
+             logits + row * V, V, row, ids, prob, max_logit, calc_prob);
+}
+
+// Register form (unaligned logits base): 16-byte loads straight from
+// global memory from the row's first 16-byte boundary.
+__global__ void __launch_bounds__(kArgmaxThreads)
     logits_argmax_kernel(const half *__restrict__ logits, int V,
                          int *__restrict__ ids, float *__restrict__ prob,
                          float *__restrict__ max_logit, int calc_prob) {
-  __shared__ Best red[8];
   const long long row = blockIdx.x;
   const half *lr = logits + row * V;
-  Best b{-FLT_MAX, INT_MAX, 0.f};
-  for (int j = threadIdx.x; j < V; j += 256) {
-    const float l = __half2float(lr[j]);
-    if (l > b.m) {
-      b.s = (b.s == 0.f ? 0.f : b.s * __expf(b.m - l)) + 1.f;
-      b.m = l;
-      b.id = j;
-    } else {
-      b.s += __expf(l - b.m);
-    }
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) {
-    Best other;
-    other.m = __shfl_xor_sync(0xffffffffu, b.m, o);
-    other.id = __shfl_xor_sync(0xffffffffu, b.id, o);
-    other.s = __shfl_xor_sync(0xffffffffu, b.s, o);
-    b = merge(b, other);
-  }
-  if ((threadIdx.x & 31) == 0)
-    red[threadIdx.x >> 5] = b;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    Best t = red[0];
-    for (int w = 1; w < 8; ++w)
-      t = merge(t, red[w]);
-    ids[row] = t.id;
-    max_logit[row] = t.m;
-    prob[row] = calc_prob ? 1.f / t.s : 1.f;
-  }
+  const int head =
+      min(V, static_cast<int>(((16 - (reinterpret_cast<uintptr_t>(lr) & 15)) & 15) >> 1));
+  const int nvec = (V - head) >> 3;
+  argmax_row(lr, head, reinterpret_cast<const uint4 *>(lr + head), nvec, lr, V,
+             row, ids, prob, max_logit, calc_prob);
 }
 
 __global__ void __launch_bounds__(256)
@@ -170,8 +319,25 @@ cudaError_t logits_argmax_prob(const half *logits, int rows, int V, int *ids,
     return cudaSuccess;
   if (V <= 0 || !ids || !prob || !max_logit)
     return cudaErrorInvalidValue;
-  logits_argmax_kernel<<<rows, 256, 0, s>>>(logits, V, ids, prob, max_logit,
-                                            calc_prob);
+  const size_t row_bytes = (2ull * V + 31) & ~size_t(15);
+  if ((reinterpret_cast<uintptr_t>(logits) & 15) == 0 && row_bytes <= 200 * 1024) {
+    static std::once_flag once[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaError_t attr = cudaSuccess;
+    std::call_once(once[dev & 63], [&] {
+      attr = cudaFuncSetAttribute(logits_argmax_bulk_kernel,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  200 * 1024);
+    });
+    if (attr != cudaSuccess)
+      return attr;
+    logits_argmax_bulk_kernel<<<rows, kArgmaxThreads, row_bytes, s>>>(
+        logits, V, ids, prob, max_logit, calc_prob, device_error_word());
+  } else {
+    logits_argmax_kernel<<<rows, kArgmaxThreads, 0, s>>>(logits, V, ids, prob,
+                                                         max_logit, calc_prob);
+  }
   return cudaGetLastError();
 }
 

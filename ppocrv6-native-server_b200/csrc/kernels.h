@@ -44,6 +44,16 @@ struct ConvShape {
 cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
                     const GemmEpilogue &epi, cudaStream_t stream);
 
+// Transposed convolution with kernel == stride (no padding) on the tensor
+// cores, Co a multiple of 64: a 1x1 implicit GEMM over the input pixels with
+// N = KH*KW*Co columns, each 64-column chunk (one tap's channel block) stored
+// to its stride-interleaved output pixels. wpacked [KH*KW*Co][Ci] (tap-major
+// rows, K-major), bias_rep [KH*KW*Co] (the bias repeated per tap) or null;
+// y [batch][H*KH][W*KW][Co]. Rounding as the fused conv epilogue.
+cudaError_t tc_deconv(const half *x, const half *wpacked, const half *bias_rep,
+                      half *y, int batch, int H, int W, int Ci, int Co, int KH,
+                      int KW, int act, cudaStream_t stream);
+
 // Vocabulary projection with fused row argmax / softmax-max reduction:
 // logits[r][v] = hidden[r][:] . wt[v][:] + bias[v] (fp32), reduced over v to
 // (max, lowest argmax, sum exp(l - max)) per vocabulary tile of 256 columns.
@@ -185,6 +195,11 @@ cudaError_t binarize(const float *prob, uint8_t *map, size_t n, float thresh,
                      cudaStream_t stream);
 // Transposed conv, kernel == stride, no padding (DB head 2x2 s2):
 // x [batch][H][W][Ci], w [Ci][KH][KW][Co], y [batch][H*KH][W*KW][Co].
+// Packs a [Ci][KH][KW][Co] transposed-conv filter for tc_deconv
+// ([KH*KW*Co][Ci]) and repeats the bias per tap (bias may be null).
+cudaError_t deconv_pack(const half *w, const half *bias, half *wpacked,
+                        half *bias_rep, int Ci, int Co, int KH, int KW,
+                        cudaStream_t s);
 cudaError_t deconv_kxk(const half *x, const half *w, const half *bias, half *y,
                        int batch, int H, int W, int Ci, int Co, int KH, int KW,
                        int act, cudaStream_t stream);

@@ -99,6 +99,16 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map,
       "r"(c2), "r"(c3)
       : "memory");
 }
+// Untiled bulk copy global -> this CTA's shared memory, completing on an
+// mbarrier. Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src,
+                                          uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes "
+               "[%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes),
+               "r"(smem_u32(bar))
+               : "memory");
+}
 // Tiled bulk-tensor stores from this CTA's shared memory (bulk-group
 // completion). Out-of-range rows/columns of the box are not written.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map,
@@ -115,6 +125,15 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap *map,
                "[%0, {%2, %3, %4, %5}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
                "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_5d(const CUtensorMap *map,
+                                             const void *src, int c0, int c1,
+                                             int c2, int c3, int c4) {
+  asm volatile("cp.async.bulk.tensor.5d.global.shared::cta.tile.bulk_group "
+               "[%0, {%2, %3, %4, %5, %6}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() {
@@ -274,5 +293,64 @@ __device__ __forceinline__ float apply_act(float x, int act) {
     return x;
   }
 }
+
+// Mixed-precision arithmetic (PTX ISA 8.6, sm_100): fp16 operands with an
+// fp32 accumulator in one instruction. fp16 -> fp32 conversion is exact and
+// the product of two fp16 values is exact in fp32, so fma2_h gives the same
+// bits as fmaf(float(x), float(w), acc) and add2_h as acc + float(x).
+// x and w hold two fp16 values each (low half, high half).
+__device__ __forceinline__ void fma2_h(float &lo, float &hi, uint32_t x,
+                                       uint32_t w) {
+  asm("{.reg .f16 xl, xh, wl, wh;\n\t"
+      "mov.b32 {xl, xh}, %2;\n\t"
+      "mov.b32 {wl, wh}, %3;\n\t"
+      "fma.rn.f32.f16 %0, xl, wl, %0;\n\t"
+      "fma.rn.f32.f16 %1, xh, wh, %1;}"
+      : "+f"(lo), "+f"(hi)
+      : "r"(x), "r"(w));
+}
+__device__ __forceinline__ void add2_h(float &lo, float &hi, uint32_t x) {
+  asm("{.reg .f16 xl, xh;\n\t"
+      "mov.b32 {xl, xh}, %2;\n\t"
+      "add.rn.f32.f16 %0, xl, %0;\n\t"
+      "add.rn.f32.f16 %1, xh, %1;}"
+      : "+f"(lo), "+f"(hi)
+      : "r"(x));
+}
+// 2^x on the special-function unit (approximate, subnormal results flushed).
+// exp(v - m) is computed as ex2(v * log2(e) - m * log2(e)).
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Host: encodes an fp16 tiled tensor map (innermost dimension first, byte
+// strides for dimensions 1..rank-1; out-of-range elements read as zero),
+// 128-byte swizzled or unswizzled. False if the driver rejects it.
+bool encode_fp16_map(CUtensorMap *m, const void *base, int rank,
+                     const cuuint64_t *dims, const cuuint64_t *strides,
+                     const cuuint32_t *box, bool swizzle128);
+
+// Unsigned division by a run-time invariant for dividends below 2^31
+// (Granlund & Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994): with l = ceil(log2 d) and
+// m = floor(2^32 (2^l - d) / d) + 1, n / d = (umulhi(n, m) + n) >> l.
+// Kernels index their work items with 32-bit counters and these in place
+// of 64-bit divisions (which compile to long instruction sequences).
+struct FastDiv {
+  uint32_t d = 1, m = 1, l = 0;
+  FastDiv() = default;
+  __host__ explicit FastDiv(uint32_t div) : d(div) {
+    l = 0;
+    while ((1ull << l) < div)
+      ++l;
+    m = static_cast<uint32_t>(((1ull << 32) * ((1ull << l) - div)) / div + 1);
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+    return (__umulhi(n, m) + n) >> l;
+  }
+};
 
 } // namespace pb2

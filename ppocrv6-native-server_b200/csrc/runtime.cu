@@ -169,6 +169,25 @@ void Runtime::deconv(int ai, int wi, int yi, Shape xs, Shape ws, Shape ys,
   const int KH = ws[2], KW = ws[3];
   if (ys[1] != Co || ys[2] != H * KH || ys[3] != W * KW)
     throw std::runtime_error("deconv output shape mismatch");
+  const size_t wn = static_cast<size_t>(Ci) * KH * KW * Co;
+  if (Co % 64 == 0 && Ci % 8 == 0 && is_constant(t[wi], wn) &&
+      (bias_id < 0 || is_constant(t[bias_id], static_cast<size_t>(Co)))) {
+    // Tensor-core path: the filter re-laid K-major per tap and the bias
+    // repeated per tap, once, at prepare time.
+    half *wp = static_cast<half *>(own(wn * sizeof(half)));
+    half *bp = bias_id >= 0 ? static_cast<half *>(own(sizeof(half) * KH * KW * Co)) : nullptr;
+    prepare.emplace_back([=] {
+      check(deconv_pack(t[wi], bias_id >= 0 ? t[bias_id] : nullptr, wp, bp, Ci,
+                        Co, KH, KW, stream),
+            "pack deconv weight");
+    });
+    add("deconv_tc", [=] {
+      check(tc_deconv(t[ai], wp, bp, t[yi], B, H, W, Ci, Co, KH, KW, activation,
+                      stream),
+            "tc_deconv");
+    });
+    return;
+  }
   add("deconv", [=] {
     check(deconv_kxk(t[ai], t[wi], bias_id >= 0 ? t[bias_id] : nullptr, t[yi],
                      B, H, W, Ci, Co, KH, KW, activation, stream),

@@ -294,6 +294,112 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Short-sequence attention (seq <= SMAX, head_dim <= 16), one line per
+// block, one thread per (head, query) row doing the whole row: the K and V
+// of the line are staged in shared memory ([head][key][16], zero-padded);
+// the thread keeps q' = round(q*scale) and its row of scores in registers,
+// S = round(q'.k) (fp16 operands, fp32 sums, two interleaved chains over d),
+// P = round(exp(S - max) * (1/sum)) with exp on the special-function unit,
+// O = round(sum_j P_j v_j) (j ascending, fp32). The K/V reads are warp-wide
+// broadcasts (a warp's rows share a head); every multiply-add is one
+// mixed-precision instruction.
+template <int SMAX>
+__global__ void __launch_bounds__(512)
+    attention_rows_kernel(const half *__restrict__ qkv, half *__restrict__ out,
+                          int seq, int heads, int dh, float scale,
+                          FastDiv by_hd, FastDiv by_dh, FastDiv by_seq) {
+  constexpr int DP = 16;
+  extern __shared__ uint4 att_smem[];
+  half *ks = reinterpret_cast<half *>(att_smem); // [heads][seq][DP]
+  half *vs = ks + heads * seq * DP;
+  const int hd = heads * dh;
+  const int width = 3 * hd;
+  const long long line = blockIdx.x;
+  const half *src = qkv + line * seq * width;
+  const half zero = __float2half_rn(0.f);
+  for (int e = threadIdx.x; e < heads * seq * DP; e += blockDim.x)
+    ks[e] = vs[e] = zero;
+  __syncthreads();
+  for (uint32_t e = threadIdx.x; e < static_cast<uint32_t>(seq * hd); e += blockDim.x) {
+    const uint32_t j = by_hd.div(e), c = e - j * hd;
+    const uint32_t h = by_dh.div(c), d = c - h * dh;
+    const int at = (h * seq + j) * DP + d;
+    ks[at] = src[j * width + hd + c];
+    vs[at] = src[j * width + 2 * hd + c];
+  }
+  __syncthreads();
+  const int rows = heads * seq;
+  for (int row = threadIdx.x; row < rows; row += blockDim.x) {
+    const int h = static_cast<int>(by_seq.div(row));
+    const int i = row - h * seq;
+    const half *qr = src + i * width + h * dh;
+    uint32_t q[DP / 2];
+#pragma unroll
+    for (int d2 = 0; d2 < DP / 2; ++d2) {
+      const int d = 2 * d2;
+      const half lo = d < dh ? __float2half_rn(__half2float(qr[d]) * scale) : zero;
+      const half hi = d + 1 < dh ? __float2half_rn(__half2float(qr[d + 1]) * scale) : zero;
+      q[d2] = static_cast<uint32_t>(__half_as_ushort(lo)) |
+              (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+    }
+    const uint4 *k4 = reinterpret_cast<const uint4 *>(ks + h * seq * DP);
+    float sc[SMAX];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < SMAX; ++j) {
+      if (j < seq) {
+        const uint4 a = k4[2 * j], b = k4[2 * j + 1];
+        float e0 = 0.f, e1 = 0.f;
+        fma2_h(e0, e1, q[0], a.x);
+        fma2_h(e0, e1, q[1], a.y);
+        fma2_h(e0, e1, q[2], a.z);
+        fma2_h(e0, e1, q[3], a.w);
+        fma2_h(e0, e1, q[4], b.x);
+        fma2_h(e0, e1, q[5], b.y);
+        fma2_h(e0, e1, q[6], b.z);
+        fma2_h(e0, e1, q[7], b.w);
+        sc[j] = round_half(e0 + e1);
+        m = fmaxf(m, sc[j]);
+      }
+    }
+    const float mL = m * kLog2e;
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < SMAX; ++j)
+      if (j < seq) {
+        sc[j] = ex2_ftz(fmaf(sc[j], kLog2e, -mL));
+        sum += sc[j];
+      }
+    const float inv = 1.f / sum;
+    float o[DP];
+#pragma unroll
+    for (int d = 0; d < DP; ++d)
+      o[d] = 0.f;
+    const uint4 *v4 = reinterpret_cast<const uint4 *>(vs + h * seq * DP);
+#pragma unroll
+    for (int j = 0; j < SMAX; ++j) {
+      if (j < seq) {
+        const uint32_t pb = __half_as_ushort(__float2half_rn(sc[j] * inv));
+        const uint32_t pp = pb | (pb << 16);
+        const uint4 a = v4[2 * j], b = v4[2 * j + 1];
+        fma2_h(o[0], o[1], pp, a.x);
+        fma2_h(o[2], o[3], pp, a.y);
+        fma2_h(o[4], o[5], pp, a.z);
+        fma2_h(o[6], o[7], pp, a.w);
+        fma2_h(o[8], o[9], pp, b.x);
+        fma2_h(o[10], o[11], pp, b.y);
+        fma2_h(o[12], o[13], pp, b.z);
+        fma2_h(o[14], o[15], pp, b.w);
+      }
+    }
+    half *dst = out + (line * seq + i) * hd + h * dh;
+#pragma unroll
+    for (int d = 0; d < DP; ++d)
+      if (d < dh)
+        dst[d] = __float2half_rn(o[d]);
+  }
+}
+
 unsigned rows_blocks(int rows) { return static_cast<unsigned>((rows + 7) / 8); }
 
 } // namespace
@@ -346,6 +452,17 @@ cudaError_t attention(const half *qkv, half *out, int lines, int seq, int heads,
                       int dh, float scale, cudaStream_t s) {
   if (lines <= 0)
     return cudaSuccess;
+  if (dh <= 16 && seq <= 64) {
+    const int rows = heads * seq;
+    const int threads = rows >= 512 ? 512 : (rows + 31) / 32 * 32;
+    const size_t smem = sizeof(half) * 2ull * heads * seq * 16;
+    if (smem <= 48 * 1024) {
+      attention_rows_kernel<64><<<lines, threads, smem, s>>>(
+          qkv, out, seq, heads, dh, scale, FastDiv(heads * dh), FastDiv(dh),
+          FastDiv(seq));
+      return cudaGetLastError();
+    }
+  }
   if (dh <= 32) {
     const int dp = dh <= 16 ? 16 : 32;
     const size_t staged =

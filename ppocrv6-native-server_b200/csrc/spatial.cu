@@ -46,7 +46,8 @@ __global__ void __launch_bounds__(kBlock, 4)
     depthwise_kernel(const half *__restrict__ x, const half *__restrict__ w,
                      const half *__restrict__ bias, half *__restrict__ y,
                      int batch, int C, int H, int W, int OH, int OW, int PH,
-                     int PW, int act) {
+                     int PW, int act, uint32_t total, FastDiv by_groups,
+                     FastDiv by_tiles, FastDiv by_oh) {
   extern __shared__ uint4 dw_smem[];
   half *ws = reinterpret_cast<half *>(dw_smem);
   constexpr int TAPS = KH * KW;
@@ -56,17 +57,16 @@ __global__ void __launch_bounds__(kBlock, 4)
   }
   __syncthreads();
   constexpr int NCOL = (PIX - 1) * SW + KW;
-  const int groups = C >> 3;
-  const int tiles = (OW + PIX - 1) / PIX;
-  const long long total = static_cast<long long>(batch) * OH * tiles * groups;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-       i < total; i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int g = static_cast<int>(i % groups);
-    long long t = i / groups;
-    const int tile = static_cast<int>(t % tiles);
-    t /= tiles;
-    const int oh = static_cast<int>(t % OH);
-    const int n = static_cast<int>(t / OH);
+  // Item i = ((n * OH + oh) * tiles + tile) * groups + g, below 2^31.
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += gridDim.x * blockDim.x) {
+    const uint32_t t0 = by_groups.div(i);
+    const int g = static_cast<int>(i - t0 * by_groups.d);
+    const uint32_t t1 = by_tiles.div(t0);
+    const int tile = static_cast<int>(t0 - t1 * by_tiles.d);
+    const uint32_t n_ = by_oh.div(t1);
+    const int oh = static_cast<int>(t1 - n_ * by_oh.d);
+    const int n = static_cast<int>(n_);
     const int c0 = g * 8;
     const int ow0 = tile * PIX;
     const int col0 = ow0 * SW - PW;
@@ -95,23 +95,16 @@ __global__ void __launch_bounds__(kBlock, 4)
       }
 #pragma unroll
       for (int b = 0; b < KW; ++b) {
-        Pack8 wt;
-        wt.u = *reinterpret_cast<const uint4 *>(ws + (a * KW + b) * C + c0);
-        float wv[8];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float2 f = __half22float2(wt.h[j]);
-          wv[2 * j] = f.x;
-          wv[2 * j + 1] = f.y;
-        }
+        const uint4 wt = *reinterpret_cast<const uint4 *>(ws + (a * KW + b) * C + c0);
 #pragma unroll
         for (int p = 0; p < PIX; ++p) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float2 f = __half22float2(strip[p * SW + b].h[j]);
-            acc[p][2 * j] = fmaf(f.x, wv[2 * j], acc[p][2 * j]);
-            acc[p][2 * j + 1] = fmaf(f.y, wv[2 * j + 1], acc[p][2 * j + 1]);
-          }
+          // fp16 x fp16 + fp32 in one instruction: same bits as fmaf on the
+          // converted values.
+          const uint4 xv = strip[p * SW + b].u;
+          fma2_h(acc[p][0], acc[p][1], xv.x, wt.x);
+          fma2_h(acc[p][2], acc[p][3], xv.y, wt.y);
+          fma2_h(acc[p][4], acc[p][5], xv.z, wt.z);
+          fma2_h(acc[p][6], acc[p][7], xv.w, wt.w);
         }
       }
     }
@@ -202,6 +195,174 @@ __global__ void __launch_bounds__(kBlock)
       y + ((static_cast<long long>(n) * OH + oh) * OW + ow) * C + c0) = o.u;
 }
 
+// TMA-staged form: a block computes one output row x TW output columns x
+// CB (<= 64) channels. One 4-D TMA box brings the KH input rows x
+// ((TW-1)*SW + KW) columns x CB channels it needs into shared memory
+// (zero-filled outside the image: the padding), the filter slice is staged
+// tap-major beside it, and each thread computes PIX columns x 8 channels
+// from shared memory with the same tap order and one mixed-precision FMA
+// per multiply-add as depthwise_kernel (bit-identical results).
+template <int KH, int KW, int SH, int SW, int PIX, int ACT>
+__global__ void __launch_bounds__(256)
+    depthwise_tma_kernel(const __grid_constant__ CUtensorMap xmap,
+                         const half *__restrict__ w,
+                         const half *__restrict__ bias, half *__restrict__ y,
+                         int C, int H, int OH, int OW, int PH, int PW, int CB,
+                         int TW, int tiles_w, int chunks, int act, int *err) {
+  constexpr int TAPS = KH * KW;
+  constexpr int NCOL = (PIX - 1) * SW + KW;
+  extern __shared__ __align__(128) uint8_t dwt_smem[];
+  __shared__ uint64_t bar;
+  __shared__ int failed;
+  const int twin = (TW - 1) * SW + KW;
+  half *xs = reinterpret_cast<half *>(dwt_smem);           // [KH][twin][CB]
+  half *ws = xs + KH * twin * CB;                           // [TAPS][CB]
+  // block -> (n, oh, column tile, channel chunk)
+  int b = blockIdx.x;
+  const int chunk = b % chunks;
+  b /= chunks;
+  const int tw = b % tiles_w;
+  b /= tiles_w;
+  const int oh = b % OH;
+  const int n = b / OH;
+  const int c0 = chunk * CB, ow0 = tw * TW;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    failed = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bar, static_cast<uint32_t>(KH * twin * CB * 2));
+    tma_load_4d(xs, &xmap, &bar, c0, ow0 * SW - PW, oh * SH - PH, n);
+  }
+  for (int j = threadIdx.x; j < TAPS * CB; j += blockDim.x) {
+    const int tap = j / CB, c = j - tap * CB; // w is [C][KH][KW]
+    ws[j] = w[static_cast<long long>(c0 + c) * TAPS + tap];
+  }
+  volatile int no_abort = 0;
+  const bool ok = mbar_wait(&bar, 0, &no_abort);
+  if (!ok)
+    failed = 1;
+  __syncthreads();
+  if (failed) {
+    if (!ok)
+      mbar_wait(&bar, 0, &no_abort);
+    if (threadIdx.x == 0 && err)
+      atomicCAS(err, 0, 7);
+    return;
+  }
+  const int groups = CB >> 3;
+  const int g = threadIdx.x % groups;
+  const int t = threadIdx.x / groups;
+  if (t * PIX >= TW)
+    return;
+  float acc[PIX][8];
+#pragma unroll
+  for (int p = 0; p < PIX; ++p)
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      acc[p][j] = 0.f;
+  const int col0 = t * PIX * SW;
+#pragma unroll
+  for (int a = 0; a < KH; ++a) {
+    // Rows outside the image (zero in shared memory) are skipped, as the
+    // reference does.
+    const int r = oh * SH - PH + a;
+    if (r < 0 || r >= H)
+      continue;
+    const uint4 *row = reinterpret_cast<const uint4 *>(xs + (a * twin + col0) * CB) + g;
+    uint4 strip[NCOL];
+#pragma unroll
+    for (int k = 0; k < NCOL; ++k)
+      strip[k] = row[k * groups];
+#pragma unroll
+    for (int bq = 0; bq < KW; ++bq) {
+      const uint4 wt = reinterpret_cast<const uint4 *>(ws + (a * KW + bq) * CB)[g];
+#pragma unroll
+      for (int p = 0; p < PIX; ++p) {
+        const uint4 xv = strip[p * SW + bq];
+        fma2_h(acc[p][0], acc[p][1], xv.x, wt.x);
+        fma2_h(acc[p][2], acc[p][3], xv.y, wt.y);
+        fma2_h(acc[p][4], acc[p][5], xv.z, wt.z);
+        fma2_h(acc[p][6], acc[p][7], xv.w, wt.w);
+      }
+    }
+  }
+  float bv[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    bv[j] = bias ? __half2float(bias[c0 + g * 8 + j]) : 0.f;
+#pragma unroll
+  for (int p = 0; p < PIX; ++p) {
+    const int ow = ow0 + t * PIX + p;
+    if (ow >= OW)
+      break;
+    Pack8 o;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float v0 = round_half(acc[p][2 * j]);
+      float v1 = round_half(acc[p][2 * j + 1]);
+      if (bias) {
+        v0 = act_t<ACT>(v0 + bv[2 * j], act);
+        v1 = act_t<ACT>(v1 + bv[2 * j + 1], act);
+      }
+      o.h[j] = __floats2half2_rn(v0, v1);
+    }
+    *reinterpret_cast<uint4 *>(
+        y + ((static_cast<long long>(n) * OH + oh) * OW + ow) * C + c0 + g * 8) = o.u;
+  }
+}
+
+template <int KH, int KW, int SH, int SW>
+cudaError_t launch_dw_tma(const half *x, const half *w, const half *bias,
+                          half *y, int batch, int C, int H, int W, int OH,
+                          int OW, int PH, int PW, int act, cudaStream_t s,
+                          bool *handled) {
+  *handled = false;
+  constexpr int PIX = 2;
+  const int CB = C % 64 == 0 ? 64 : (C <= 64 ? C : 0);
+  if (!CB || (reinterpret_cast<uintptr_t>(x) & 15))
+    return cudaSuccess;
+  const int groups = CB / 8;
+  const int ntile = 256 / groups;     // column items per block
+  const int TW = ntile * PIX;         // output columns per block
+  const int twin = (TW - 1) * SW + KW;
+  if (twin > 256)
+    return cudaSuccess;
+  const size_t smem =
+      sizeof(half) * (static_cast<size_t>(KH) * twin * CB + KH * KW * CB);
+  if (smem > 200 * 1024)
+    return cudaSuccess;
+  const int tiles_w = (OW + TW - 1) / TW;
+  const int chunks = C / CB;
+  const long long blocks = static_cast<long long>(batch) * OH * tiles_w * chunks;
+  if (blocks >= (1LL << 31))
+    return cudaSuccess;
+  CUtensorMap map;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(W),
+                        static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(C) * 2,
+                           static_cast<cuuint64_t>(W) * C * 2,
+                           static_cast<cuuint64_t>(H) * W * C * 2};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(CB), static_cast<cuuint32_t>(twin),
+                       static_cast<cuuint32_t>(KH), 1};
+  if (!encode_fp16_map(&map, x, 4, dims, strides, box, false))
+    return cudaSuccess;
+  auto kernel = act == kActRelu        ? depthwise_tma_kernel<KH, KW, SH, SW, PIX, kActRelu>
+                : act == kActHardSwish ? depthwise_tma_kernel<KH, KW, SH, SW, PIX, kActHardSwish>
+                                       : depthwise_tma_kernel<KH, KW, SH, SW, PIX, -1>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess)
+    return e;
+  *handled = true;
+  kernel<<<static_cast<unsigned>(blocks), 256, smem, s>>>(
+      map, w, bias, y, C, H, OH, OW, PH, PW, CB, TW, tiles_w, chunks, act,
+      device_error_word());
+  return cudaGetLastError();
+}
+
 template <int KH, int KW, int SH, int SW>
 cudaError_t launch_dw(const half *x, const half *w, const half *bias, half *y,
                       int batch, int C, int H, int W, int OH, int OW, int PH,
@@ -209,10 +370,10 @@ cudaError_t launch_dw(const half *x, const half *w, const half *bias, half *y,
   // Two output columns per item keeps the kernel at <= 64 registers (four
   // resident blocks per SM) so enough loads are in flight to cover latency.
   constexpr int PIX = 2;
-  const long long total =
-      static_cast<long long>(batch) * OH * ((OW + PIX - 1) / PIX) * (C / 8);
+  const int tiles = (OW + PIX - 1) / PIX;
+  const long long total = static_cast<long long>(batch) * OH * tiles * (C / 8);
   const size_t smem = static_cast<size_t>(C) * KH * KW * sizeof(half);
-  if (smem > 200 * 1024)
+  if (smem > 200 * 1024 || total >= (1LL << 31))
     return cudaErrorInvalidValue;
   long long blocks = (total + kBlock - 1) / kBlock;
   const long long cap = static_cast<long long>(sm_count()) * 16;
@@ -231,7 +392,8 @@ cudaError_t launch_dw(const half *x, const half *w, const half *bias, half *y,
       return e;
   }
   kernel<<<static_cast<unsigned>(blocks), kBlock, smem, s>>>(
-      x, w, bias, y, batch, C, H, W, OH, OW, PH, PW, act);
+      x, w, bias, y, batch, C, H, W, OH, OW, PH, PW, act,
+      static_cast<uint32_t>(total), FastDiv(C / 8), FastDiv(tiles), FastDiv(OH));
   return cudaGetLastError();
 }
 
@@ -304,7 +466,8 @@ __global__ void __launch_bounds__(kBlock)
     stem_conv_kernel(const half *__restrict__ x, const half *__restrict__ w,
                      const half *__restrict__ bias, half *__restrict__ y,
                      int batch, int Ci, int H, int W, int OH, int OW, int KH,
-                     int KW, int SH, int SW, int PH, int PW, int act) {
+                     int KW, int SH, int SW, int PH, int PW, int act,
+                     uint32_t total, FastDiv by_ow, FastDiv by_oh) {
   extern __shared__ float wsm[];
   const int taps = KH * KW * Ci;
   for (int j = threadIdx.x; j < taps * CO; j += blockDim.x) {
@@ -312,13 +475,14 @@ __global__ void __launch_bounds__(kBlock)
     wsm[k * CO + co] = __half2float(w[j]);
   }
   __syncthreads();
-  const long long p = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long long total = static_cast<long long>(batch) * OH * OW;
+  const uint32_t p = blockIdx.x * blockDim.x + threadIdx.x; // below 2^31
   if (p >= total)
     return;
-  const int ow = static_cast<int>(p % OW);
-  const int oh = static_cast<int>((p / OW) % OH);
-  const long long n = p / (static_cast<long long>(OW) * OH);
+  const uint32_t r0 = by_ow.div(p);
+  const int ow = static_cast<int>(p - r0 * by_ow.d);
+  const uint32_t n0 = by_oh.div(r0);
+  const int oh = static_cast<int>(r0 - n0 * by_oh.d);
+  const long long n = n0;
   float acc[CO];
 #pragma unroll
   for (int c = 0; c < CO; ++c)
@@ -346,7 +510,7 @@ __global__ void __launch_bounds__(kBlock)
       }
     }
   }
-  half *dst = y + p * CO;
+  half *dst = y + static_cast<long long>(p) * CO;
 #pragma unroll
   for (int g = 0; g < CO / 8; ++g) {
     Pack8 o;
@@ -777,9 +941,16 @@ cudaError_t depthwise(const half *x, const half *w, const half *bias, half *y,
   if (C % 8 || !al16(x) || !al16(y))
     return cudaErrorInvalidValue;
 #define PB2_DW(kh, kw, sh, sw)                                                 \
-  if (KH == kh && KW == kw && SH == sh && SW == sw)                            \
+  if (KH == kh && KW == kw && SH == sh && SW == sw) {                          \
+    bool handled = false;                                                      \
+    cudaError_t e = launch_dw_tma<kh, kw, sh, sw>(x, w, bias, y, batch, C, H,  \
+                                                  W, OH, OW, PH, PW, act, s,   \
+                                                  &handled);                   \
+    if (handled || e != cudaSuccess)                                           \
+      return e;                                                                \
     return launch_dw<kh, kw, sh, sw>(x, w, bias, y, batch, C, H, W, OH, OW,    \
-                                     PH, PW, act, s);
+                                     PH, PW, act, s);                          \
+  }
   PB2_DW(3, 3, 1, 1)
   PB2_DW(3, 3, 2, 2)
   PB2_DW(3, 3, 2, 1)
@@ -803,12 +974,16 @@ cudaError_t direct_conv(const half *x, const half *w, const half *bias,
   const size_t smem = sizeof(float) * static_cast<size_t>(Co) * KH * KW * Ci;
   if (Co % 8 || !al16(y) || smem > 48 * 1024)
     return cudaErrorInvalidValue;
-  if (Ci <= 4 && (Co == 16 || Co == 32 || Co == 48 || Co == 64)) {
-    const long long pixels = static_cast<long long>(batch) * OH * OW;
+  const long long pixels = static_cast<long long>(batch) * OH * OW;
+  if (Ci <= 4 && (Co == 16 || Co == 32 || Co == 48 || Co == 64) &&
+      pixels < (1LL << 31)) {
 #define PB2_STEM(co)                                                           \
   if (Co == co) {                                                              \
-    (act == kActRelu ? stem_conv_kernel<co, kActRelu> : stem_conv_kernel<co, -1>)<<<blocks_for(pixels), kBlock, smem, s>>>(             \
-        x, w, bias, y, batch, Ci, H, W, OH, OW, KH, KW, SH, SW, PH, PW, act);  \
+    (act == kActRelu ? stem_conv_kernel<co, kActRelu>                          \
+                     : stem_conv_kernel<co, -1>)<<<blocks_for(pixels), kBlock, \
+                                                   smem, s>>>(                 \
+        x, w, bias, y, batch, Ci, H, W, OH, OW, KH, KW, SH, SW, PH, PW, act,   \
+        static_cast<uint32_t>(pixels), FastDiv(OW), FastDiv(OH));              \
     return cudaGetLastError();                                                 \
   }
     PB2_STEM(16)

@@ -13,6 +13,13 @@
 // The TMEM accumulator is double buffered so the epilogue of tile i overlaps
 // the main loop of tile i+1. Operand tiles are K-major, 128-byte swizzled.
 //
+// Long-K layers use 256-row tiles instead (MH = 2 M halves): both halves
+// multiply the same B stage, so a k-block moves 64 KB of operands for
+// 2x128x256x64 MACs instead of 48 KB for half of that (a third fewer bytes
+// from L2 per FLOP, and 3 x 64 KB of loads in flight). The two halves fill
+// all 512 TMEM columns, so the accumulator is single buffered and 8
+// epilogue warps (two per lane quarter, one per half) drain it.
+//
 // Implicit GEMM: output rows are enumerated as (image, out_row, pixel
 // segment of 16 or 32); one A stage (128 rows x 64 channels of one filter
 // tap) is eight (or four) 4-D TMA boxes of one segment x 64 channels at the
@@ -24,6 +31,7 @@
 #include <cfloat>
 #include <climits>
 #include <mutex>
+#include <type_traits>
 #include <vector>
 
 namespace pb2 {
@@ -31,15 +39,21 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-enum Epi : int { kEpiStore = 0, kEpiVocab = 1 };
+// Epilogues: fused store (NHWC / row-major output), vocabulary argmax/exp
+// partials, and the transposed-convolution store (each 64-column chunk is
+// one filter tap of KH x KW, written to its stride-interleaved output
+// pixels through a 5-D tensor map).
+enum Epi : int { kEpiStore = 0, kEpiVocab = 1, kEpiDeconv = 2 };
 
-// Epilogue warps: 4 (one per TMEM lane quarter) for stores; 16 for the
-// exp-heavy vocabulary reduction (four warps per quarter, 64 columns each).
-template <int EPI> struct EpiWarps {
-  static constexpr int value = EPI == kEpiVocab ? 16 : 4;
+// Epilogue warps: 4 (one per TMEM lane quarter) for stores, 8 with 256-row
+// tiles (one per quarter and M half); 16 for the exp-heavy vocabulary
+// reduction (four warps per quarter, 64 columns each).
+template <int EPI, int MH> struct EpiWarps {
+  static constexpr int value = EPI == kEpiVocab ? 16 : 4 * MH;
 };
-template <int EPI> constexpr int threads_for() {
-  return 64 + 32 * EpiWarps<EPI>::value;
+static_assert(kEpiDeconv != kEpiVocab, "deconv uses the store warps");
+template <int EPI, int MH> constexpr int threads_for() {
+  return 64 + 32 * EpiWarps<EPI, MH>::value;
 }
 
 struct Args {
@@ -55,23 +69,32 @@ struct Args {
   int *part_id;
   float *part_sum;
   int part_ld, calc_prob;
+  int dec_co, dec_kw; // deconv: output channels, filter width
   int *err;
 };
 
-template <int BN> struct Cfg {
-  static constexpr uint32_t A_BYTES = kBM * kBK * 2;
+template <int BN, int MH = 1> struct Cfg {
+  static constexpr int BM = kBM * MH;                  // tile rows
+  static constexpr uint32_t A_HALF = kBM * kBK * 2;    // one 128-row A block
+  static constexpr uint32_t A_BYTES = MH * A_HALF;
   static constexpr uint32_t B_BYTES = BN * kBK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  // Accumulator buffers: two (epilogue overlaps the next tile) with one M
+  // half; one holding both halves with two.
+  static constexpr int NACC = MH == 1 ? 2 : 1;
   static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
   static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
   // TMA-store epilogue: each epilogue warp stages 32 rows x 64 columns
-  // (4 KB, 128-byte swizzled) in a double buffer, then one lane stores it.
+  // (4 KB, 128-byte swizzled), double buffered with 4 epilogue warps and
+  // single buffered with 8, then one lane stores it.
   static constexpr bool TMA_EPI = BN % 64 == 0;
-  static constexpr uint32_t EPI_BYTES = TMA_EPI ? 4 * 2 * 4096 : 0;
+  static constexpr int EPI_BUFS = MH == 1 ? 2 : 1;
+  static constexpr uint32_t EPI_BYTES = TMA_EPI ? 4 * MH * EPI_BUFS * 4096 : 0;
   static constexpr size_t SMEM =
       size_t(STAGES) * STAGE_BYTES + EPI_BYTES + 1024 + 256;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
+  static_assert(MH == 1 || (MH == 2 && BN == 256), "256-row tiles use N = 256");
   static_assert(B_BYTES % 1024 == 0, "B tile must keep 1024-byte alignment");
   static_assert(SMEM <= 232448, "dynamic shared memory above 227 KB");
 };
@@ -126,13 +149,15 @@ __device__ __forceinline__ void fail(const Args &g, volatile int *abort,
     atomicCAS(g.err, 0, code);
 }
 
-template <int BN, bool CONV, int EPI, int ACT>
-__global__ void __launch_bounds__(threads_for<EPI>(), 1)
+template <int BN, bool CONV, int EPI, int ACT, int MH>
+__global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap mapA,
                    const __grid_constant__ CUtensorMap mapB,
                    const __grid_constant__ CUtensorMap mapC,
                    const __grid_constant__ Args g) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, MH>;
+  constexpr int BM = C::BM;
+  constexpr int NACC = C::NACC;
   constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -161,7 +186,7 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 32 * EpiWarps<EPI>::value);
+      mbar_init(&tempty[a], 32 * EpiWarps<EPI, MH>::value);
     }
     mbar_init(drain, 1);
     for (int p = 0; p < 8; ++p)
@@ -189,15 +214,16 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
         const int mb = tile / g.nt, nb = tile - mb * g.nt;
-        // Implicit GEMM: the pixel segments of this M tile (8 of 16 pixels or
-        // 4 of 32) are fixed for the whole K loop; only the filter tap and
-        // channel block move.
-        const int nbox = kBM >> g.seg_log2;
-        int seg_x[kBM / 16], seg_y[kBM / 16], seg_n[kBM / 16];
+        // Implicit GEMM: the pixel segments of this M tile (BM/16 of 16
+        // pixels or BM/32 of 32) are fixed for the whole K loop; only the
+        // filter tap and channel block move.
+        const int nbox = BM >> g.seg_log2;
+        const int seg0 = mb * nbox;
+        int seg_x[BM / 16], seg_y[BM / 16], seg_n[BM / 16];
         if (CONV) {
 #pragma unroll
-          for (int s = 0; s < kBM / 16; ++s) {
-            const int seg = (mb << (7 - g.seg_log2)) + s;
+          for (int s = 0; s < BM / 16; ++s) {
+            const int seg = seg0 + s;
             const int r = seg / g.Wseg;
             seg_x[s] = ((seg - r * g.Wseg) << g.seg_log2) - g.pad_w;
             seg_n[s] = r / g.OH;
@@ -218,7 +244,7 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
           issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
           if (CONV) {
 #pragma unroll
-            for (int s = 0; s < kBM / 16; ++s)
+            for (int s = 0; s < BM / 16; ++s)
               if (s < nbox)
                 tma_load_4d(sa + (s << (g.seg_log2 + 7)), &mapA, &full[stage],
                             cb * kBK, seg_x[s] + kw, seg_y[s] + kh, seg_n[s]);
@@ -232,7 +258,10 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
               }
             }
           } else {
-            tma_load_2d(sa, &mapA, &full[stage], kb * kBK, mb * kBM);
+#pragma unroll
+            for (int h = 0; h < MH; ++h)
+              tma_load_2d(sa + h * C::A_HALF, &mapA, &full[stage], kb * kBK,
+                          mb * BM + h * kBM);
             tma_load_2d(sb, &mapB, &full[stage], kb * kBK, nb * BN);
           }
           if (++stage == STAGES) {
@@ -261,8 +290,8 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
       bool ok = true;
       int it = 0;
       for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++it) {
-        const int acc = it & 1;
-        const uint32_t acc_phase = (it >> 1) & 1;
+        const int acc = it % NACC;
+        const uint32_t acc_phase = (it / NACC) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort)) {
           fail(g, abort, 2);
           ok = false;
@@ -280,9 +309,11 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
           const uint32_t a0 = smem_u32(smem + stage * C::STAGE_BYTES);
           const uint32_t b0 = a0 + C::A_BYTES;
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k)
-            umma_f16(d, sdesc_k_sw128(a0 + k * 32), sdesc_k_sw128(b0 + k * 32),
-                     idesc, (kb | k) != 0);
+          for (int h = 0; h < MH; ++h)
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k)
+              umma_f16(d + h * C::ACC_COLS, sdesc_k_sw128(a0 + h * C::A_HALF + k * 32),
+                       sdesc_k_sw128(b0 + k * 32), idesc, (kb | k) != 0);
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -301,25 +332,27 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
   } else {
     // Epilogue warps: TMEM lane quarter is fixed by warp id modulo 4.
     const int q = warp & 3;          // TMEM lane quarter
-    const int hf = (warp - 2) >> 2;  // vocab: column quarter of the tile
-    const int row_in_tile = q * 32 + lane;
+    const int hf = (warp - 2) >> 2;  // vocab: column quarter; MH = 2: M half
+    const int mh = MH == 2 ? hf : 0; // M half drained by this warp
+    const int row_in_tile = mh * kBM + q * 32 + lane;
+    const int ew = warp - 2;         // epilogue warp index (staging buffer)
     int it = 0;
     int epi_buf = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
       const int mb = tile / g.nt, nb = tile - mb * g.nt;
-      const int acc = it & 1;
-      const uint32_t acc_phase = (it >> 1) & 1;
+      const int acc = it % NACC;
+      const uint32_t acc_phase = (it / NACC) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, abort)) {
         fail(g, abort, 4);
         break;
       }
       tc_fence_after();
-      const uint32_t taddr =
-          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * C::ACC_COLS;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                             (acc + mh) * C::ACC_COLS;
       // Map this thread's accumulator row to an output row.
       long long orow = -1;
       if (CONV) {
-        const int seg = (mb << (7 - g.seg_log2)) + (row_in_tile >> g.seg_log2);
+        const int seg = mb * (BM >> g.seg_log2) + (row_in_tile >> g.seg_log2);
         const int r = seg / g.Wseg;
         const int owseg = seg - r * g.Wseg;
         const int n = r / g.OH;
@@ -329,12 +362,12 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
         if (n < g.batch && ow < g.OW)
           orow = (static_cast<long long>(n) * g.OH + oh) * g.OW + ow;
       } else {
-        const int m = mb * kBM + row_in_tile;
+        const int m = mb * BM + row_in_tile;
         if (m < g.M)
           orow = m;
       }
       const int n_base = nb * BN;
-      if (EPI == kEpiStore && C::TMA_EPI) {
+      if constexpr ((EPI == kEpiStore || EPI == kEpiDeconv) && C::TMA_EPI) {
         // 64-column chunks: TMEM -> registers -> fused epilogue -> swizzled
         // smem row (this thread's row) -> one TMA store per warp. TMA drops
         // rows past M / past the image width and columns past N.
@@ -351,12 +384,12 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             packed[j] = epilogue8<ACT>(r + 8 * j, e, n_base + c + 8 * j, g.N, orow);
-          // The store issued from this buffer two chunks ago must have read
-          // its source before the buffer is overwritten.
+          // The store issued from this buffer EPI_BUFS chunks ago must have
+          // read its source before the buffer is overwritten.
           if (lane == 0)
-            bulk_wait_read<1>();
+            bulk_wait_read<C::EPI_BUFS - 1>();
           __syncwarp();
-          uint8_t *buf = epi_smem + (q * 2 + epi_buf) * 4096;
+          uint8_t *buf = epi_smem + (ew * C::EPI_BUFS + (C::EPI_BUFS == 2 ? epi_buf : 0)) * 4096;
           uint8_t *row = buf + lane * 128;
 #pragma unroll
           for (int j = 0; j < 8; ++j)
@@ -368,22 +401,32 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
             if (CONV) {
               // This warp's 32 rows are 32 >> seg_log2 whole segments.
               for (int h = 0; h < (32 >> g.seg_log2); ++h) {
-                const int seg = (mb << (7 - g.seg_log2)) +
-                                ((q * 32) >> g.seg_log2) + h;
+                const int seg = mb * (BM >> g.seg_log2) +
+                                ((mh * kBM + q * 32) >> g.seg_log2) + h;
                 const int rr = seg / g.Wseg;
-                const int n = rr / g.OH;
-                tma_store_4d(&mapC, buf + (h << (g.seg_log2 + 7)), n_base + c,
-                             (seg - rr * g.Wseg) << g.seg_log2, rr - n * g.OH,
-                             n);
+                const int w0 = (seg - rr * g.Wseg) << g.seg_log2;
+                if constexpr (EPI == kEpiDeconv) {
+                  // Columns [n_base + c, +64) are channels co0.. of tap
+                  // (a, b); rr is the input row n * H + h.
+                  const int tap = (n_base + c) / g.dec_co;
+                  const int co0 = n_base + c - tap * g.dec_co;
+                  const int a = tap / g.dec_kw;
+                  tma_store_5d(&mapC, buf + (h << (g.seg_log2 + 7)), co0,
+                               tap - a * g.dec_kw, w0, a, rr);
+                } else {
+                  const int n = rr / g.OH;
+                  tma_store_4d(&mapC, buf + (h << (g.seg_log2 + 7)), n_base + c,
+                               w0, rr - n * g.OH, n);
+                }
               }
             } else {
-              tma_store_2d(&mapC, buf, n_base + c, mb * kBM + q * 32);
+              tma_store_2d(&mapC, buf, n_base + c, mb * BM + mh * kBM + q * 32);
             }
             bulk_commit();
           }
           epi_buf ^= 1;
         }
-      } else if (EPI == kEpiStore) {
+      } else if constexpr (EPI == kEpiStore) {
         const GemmEpilogue &e = g.epi;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 16) {
@@ -401,61 +444,68 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
             }
           }
         }
-      } else {
+      } else if constexpr (EPI == kEpiVocab) {
         // Vocabulary tile: fp32 logits = acc + bias, reduced to
         // (max, lowest argmax, sum exp(l - max)) without leaving registers.
         // Four warps share each TMEM lane quarter, each reducing 64 of the
-        // tile's 256 columns with 4 independent accumulator lanes (breaks the
-        // compare/add dependency chains). Parts 1..3 hand their result to
-        // part 0 through shared memory (double-buffered by tile parity) and
-        // the per-parity hand-off mbarrier; part 0 merges in column order and
-        // writes the tile's partial.
+        // tile's 256 columns: the 64 accumulators are read from TMEM once
+        // (four loads, one wait, the bias loads in between), then a max pass
+        // and an exp pass run on registers with 4 independent accumulator
+        // lanes (breaks the compare/add dependency chains). Parts 1..3 hand
+        // their result to part 0 through shared memory (double-buffered by
+        // tile parity) and the per-parity hand-off mbarrier; part 0 merges
+        // in column order and writes the tile's partial.
         constexpr int PART = BN / 4;
-        const int c_lo = hf * PART;
+        static_assert(PART == 64, "vocabulary parts are 64 columns");
+        const int n_lo = n_base + hf * PART;
+        const int valid = min(PART, g.N - n_lo); // columns of this part < N
+        uint32_t r[PART];
+        tmem_ld16(taddr + hf * PART, *reinterpret_cast<uint32_t(*)[16]>(r));
+        tmem_ld16(taddr + hf * PART + 16, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
+        tmem_ld16(taddr + hf * PART + 32, *reinterpret_cast<uint32_t(*)[16]>(r + 32));
+        tmem_ld16(taddr + hf * PART + 48, *reinterpret_cast<uint32_t(*)[16]>(r + 48));
         const bool vec_bias =
-            (reinterpret_cast<uintptr_t>(g.epi.bias) & 15) == 0;
-        // Bias for columns [n0, n0+16): two 16-byte loads when aligned and
-        // in range (L1-resident across the warp), guarded scalars otherwise.
-        auto load_bias = [&](int n0, float (&bf)[16]) {
-          if (vec_bias && n0 + 16 <= g.N) {
-            const uint4 b0 = __ldg(reinterpret_cast<const uint4 *>(g.epi.bias + n0));
-            const uint4 b1 = __ldg(reinterpret_cast<const uint4 *>(g.epi.bias + n0 + 8));
-            const half2 *h0 = reinterpret_cast<const half2 *>(&b0);
-            const half2 *h1 = reinterpret_cast<const half2 *>(&b1);
+            valid == PART && (reinterpret_cast<uintptr_t>(g.epi.bias) & 15) == 0;
+        tmem_ld_wait();
+        // Logits = accumulators + bias (L1-resident, 16-byte loads), 8
+        // columns at a time.
+        float lg[PART];
+        if (vec_bias) {
+#pragma unroll
+          for (int j8 = 0; j8 < PART / 8; ++j8) {
+            const uint4 bb = __ldg(reinterpret_cast<const uint4 *>(g.epi.bias + n_lo + 8 * j8));
+            const uint32_t bw[4] = {bb.x, bb.y, bb.z, bb.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const float2 f0 = __half22float2(h0[j]), f1 = __half22float2(h1[j]);
-              bf[2 * j] = f0.x;
-              bf[2 * j + 1] = f0.y;
-              bf[8 + 2 * j] = f1.x;
-              bf[8 + 2 * j + 1] = f1.y;
+              float lo = __uint_as_float(r[8 * j8 + 2 * j]);
+              float hi = __uint_as_float(r[8 * j8 + 2 * j + 1]);
+              add2_h(lo, hi, bw[j]); // + fp16 bias, one instruction each
+              lg[8 * j8 + 2 * j] = lo;
+              lg[8 * j8 + 2 * j + 1] = hi;
             }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              bf[j] = n0 + j < g.N ? __half2float(g.epi.bias[n0 + j]) : 0.f;
           }
-        };
+        } else {
+#pragma unroll
+          for (int j = 0; j < PART; ++j)
+            lg[j] = j < valid ? __uint_as_float(r[j]) + __half2float(g.epi.bias[n_lo + j])
+                              : -FLT_MAX;
+        }
         float bm[4] = {-FLT_MAX, -FLT_MAX, -FLT_MAX, -FLT_MAX};
         int bi[4] = {INT_MAX, INT_MAX, INT_MAX, INT_MAX};
-#pragma unroll 1
-        for (int c = c_lo; c < c_lo + PART; c += 16) {
-          const int n0 = n_base + c;
-          uint32_t r[16];
-          float bf[16];
-          tmem_ld16(taddr + c, r);
-          load_bias(n0, bf);
-          tmem_ld_wait();
-          const bool full_chunk = n0 + 16 <= g.N;
+        // Whole parts (all but the vocabulary's last tile) skip the
+        // per-column range test.
+        auto max_pass = [&](auto whole) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float l = __uint_as_float(r[j]) + bf[j];
-            if ((full_chunk || n0 + j < g.N) && l > bm[j & 3]) {
-              bm[j & 3] = l;
-              bi[j & 3] = n0 + j;
+          for (int j = 0; j < PART; ++j)
+            if ((decltype(whole)::value || j < valid) && lg[j] > bm[j & 3]) {
+              bm[j & 3] = lg[j];
+              bi[j & 3] = n_lo + j;
             }
-          }
-        }
+        };
+        if (valid == PART)
+          max_pass(std::true_type{});
+        else
+          max_pass(std::false_type{});
         float best = bm[0];
         int best_id = bi[0];
 #pragma unroll
@@ -465,22 +515,20 @@ __global__ void __launch_bounds__(threads_for<EPI>(), 1)
             best_id = bi[k];
           }
         float sum = 0.f;
-        if (g.calc_prob) {
+        if (g.calc_prob && valid > 0) {
+          // exp(l - best) = 2^(l*log2e - best*log2e)
+          const float bL = best * kLog2e;
           float sp[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-          for (int c = c_lo; c < c_lo + PART; c += 16) {
-            const int n0 = n_base + c;
-            uint32_t r[16];
-            float bf[16];
-            tmem_ld16(taddr + c, r);
-            load_bias(n0, bf);
-            tmem_ld_wait();
-            const bool full_chunk = n0 + 16 <= g.N;
+          auto exp_pass = [&](auto whole) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              if (full_chunk || n0 + j < g.N)
-                sp[j & 3] += __expf(__uint_as_float(r[j]) + bf[j] - best);
-          }
+            for (int j = 0; j < PART; ++j)
+              if (decltype(whole)::value || j < valid)
+                sp[j & 3] += ex2_ftz(fmaf(lg[j], kLog2e, -bL));
+          };
+          if (valid == PART)
+            exp_pass(std::true_type{});
+          else
+            exp_pass(std::false_type{});
           sum = (sp[0] + sp[1]) + (sp[2] + sp[3]);
         }
         // Hand-off buffer: [parity][quarter][part 1..3][max | id | sum][lane].
@@ -576,12 +624,12 @@ bool encode(CUtensorMap *m, const void *base, int rank, const cuuint64_t *dims,
   return r == CUDA_SUCCESS;
 }
 
-template <int BN, bool CONV, int EPI, int ACT>
+template <int BN, bool CONV, int EPI, int ACT, int MH = 1>
 cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &c,
                    const Args &g,
                    cudaStream_t stream) {
-  using C = Cfg<BN>;
-  auto kernel = tc_gemm_kernel<BN, CONV, EPI, ACT>;
+  using C = Cfg<BN, MH>;
+  auto kernel = tc_gemm_kernel<BN, CONV, EPI, ACT, MH>;
   static std::once_flag once[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -595,7 +643,7 @@ cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap
     return attr;
   const int total = g.mt * g.nt;
   const int grid = total < sm_count() ? total : sm_count();
-  kernel<<<grid, threads_for<EPI>(), C::SMEM, stream>>>(a, b, c, g);
+  kernel<<<grid, threads_for<EPI, MH>(), C::SMEM, stream>>>(a, b, c, g);
   return cudaGetLastError();
 }
 
@@ -618,26 +666,34 @@ int pick_bn(int N) {
 
 // Activations used by the generated graphs get their own instantiation; the
 // rest share one with a runtime switch.
-template <int BN, bool CONV, int EPI>
+template <int BN, bool CONV, int EPI, int MH = 1>
 cudaError_t dispatch_act(const CUtensorMap &a, const CUtensorMap &b,
                          const CUtensorMap &c, const Args &g, cudaStream_t s) {
   switch (g.epi.act) {
   case kActNone:
-    return launch<BN, CONV, EPI, kActNone>(a, b, c, g, s);
+    return launch<BN, CONV, EPI, kActNone, MH>(a, b, c, g, s);
   case kActRelu:
-    return launch<BN, CONV, EPI, kActRelu>(a, b, c, g, s);
+    return launch<BN, CONV, EPI, kActRelu, MH>(a, b, c, g, s);
   case kActHardSwish:
-    return launch<BN, CONV, EPI, kActHardSwish>(a, b, c, g, s);
+    return launch<BN, CONV, EPI, kActHardSwish, MH>(a, b, c, g, s);
   case kActSwish:
-    return launch<BN, CONV, EPI, kActSwish>(a, b, c, g, s);
+    return launch<BN, CONV, EPI, kActSwish, MH>(a, b, c, g, s);
   default:
-    return launch<BN, CONV, EPI, -1>(a, b, c, g, s);
+    return launch<BN, CONV, EPI, -1, MH>(a, b, c, g, s);
   }
 }
 
+// 256-row tiles pay off when the K loop is long (the single-buffered
+// accumulator leaves the epilogue exposed once per tile) and there are
+// still at least four 256-row tiles per SM (wave quantisation).
+bool use_two_halves(int bn, int num_kb, long long M, int nt) {
+  return bn == 256 && num_kb >= 32 &&
+         (M + 2 * kBM - 1) / (2 * kBM) * nt >= 4LL * sm_count();
+}
+
 template <bool CONV, int EPI>
-cudaError_t dispatch_bn(int bn, const CUtensorMap &a, const CUtensorMap &b,
-                        const CUtensorMap &c,
+cudaError_t dispatch_bn(int bn, bool two_halves, const CUtensorMap &a,
+                        const CUtensorMap &b, const CUtensorMap &c,
                         const Args &g, cudaStream_t s) {
   switch (bn) {
   case 48:
@@ -647,7 +703,8 @@ cudaError_t dispatch_bn(int bn, const CUtensorMap &a, const CUtensorMap &b,
   case 128:
     return dispatch_act<128, CONV, EPI>(a, b, c, g, s);
   default:
-    return dispatch_act<256, CONV, EPI>(a, b, c, g, s);
+    return two_halves ? dispatch_act<256, CONV, EPI, 2>(a, b, c, g, s)
+                      : dispatch_act<256, CONV, EPI>(a, b, c, g, s);
   }
 }
 
@@ -658,6 +715,20 @@ bool aligned16(const void *p) {
 } // namespace
 
 int vocab_tiles(int V) { return (V + 255) / 256; }
+
+bool encode_fp16_map(CUtensorMap *m, const void *base, int rank,
+                     const cuuint64_t *dims, const cuuint64_t *strides,
+                     const cuuint32_t *box, bool swizzle128) {
+  EncodeTiled fn = encoder();
+  if (!fn)
+    return false;
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void *>(base),
+            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 cudaError_t tc_gemm(const half *A, int M, int K, int lda, const half *W, int N,
                     int ldw, const GemmEpilogue &epi, cudaStream_t stream) {
@@ -690,13 +761,15 @@ cudaError_t tc_gemm(const half *A, int M, int K, int lda, const half *W, int N,
   g.num_kb = (K + kBK - 1) / kBK;
   g.kb_per_tap = g.num_kb;
   g.KW = 1;
-  g.mt = (M + kBM - 1) / kBM;
+  const bool two = use_two_halves(bn, g.num_kb, M, (N + bn - 1) / bn);
+  const int bm = two ? 2 * kBM : kBM;
+  g.mt = (M + bm - 1) / bm;
   g.nt = (N + bn - 1) / bn;
   g.Wseg = g.OH = g.OW = g.batch = 1;
   g.seg_log2 = 4;
   g.epi = epi;
   g.err = device_error_word();
-  return dispatch_bn<false, kEpiStore>(bn, ma, mb, mc, g, stream);
+  return dispatch_bn<false, kEpiStore>(bn, two, ma, mb, mc, g, stream);
 }
 
 cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
@@ -755,11 +828,81 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   g.KW = s.KW;
   g.pad_h = s.pad_h;
   g.pad_w = s.pad_w;
-  g.mt = (g.M + kBM - 1) / kBM;
+  const bool two = use_two_halves(bn, g.num_kb, g.M, (s.Co + bn - 1) / bn);
+  const int bm = two ? 2 * kBM : kBM;
+  g.mt = (g.M + bm - 1) / bm;
   g.nt = (s.Co + bn - 1) / bn;
   g.epi = epi;
   g.err = device_error_word();
-  return dispatch_bn<true, kEpiStore>(bn, ma, mb, mc, g, stream);
+  return dispatch_bn<true, kEpiStore>(bn, two, ma, mb, mc, g, stream);
+}
+
+cudaError_t tc_deconv(const half *x, const half *wpacked, const half *bias_rep,
+                      half *y, int batch, int H, int W, int Ci, int Co, int KH,
+                      int KW, int act, cudaStream_t stream) {
+  if (batch <= 0 || H <= 0 || W <= 0)
+    return cudaSuccess;
+  const int N = KH * KW * Co;
+  if (Co % 64 || Ci % 8 || !aligned16(x) || !aligned16(wpacked) ||
+      !aligned16(y) || (bias_rep && !aligned16(bias_rep)))
+    return cudaErrorInvalidValue;
+  // N is a multiple of 64, so the tile (256, 128 or 64 columns) and each
+  // 64-column store chunk cover whole taps' channel blocks.
+  const int bn = pick_bn(N);
+  const int seg_log2 = W % 32 == 0 ? 5 : 4;
+  const cuuint32_t seg = 1u << seg_log2;
+  CUtensorMap ma, mb, mc;
+  cuuint64_t da[4] = {static_cast<cuuint64_t>(Ci), static_cast<cuuint64_t>(W),
+                      static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(batch)};
+  cuuint64_t sa[3] = {static_cast<cuuint64_t>(Ci) * 2, static_cast<cuuint64_t>(W) * Ci * 2,
+                      static_cast<cuuint64_t>(H) * W * Ci * 2};
+  cuuint32_t ba[4] = {kBK, seg, 1, 1};
+  cuuint64_t db[3] = {static_cast<cuuint64_t>(Ci), 1, static_cast<cuuint64_t>(N)};
+  cuuint64_t sb[2] = {static_cast<cuuint64_t>(Ci) * 2, static_cast<cuuint64_t>(Ci) * 2};
+  cuuint32_t bb[3] = {kBK, 1, static_cast<cuuint32_t>(bn)};
+  // Output y [batch][H*KH][W*KW][Co] seen as (co, b, w, a, n*H + h).
+  const cuuint64_t ow = static_cast<cuuint64_t>(W) * KW;
+  cuuint64_t dc[5] = {static_cast<cuuint64_t>(Co), static_cast<cuuint64_t>(KW),
+                      static_cast<cuuint64_t>(W), static_cast<cuuint64_t>(KH),
+                      static_cast<cuuint64_t>(batch) * H};
+  cuuint64_t scs[4] = {static_cast<cuuint64_t>(Co) * 2,
+                       static_cast<cuuint64_t>(KW) * Co * 2, ow * Co * 2,
+                       static_cast<cuuint64_t>(KH) * ow * Co * 2};
+  cuuint32_t bc[5] = {64, 1, seg, 1, 1};
+  if (!encode(&ma, x, 4, da, sa, ba) || !encode(&mb, wpacked, 3, db, sb, bb) ||
+      !encode(&mc, y, 5, dc, scs, bc))
+    return cudaErrorInvalidValue;
+  Args g{};
+  g.seg_log2 = seg_log2;
+  g.Wseg = (W + static_cast<int>(seg) - 1) / static_cast<int>(seg);
+  g.OH = H;
+  g.OW = W;
+  g.batch = batch;
+  g.M = batch * H * g.Wseg * static_cast<int>(seg);
+  g.N = N;
+  g.kb_per_tap = (Ci + kBK - 1) / kBK;
+  g.num_kb = g.kb_per_tap;
+  g.KW = 1;
+  g.mt = (g.M + kBM - 1) / kBM;
+  g.nt = (N + bn - 1) / bn;
+  g.epi.bias = bias_rep;
+  g.epi.out = y;
+  g.epi.ldo = Co;
+  g.epi.act = act;
+  g.dec_co = Co;
+  g.dec_kw = KW;
+  g.err = device_error_word();
+  switch (bn) {
+  case 64:
+    return act == kActRelu ? launch<64, true, kEpiDeconv, kActRelu>(ma, mb, mc, g, stream)
+                           : launch<64, true, kEpiDeconv, -1>(ma, mb, mc, g, stream);
+  case 128:
+    return act == kActRelu ? launch<128, true, kEpiDeconv, kActRelu>(ma, mb, mc, g, stream)
+                           : launch<128, true, kEpiDeconv, -1>(ma, mb, mc, g, stream);
+  default:
+    return act == kActRelu ? launch<256, true, kEpiDeconv, kActRelu>(ma, mb, mc, g, stream)
+                           : launch<256, true, kEpiDeconv, -1>(ma, mb, mc, g, stream);
+  }
 }
 
 cudaError_t tc_vocab_partials(const half *hidden, int rows, int H,

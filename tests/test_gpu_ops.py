@@ -35,6 +35,9 @@ GEMM_CASES = [
     (77, 120, 240, True, False, 5),     # swish
     (300, 64, 128, True, False, 3),     # hardswish
     (1, 128, 64, False, False, 0),      # single row, no bias
+    # 256-row tiles (K >= 32 k-blocks, >= 4 tiles per SM), partial last tile
+    (40000, 2048, 1024, True, False, 1),
+    (37900, 2048, 1024, True, True, 0),
 ]
 
 
@@ -68,6 +71,9 @@ CONV_CASES = [
     (1, 12, 80, 48, 128, 3),
     (1, 7, 9, 64, 64, 5),       # 5x5, tiny image
     (3, 3, 80, 512, 256, 3),
+    # 256-row tiles: 16-pixel segments (OW 80) and 32-pixel ones (OW 160)
+    (316, 3, 80, 512, 512, 3),
+    (160, 3, 160, 512, 512, 3),
 ]
 
 
@@ -207,18 +213,30 @@ def test_resize_add_and_concat(native, cuda):
     assert torch.equal(host(c), want)
 
 
-@pytest.mark.parametrize("co,act", [(64, 1), (1, 4)])
-def test_deconv(native, cuda, co, act):
-    r = rng(16 + co)
-    x = f16(r.uniform(-1, 1, (2, 16, 16, 64)))
-    w = f16(r.standard_normal((64, 2, 2, co)) * np.sqrt(2.0 / 256))
-    b = f16(r.normal(0, 0.1, co))
-    y = torch.empty(2, 32, 32, co, dtype=torch.float16, device=cuda)
-    dx, dw, db = dev(x), dev(w), dev(b)
-    assert native.ppocr_b200_deconv_nhwc(ptr(dx), ptr(dw), ptr(db), ptr(y), 2, 16, 16, 64, co, 2, 2, act,
-                                         stream_handle()) == 0
+DECONV_CASES = [
+    # batch, h, w, ci, co, act, bias
+    (2, 16, 16, 64, 64, 1, True),     # tensor-core path (Co % 64 == 0)
+    (2, 16, 16, 64, 1, 4, True),      # one output channel: SIMT path, sigmoid
+    (1, 7, 30, 64, 128, 0, True),     # tensor cores, ragged 16-pixel segments
+    (2, 12, 64, 64, 64, 1, False),    # tensor cores, 32-pixel segments, no bias
+    (1, 9, 11, 24, 3, 0, True),       # 12 outputs per pixel, Ci not a multiple of 8
+]
+
+
+@pytest.mark.parametrize("batch,h,w,ci,co,act,bias", DECONV_CASES)
+def test_deconv(native, cuda, batch, h, w, ci, co, act, bias):
+    r = rng(16 + co + h)
+    x = f16(r.uniform(-1, 1, (batch, h, w, ci)))
+    wt = f16(r.standard_normal((ci, 2, 2, co)) * np.sqrt(2.0 / (4 * ci)))
+    b = f16(r.normal(0, 0.1, co)) if bias else None
+    y = torch.empty(batch, 2 * h, 2 * w, co, dtype=torch.float16, device=cuda)
+    dx, dw = dev(x), dev(wt)
+    db = dev(b) if bias else None
+    assert native.ppocr_b200_deconv_nhwc(ptr(dx), ptr(dw), ptr(db) if bias else None, ptr(y), batch, h, w, ci,
+                                         co, 2, 2, act, stream_handle()) == 0, native.ppocr_b200_last_error()
     sync()
-    assert_close(host(y), L.deconv_kxk(x, w, b, act), what="deconv")
+    check_device_error(native)
+    assert_close(host(y), L.deconv_kxk(x, wt, b, act), what=f"deconv {batch}x{h}x{w}x{ci}->{co}")
 
 
 def test_binarize_bit_exact(native, cuda):
@@ -271,6 +289,36 @@ def test_logits_argmax_and_collapse(native, cuda, oracle_c):
     assert np.array_equal(oid.cpu().numpy(), c_ids)
     assert np.array_equal(olen.cpu().numpy(), c_len)
     assert np.abs(osc.cpu().numpy() - c_sc).max() <= 1e-5
+
+
+@pytest.mark.parametrize("rows,V,offset", [(3, 5, 0), (7, 1, 0), (64, 300, 0), (64, 300, 1),
+                                           (40, 18385, 1), (33, 4099, 0)])
+def test_logits_argmax_shapes(native, cuda, oracle_c, rows, V, offset):
+    """Row staging edge cases: rows shorter than one 16-byte vector, odd
+    vocabularies (rows start at any 2-byte offset), a base pointer that is
+    not 16-byte aligned (register path), ties (repeated maxima)."""
+    r = rng(30 + V + offset)
+    logits = r.standard_normal((rows, V)).astype(np.float16)
+    logits[::3, V // 2] = 8.0
+    logits[::3, V - 1] = 8.0  # tie: the lower id must win
+    buf = torch.zeros(rows * V + offset, dtype=torch.float16, device=cuda)
+    d = buf[offset:]
+    d.copy_(torch.from_numpy(logits.reshape(-1)))
+    ids = torch.empty(rows, dtype=torch.int32, device=cuda)
+    prob = torch.empty(rows, dtype=torch.float32, device=cuda)
+    mx = torch.empty(rows, dtype=torch.float32, device=cuda)
+    assert native.ppocr_b200_logits_argmax_prob(ptr(d), rows, V, ptr(ids), ptr(prob), ptr(mx), 1,
+                                                stream_handle()) == 0
+    sync()
+    check_device_error(native)
+    want_ids = np.empty(rows, np.int32)
+    want_prob = np.empty(rows, np.float32)
+    want_max = np.empty(rows, np.float32)
+    oracle_c.oracle_argmax_prob(logits.ctypes.data, rows, V, want_ids.ctypes.data, want_prob.ctypes.data,
+                                want_max.ctypes.data, 4)
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
+    assert np.array_equal(mx.cpu().numpy(), want_max)
+    assert np.abs(prob.cpu().numpy() - want_prob).max() <= 1e-5
 
 
 def test_collapse_bit_exact_on_device_inputs(native, cuda, oracle_c):
