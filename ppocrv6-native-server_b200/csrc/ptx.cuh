@@ -70,7 +70,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
 
 // ---------------------------------------------------------------- TMA loads
 // Tiled bulk-tensor loads into this CTA's shared memory, completing on an
-// mbarrier (complete_tx). No multicast variant exists in this code base.
+// mbarrier (complete_tx). Every load targets this CTA's own shared memory.
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map,
                                             uint64_t *bar, int c0, int c1) {
   asm volatile(

@@ -26,6 +26,7 @@ extension for the SVTR mixing block.
 from __future__ import annotations
 
 import json
+import os
 import math
 from dataclasses import dataclass, field
 from pathlib import Path
@@ -202,8 +203,10 @@ class Graph:
 
 
 def write_weights(path: Path, consts) -> None:
+    """Writes atomically: several processes (one per GPU) may generate the
+    same deterministic file at once; each renames its own temporary."""
     path.parent.mkdir(parents=True, exist_ok=True)
-    tmp = path.with_suffix(".tmp")
+    tmp = path.with_suffix(f".tmp{os.getpid()}")
     with tmp.open("wb") as f:
         for pad, v in consts:
             if pad:
