@@ -331,6 +331,10 @@ def b200_arm(args):
     digest = tokens_digest(*rec.results(LINES))
     identical = all_equal_over_ranks(digest)
 
+    # ---- the CTC head alone (vocabulary projection + merge + collapse)
+    head_ms = _event_steps(stream, 10, lambda i: rec.enqueue_head(LINES), flush)
+    head_ms = min(head_ms)
+
     # ---- roofline of the dominant kernel (stage-4 3x3 implicit GEMM)
     prof = [rec.model.lib.profile(rec.model.handle) for _ in range(3)]
     per_op = [min(p[i] for p in prof) for i in range(len(op_names))]
@@ -377,6 +381,7 @@ def b200_arm(args):
             "gpu_launches": gpu_launches,
             "clocks": clocks.summary(),
             "replica_tokens": {"sha256": digest[:16], "identical_across_ranks": identical},
+            "head_ms": round(head_ms, 4),
             "ops_ms": {f"{op_names[i]}#{i}": round(per_op[i], 4)
                        for i in sorted(range(len(per_op)), key=lambda i: -per_op[i])[:16]},
         }

@@ -64,6 +64,11 @@ struct Args {
   int mt, nt;          // tile grid
   int Wseg, OH, OW, batch; // conv geometry (Wseg = pixel segments per row)
   int seg_log2;            // conv: log2 of the segment length (16 or 32)
+  // Row mode (conv, 256-row tiles, OW a multiple of 16 and <= 128): a tile
+  // is row_segs whole output rows of OW pixels, each loaded as one TMA box
+  // per k-block; tile rows past row_segs * OW compute unused values.
+  int row_segs;            // 0: pixel-segment mode
+
   GemmEpilogue epi;
   float *part_max;
   int *part_id;
@@ -217,17 +222,29 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
         // Implicit GEMM: the pixel segments of this M tile (BM/16 of 16
         // pixels or BM/32 of 32) are fixed for the whole K loop; only the
         // filter tap and channel block move.
-        const int nbox = BM >> g.seg_log2;
+        const int nbox = g.row_segs ? g.row_segs : BM >> g.seg_log2;
         const int seg0 = mb * nbox;
+        // A bytes per stage: whole rows of 128 bytes actually loaded.
+        const uint32_t a_bytes = g.row_segs ? static_cast<uint32_t>(g.row_segs * g.OW * 128)
+                                            : C::A_BYTES;
+        // smem row offset (log2 of bytes) between boxes in pixel-segment mode
+        const int box_shift = g.seg_log2 + 7;
         int seg_x[BM / 16], seg_y[BM / 16], seg_n[BM / 16];
         if (CONV) {
 #pragma unroll
           for (int s = 0; s < BM / 16; ++s) {
-            const int seg = seg0 + s;
-            const int r = seg / g.Wseg;
-            seg_x[s] = ((seg - r * g.Wseg) << g.seg_log2) - g.pad_w;
-            seg_n[s] = r / g.OH;
-            seg_y[s] = r - seg_n[s] * g.OH - g.pad_h;
+            if (g.row_segs) {
+              const int r = seg0 + s; // output row index n * OH + oh
+              seg_x[s] = -g.pad_w;
+              seg_n[s] = r / g.OH;
+              seg_y[s] = r - seg_n[s] * g.OH - g.pad_h;
+            } else {
+              const int seg = seg0 + s;
+              const int r = seg / g.Wseg;
+              seg_x[s] = ((seg - r * g.Wseg) << g.seg_log2) - g.pad_w;
+              seg_n[s] = r / g.OH;
+              seg_y[s] = r - seg_n[s] * g.OH - g.pad_h;
+            }
           }
         }
         int cb = 0, tap = 0, kh = 0, kw = 0;
@@ -239,15 +256,15 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
           }
           uint8_t *sa = smem + stage * C::STAGE_BYTES;
           uint8_t *sb = sa + C::A_BYTES;
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          mbar_arrive_expect_tx(&full[stage], a_bytes + C::B_BYTES);
           issued |= 1u << stage;
           issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
           if (CONV) {
 #pragma unroll
             for (int s = 0; s < BM / 16; ++s)
               if (s < nbox)
-                tma_load_4d(sa + (s << (g.seg_log2 + 7)), &mapA, &full[stage],
-                            cb * kBK, seg_x[s] + kw, seg_y[s] + kh, seg_n[s]);
+                tma_load_4d(sa + (g.row_segs ? s * g.OW * 128 : s << box_shift), &mapA,
+                            &full[stage], cb * kBK, seg_x[s] + kw, seg_y[s] + kh, seg_n[s]);
             tma_load_3d(sb, &mapB, &full[stage], cb * kBK, tap, nb * BN);
             if (++cb == g.kb_per_tap) {
               cb = 0;
@@ -351,7 +368,13 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
                              (acc + mh) * C::ACC_COLS;
       // Map this thread's accumulator row to an output row.
       long long orow = -1;
-      if (CONV) {
+      if (CONV && g.row_segs) {
+        const int sidx = row_in_tile / g.OW;
+        const int r = mb * g.row_segs + sidx;
+        const int n = r / g.OH;
+        if (sidx < g.row_segs && n < g.batch)
+          orow = static_cast<long long>(r) * g.OW + (row_in_tile - sidx * g.OW);
+      } else if (CONV) {
         const int seg = mb * (BM >> g.seg_log2) + (row_in_tile >> g.seg_log2);
         const int r = seg / g.Wseg;
         const int owseg = seg - r * g.Wseg;
@@ -398,7 +421,19 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
-            if (CONV) {
+            if (CONV && g.row_segs) {
+              // Two 16-row pieces; OW is a multiple of 16, so a piece lies
+              // inside one output row.
+              for (int h = 0; h < 2; ++h) {
+                const int row0 = mh * kBM + q * 32 + h * 16;
+                const int sidx = row0 / g.OW;
+                const int r = mb * g.row_segs + sidx;
+                const int n = r / g.OH;
+                if (sidx < g.row_segs && n < g.batch)
+                  tma_store_4d(&mapC, buf + h * 2048, n_base + c, row0 - sidx * g.OW,
+                               r - n * g.OH, n);
+              }
+            } else if (CONV) {
               // This warp's 32 rows are 32 >> seg_log2 whole segments.
               for (int h = 0; h < (32 >> g.seg_log2); ++h) {
                 const int seg = mb * (BM >> g.seg_log2) +
@@ -789,6 +824,15 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   // boxes per stage), else 16.
   const int seg_log2 = OW % 32 == 0 ? 5 : 4;
   const cuuint32_t seg = 1u << seg_log2;
+  const int kb_tap = (s.Ci + kBK - 1) / kBK;
+  const long long m_seg = static_cast<long long>(s.batch) * OH *
+                          ((OW + static_cast<int>(seg) - 1) / static_cast<int>(seg)) * seg;
+  const bool two = use_two_halves(bn, kb_tap * taps, m_seg, (s.Co + bn - 1) / bn);
+  // Row mode for 256-row tiles: whole output rows per TMA box when at most
+  // one eighth of the tile is left unused.
+  int row_segs = 0;
+  if (two && OW % 16 == 0 && OW <= 128 && (2 * kBM / OW) * OW * 8 >= 7 * 2 * kBM)
+    row_segs = 2 * kBM / OW;
   CUtensorMap ma, mb;
   cuuint64_t da[4] = {static_cast<cuuint64_t>(s.Ci), static_cast<cuuint64_t>(s.W),
                       static_cast<cuuint64_t>(s.H),
@@ -796,7 +840,7 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   cuuint64_t sa[3] = {static_cast<cuuint64_t>(s.Ci) * 2,
                       static_cast<cuuint64_t>(s.W) * s.Ci * 2,
                       static_cast<cuuint64_t>(s.H) * s.W * s.Ci * 2};
-  cuuint32_t ba[4] = {kBK, seg, 1, 1};
+  cuuint32_t ba[4] = {kBK, row_segs ? static_cast<cuuint32_t>(OW) : seg, 1, 1};
   cuuint64_t db[3] = {static_cast<cuuint64_t>(s.Ci), static_cast<cuuint64_t>(taps),
                       static_cast<cuuint64_t>(s.Co)};
   cuuint64_t sb[2] = {static_cast<cuuint64_t>(s.Ci) * 2,
@@ -811,12 +855,13 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   cuuint64_t sc[3] = {static_cast<cuuint64_t>(epi.ldo) * 2,
                       static_cast<cuuint64_t>(OW) * epi.ldo * 2,
                       static_cast<cuuint64_t>(OH) * OW * epi.ldo * 2};
-  cuuint32_t bc[4] = {64, seg, 1, 1};
+  cuuint32_t bc[4] = {64, row_segs ? 16u : seg, 1, 1};
   if (!encode(&ma, x, 4, da, sa, ba) || !encode(&mb, w, 3, db, sb, bb) ||
       !encode(&mc, epi.out, 4, dc, sc, bc))
     return cudaErrorInvalidValue;
   Args g{};
   g.seg_log2 = seg_log2;
+  g.row_segs = row_segs;
   g.Wseg = (OW + static_cast<int>(seg) - 1) / static_cast<int>(seg);
   g.OH = OH;
   g.OW = OW;
@@ -828,9 +873,8 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   g.KW = s.KW;
   g.pad_h = s.pad_h;
   g.pad_w = s.pad_w;
-  const bool two = use_two_halves(bn, g.num_kb, g.M, (s.Co + bn - 1) / bn);
   const int bm = two ? 2 * kBM : kBM;
-  g.mt = (g.M + bm - 1) / bm;
+  g.mt = row_segs ? (s.batch * OH + row_segs - 1) / row_segs : (g.M + bm - 1) / bm;
   g.nt = (s.Co + bn - 1) / bn;
   g.epi = epi;
   g.err = device_error_word();

@@ -111,14 +111,19 @@ class LineRecognizer:
 
     def enqueue(self, x_nhwc: torch.Tensor) -> None:
         """Full forward of an FP16 NHWC batch on self.stream (asynchronous)."""
-        s = ctypes.c_void_p(self.stream.cuda_stream)
         self.model.enqueue_nhwc(x_nhwc, self.hidden, self.stream)
-        rows = x_nhwc.shape[0] * self.T
+        self.enqueue_head(x_nhwc.shape[0])
+
+    def enqueue_head(self, n: int) -> None:
+        """Vocabulary projection + argmax/softmax-max + collapse of the first
+        n lines of self.hidden (asynchronous, on self.stream)."""
+        s = ctypes.c_void_p(self.stream.cuda_stream)
+        rows = n * self.T
         capi.check(self.lib.ppocr_b200_classifier_run_packed(
             _p(self.hidden), _p(self.head.packed), _p(self.head.bias), _p(self.ids), _p(self.prob), _p(self.maxl),
             rows, self.H, self.vocab, _p(self.part_id), _p(self.part_max), _p(self.part_sum), 1, s))
         capi.check(self.lib.ppocr_b200_ctc_collapse(
-            _p(self.ids), _p(self.prob), x_nhwc.shape[0], self.T, self.blank, _p(self.out_ids), _p(self.out_len),
+            _p(self.ids), _p(self.prob), n, self.T, self.blank, _p(self.out_ids), _p(self.out_len),
             _p(self.out_score), s))
 
     def results(self, n: int):

@@ -71,8 +71,10 @@ CONV_CASES = [
     (1, 12, 80, 48, 128, 3),
     (1, 7, 9, 64, 64, 5),       # 5x5, tiny image
     (3, 3, 80, 512, 256, 3),
-    # 256-row tiles: 16-pixel segments (OW 80) and 32-pixel ones (OW 160)
+    # 256-row tiles: whole-row boxes (OW 80: 3 rows per tile; OW 64: 4 rows,
+    # partial last tile) and 32-pixel segments (OW 160)
     (316, 3, 80, 512, 512, 3),
+    (301, 5, 64, 512, 512, 3),
     (160, 3, 160, 512, 512, 3),
 ]
 
