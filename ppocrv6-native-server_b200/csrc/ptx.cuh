@@ -317,6 +317,16 @@ __device__ __forceinline__ void add2_h(float &lo, float &hi, uint32_t x) {
       : "+f"(lo), "+f"(hi)
       : "r"(x));
 }
+// Packed fp32 pair FMA (PTX ISA 8.6, sm_100): acc.{x,y} = a.{x,y} * b.{x,y}
+// + acc.{x,y}, each lane rounded once (the same bits as two fmaf calls).
+__device__ __forceinline__ void ffma2(float2 &acc, float2 a, float2 b) {
+  uint64_t d = (static_cast<uint64_t>(__float_as_uint(acc.y)) << 32) | __float_as_uint(acc.x);
+  const uint64_t x = (static_cast<uint64_t>(__float_as_uint(a.y)) << 32) | __float_as_uint(a.x);
+  const uint64_t y = (static_cast<uint64_t>(__float_as_uint(b.y)) << 32) | __float_as_uint(b.x);
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(d) : "l"(x), "l"(y));
+  acc.x = __uint_as_float(static_cast<uint32_t>(d));
+  acc.y = __uint_as_float(static_cast<uint32_t>(d >> 32));
+}
 // 2^x on the special-function unit (approximate, subnormal results flushed).
 // exp(v - m) is computed as ex2(v * log2(e) - m * log2(e)).
 __device__ __forceinline__ float ex2_ftz(float x) {

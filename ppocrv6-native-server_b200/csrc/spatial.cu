@@ -201,7 +201,8 @@ __global__ void __launch_bounds__(kBlock)
 // (zero-filled outside the image: the padding), the filter slice is staged
 // tap-major beside it, and each thread computes PIX columns x 8 channels
 // from shared memory with the same tap order and one mixed-precision FMA
-// per multiply-add as depthwise_kernel (bit-identical results).
+// per multiply-add as depthwise_kernel (bit-identical results). (Packed
+// fp32-pair FMAs on converted strips measured slower on B200.)
 template <int KH, int KW, int SH, int SW, int PIX, int ACT>
 __global__ void __launch_bounds__(256)
     depthwise_tma_kernel(const __grid_constant__ CUtensorMap xmap,
@@ -526,6 +527,93 @@ __global__ void __launch_bounds__(kBlock)
     }
     *reinterpret_cast<uint4 *>(dst + g * 8) = o.u;
   }
+}
+
+// Two horizontally adjacent output pixels per thread for small Ci (the
+// stem): each filter tap's CO fp32 weights are read from shared memory once
+// (broadcast) for both pixels, and the multiply-adds run as packed fp32
+// pairs over output channels. Sum order per output is (kh, kw, ci) as in
+// stem_conv_kernel, so results are bit-identical to it.
+template <int CO, int ACT>
+__global__ void __launch_bounds__(kBlock)
+    stem_conv2_kernel(const half *__restrict__ x, const half *__restrict__ w,
+                      const half *__restrict__ bias, half *__restrict__ y,
+                      int Ci, int H, int W, int OH, int OW, int KH, int KW,
+                      int SH, int SW, int PH, int PW, int act, uint32_t items,
+                      FastDiv by_pairs, FastDiv by_oh) {
+  extern __shared__ float wsm[];
+  const int taps = KH * KW * Ci;
+  for (int j = threadIdx.x; j < taps * CO; j += blockDim.x) {
+    const int co = j / taps, k = j - co * taps; // w is [co][kh][kw][ci]
+    wsm[k * CO + co] = __half2float(w[j]);
+  }
+  __syncthreads();
+  const uint32_t it = blockIdx.x * blockDim.x + threadIdx.x;
+  if (it >= items)
+    return;
+  const uint32_t r0 = by_pairs.div(it);
+  const int ow = static_cast<int>(it - r0 * by_pairs.d) * 2;
+  const uint32_t n0 = by_oh.div(r0);
+  const int oh = static_cast<int>(r0 - n0 * by_oh.d);
+  const long long n = n0;
+  const bool two = ow + 1 < OW;
+  float2 acc0[CO / 2], acc1[CO / 2];
+#pragma unroll
+  for (int c = 0; c < CO / 2; ++c)
+    acc0[c] = acc1[c] = make_float2(0.f, 0.f);
+  for (int a = 0; a < KH; ++a) {
+    const int r = oh * SH - PH + a;
+    if (r < 0 || r >= H)
+      continue;
+    for (int b = 0; b < KW; ++b) {
+      const int c0 = ow * SW - PW + b, c1 = c0 + SW;
+      const bool in0 = c0 >= 0 && c0 < W, in1 = two && c1 >= 0 && c1 < W;
+      if (!in0 && !in1)
+        continue;
+      const half *p0 = x + ((n * H + r) * W + c0) * Ci;
+      const half *p1 = p0 + static_cast<long long>(SW) * Ci;
+      const float4 *wt = reinterpret_cast<const float4 *>(wsm + (a * KW + b) * Ci * CO);
+      for (int ci = 0; ci < Ci; ++ci) {
+        const float x0 = in0 ? __half2float(p0[ci]) : 0.f;
+        const float x1 = in1 ? __half2float(p1[ci]) : 0.f;
+        const float2 xx0 = make_float2(x0, x0), xx1 = make_float2(x1, x1);
+#pragma unroll
+        for (int q = 0; q < CO / 4; ++q) {
+          const float4 wv = wt[ci * (CO / 4) + q];
+          const float2 wlo = make_float2(wv.x, wv.y), whi = make_float2(wv.z, wv.w);
+          if (in0) {
+            ffma2(acc0[2 * q], xx0, wlo);
+            ffma2(acc0[2 * q + 1], xx0, whi);
+          }
+          if (in1) {
+            ffma2(acc1[2 * q], xx1, wlo);
+            ffma2(acc1[2 * q + 1], xx1, whi);
+          }
+        }
+      }
+    }
+  }
+  auto store = [&](const float2 (&acc)[CO / 2], int col) {
+    half *dst = y + ((n * OH + oh) * OW + col) * CO;
+#pragma unroll
+    for (int g = 0; g < CO / 8; ++g) {
+      Pack8 o;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c0 = g * 8 + 2 * j;
+        float v0 = round_half(acc[c0 / 2].x), v1 = round_half(acc[c0 / 2].y);
+        if (bias) {
+          v0 += __half2float(bias[c0]);
+          v1 += __half2float(bias[c0 + 1]);
+        }
+        o.h[j] = __floats2half2_rn(act_t<ACT>(v0, act), act_t<ACT>(v1, act));
+      }
+      *reinterpret_cast<uint4 *>(dst + g * 8) = o.u;
+    }
+  };
+  store(acc0, ow);
+  if (two)
+    store(acc1, ow + 1);
 }
 
 // ----------------------------------------------------------------- pool
@@ -975,6 +1063,23 @@ cudaError_t direct_conv(const half *x, const half *w, const half *bias,
   if (Co % 8 || !al16(y) || smem > 48 * 1024)
     return cudaErrorInvalidValue;
   const long long pixels = static_cast<long long>(batch) * OH * OW;
+  const long long pairs = static_cast<long long>(batch) * OH * ((OW + 1) / 2);
+  if (Ci <= 4 && (Co == 16 || Co == 32 || Co == 48) && pairs < (1LL << 31)) {
+    const int per_row = (OW + 1) / 2;
+#define PB2_STEM2(co)                                                          \
+  if (Co == co) {                                                              \
+    (act == kActRelu ? stem_conv2_kernel<co, kActRelu>                         \
+                     : stem_conv2_kernel<co, -1>)<<<blocks_for(pairs), kBlock, \
+                                                    smem, s>>>(                \
+        x, w, bias, y, Ci, H, W, OH, OW, KH, KW, SH, SW, PH, PW, act,          \
+        static_cast<uint32_t>(pairs), FastDiv(per_row), FastDiv(OH));          \
+    return cudaGetLastError();                                                 \
+  }
+    PB2_STEM2(16)
+    PB2_STEM2(32)
+    PB2_STEM2(48)
+#undef PB2_STEM2
+  }
   if (Ci <= 4 && (Co == 16 || Co == 32 || Co == 48 || Co == 64) &&
       pixels < (1LL << 31)) {
 #define PB2_STEM(co)                                                           \

@@ -64,10 +64,12 @@ struct Args {
   int mt, nt;          // tile grid
   int Wseg, OH, OW, batch; // conv geometry (Wseg = pixel segments per row)
   int seg_log2;            // conv: log2 of the segment length (16 or 32)
-  // Row mode (conv, 256-row tiles, OW a multiple of 16 and <= 128): a tile
-  // is row_segs whole output rows of OW pixels, each loaded as one TMA box
-  // per k-block; tile rows past row_segs * OW compute unused values.
+  // Long-segment mode (conv, 256-row tiles): an output row is seg_parts
+  // segments of seg_len pixels (a multiple of 16, at most 128); a tile is
+  // row_segs segments, each loaded as one TMA box per k-block. Tile rows
+  // past row_segs * seg_len compute unused values.
   int row_segs;            // 0: pixel-segment mode
+  int seg_len, seg_parts;
 
   GemmEpilogue epi;
   float *part_max;
@@ -85,21 +87,25 @@ template <int BN, int MH = 1> struct Cfg {
   static constexpr uint32_t B_BYTES = BN * kBK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int ACC_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
-  // Accumulator buffers: two (epilogue overlaps the next tile) with one M
-  // half; one holding both halves with two.
-  static constexpr int NACC = MH == 1 ? 2 : 1;
-  static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
-  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES > 8 ? 8 : (200 * 1024) / STAGE_BYTES;
+  // Accumulator buffers: two (the epilogue of a tile overlaps the main loop
+  // of the next) while both fit the 512 TMEM columns, else one.
+  static constexpr int NACC = MH * ACC_COLS <= 256 ? 2 : 1;
+  static constexpr uint32_t TMEM_COLS = NACC * MH * ACC_COLS;
   // TMA-store epilogue: each epilogue warp stages 32 rows x 64 columns
   // (4 KB, 128-byte swizzled), double buffered with 4 epilogue warps and
   // single buffered with 8, then one lane stores it.
   static constexpr bool TMA_EPI = BN % 64 == 0;
   static constexpr int EPI_BUFS = MH == 1 ? 2 : 1;
   static constexpr uint32_t EPI_BYTES = TMA_EPI ? 4 * MH * EPI_BUFS * 4096 : 0;
+  // As many operand stages (up to 8) as the rest of the 227 KB leaves.
+  static constexpr int STAGES_FIT = (232448 - 1024 - 256 - EPI_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
   static constexpr size_t SMEM =
       size_t(STAGES) * STAGE_BYTES + EPI_BYTES + 1024 + 256;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
-  static_assert(MH == 1 || (MH == 2 && BN == 256), "256-row tiles use N = 256");
+  static_assert(MH == 1 || MH == 2, "one or two M halves");
+  static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0,
+                "TMEM allocation");
   static_assert(B_BYTES % 1024 == 0, "B tile must keep 1024-byte alignment");
   static_assert(SMEM <= 232448, "dynamic shared memory above 227 KB");
 };
@@ -225,7 +231,7 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
         const int nbox = g.row_segs ? g.row_segs : BM >> g.seg_log2;
         const int seg0 = mb * nbox;
         // A bytes per stage: whole rows of 128 bytes actually loaded.
-        const uint32_t a_bytes = g.row_segs ? static_cast<uint32_t>(g.row_segs * g.OW * 128)
+        const uint32_t a_bytes = g.row_segs ? static_cast<uint32_t>(g.row_segs * g.seg_len * 128)
                                             : C::A_BYTES;
         // smem row offset (log2 of bytes) between boxes in pixel-segment mode
         const int box_shift = g.seg_log2 + 7;
@@ -234,8 +240,9 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
 #pragma unroll
           for (int s = 0; s < BM / 16; ++s) {
             if (g.row_segs) {
-              const int r = seg0 + s; // output row index n * OH + oh
-              seg_x[s] = -g.pad_w;
+              const int sg = seg0 + s; // segment: (n * OH + oh) * parts + part
+              const int r = sg / g.seg_parts;
+              seg_x[s] = (sg - r * g.seg_parts) * g.seg_len - g.pad_w;
               seg_n[s] = r / g.OH;
               seg_y[s] = r - seg_n[s] * g.OH - g.pad_h;
             } else {
@@ -263,7 +270,7 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
 #pragma unroll
             for (int s = 0; s < BM / 16; ++s)
               if (s < nbox)
-                tma_load_4d(sa + (g.row_segs ? s * g.OW * 128 : s << box_shift), &mapA,
+                tma_load_4d(sa + (g.row_segs ? s * g.seg_len * 128 : s << box_shift), &mapA,
                             &full[stage], cb * kBK, seg_x[s] + kw, seg_y[s] + kh, seg_n[s]);
             tma_load_3d(sb, &mapB, &full[stage], cb * kBK, tap, nb * BN);
             if (++cb == g.kb_per_tap) {
@@ -315,7 +322,7 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem_base + acc * C::ACC_COLS;
+        const uint32_t d = tmem_base + acc * MH * C::ACC_COLS;
         for (int kb = 0; kb < g.num_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort)) {
             fail(g, abort, 3);
@@ -365,15 +372,17 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
       }
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                             (acc + mh) * C::ACC_COLS;
+                             (acc * MH + mh) * C::ACC_COLS;
       // Map this thread's accumulator row to an output row.
       long long orow = -1;
       if (CONV && g.row_segs) {
-        const int sidx = row_in_tile / g.OW;
-        const int r = mb * g.row_segs + sidx;
+        const int sidx = row_in_tile / g.seg_len;
+        const int sg = mb * g.row_segs + sidx;
+        const int r = sg / g.seg_parts;
         const int n = r / g.OH;
         if (sidx < g.row_segs && n < g.batch)
-          orow = static_cast<long long>(r) * g.OW + (row_in_tile - sidx * g.OW);
+          orow = static_cast<long long>(r) * g.OW + (sg - r * g.seg_parts) * g.seg_len +
+                 (row_in_tile - sidx * g.seg_len);
       } else if (CONV) {
         const int seg = mb * (BM >> g.seg_log2) + (row_in_tile >> g.seg_log2);
         const int r = seg / g.Wseg;
@@ -422,15 +431,17 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
           __syncwarp();
           if (lane == 0) {
             if (CONV && g.row_segs) {
-              // Two 16-row pieces; OW is a multiple of 16, so a piece lies
-              // inside one output row.
+              // Two 16-row pieces; seg_len is a multiple of 16, so a piece
+              // lies inside one segment.
               for (int h = 0; h < 2; ++h) {
                 const int row0 = mh * kBM + q * 32 + h * 16;
-                const int sidx = row0 / g.OW;
-                const int r = mb * g.row_segs + sidx;
+                const int sidx = row0 / g.seg_len;
+                const int sg = mb * g.row_segs + sidx;
+                const int r = sg / g.seg_parts;
                 const int n = r / g.OH;
                 if (sidx < g.row_segs && n < g.batch)
-                  tma_store_4d(&mapC, buf + h * 2048, n_base + c, row0 - sidx * g.OW,
+                  tma_store_4d(&mapC, buf + h * 2048, n_base + c,
+                               (sg - r * g.seg_parts) * g.seg_len + row0 - sidx * g.seg_len,
                                r - n * g.OH, n);
               }
             } else if (CONV) {
@@ -726,10 +737,27 @@ bool use_two_halves(int bn, int num_kb, long long M, int nt) {
          (M + 2 * kBM - 1) / (2 * kBM) * nt >= 4LL * sm_count();
 }
 
+// 256-row tiles exist for N tiles of 64, 128 and 256 in the convolution
+// path and for N = 256 in the GEMM path.
 template <bool CONV, int EPI>
 cudaError_t dispatch_bn(int bn, bool two_halves, const CUtensorMap &a,
                         const CUtensorMap &b, const CUtensorMap &c,
                         const Args &g, cudaStream_t s) {
+  if constexpr (CONV) {
+    if (two_halves && bn != 48) {
+      switch (bn) {
+      case 64:
+        return dispatch_act<64, CONV, EPI, 2>(a, b, c, g, s);
+      case 128:
+        return dispatch_act<128, CONV, EPI, 2>(a, b, c, g, s);
+      default:
+        return dispatch_act<256, CONV, EPI, 2>(a, b, c, g, s);
+      }
+    }
+  } else {
+    if (two_halves && bn == 256)
+      return dispatch_act<256, CONV, EPI, 2>(a, b, c, g, s);
+  }
   switch (bn) {
   case 48:
     return dispatch_act<48, CONV, EPI>(a, b, c, g, s);
@@ -738,8 +766,7 @@ cudaError_t dispatch_bn(int bn, bool two_halves, const CUtensorMap &a,
   case 128:
     return dispatch_act<128, CONV, EPI>(a, b, c, g, s);
   default:
-    return two_halves ? dispatch_act<256, CONV, EPI, 2>(a, b, c, g, s)
-                      : dispatch_act<256, CONV, EPI>(a, b, c, g, s);
+    return dispatch_act<256, CONV, EPI>(a, b, c, g, s);
   }
 }
 
@@ -825,14 +852,38 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   const int seg_log2 = OW % 32 == 0 ? 5 : 4;
   const cuuint32_t seg = 1u << seg_log2;
   const int kb_tap = (s.Ci + kBK - 1) / kBK;
-  const long long m_seg = static_cast<long long>(s.batch) * OH *
-                          ((OW + static_cast<int>(seg) - 1) / static_cast<int>(seg)) * seg;
-  const bool two = use_two_halves(bn, kb_tap * taps, m_seg, (s.Co + bn - 1) / bn);
-  // Row mode for 256-row tiles: whole output rows per TMA box when at most
-  // one eighth of the tile is left unused.
+  const int num_kb = kb_tap * taps;
+  // Long-segment mode: 256-row tiles of whole output rows, or of equal
+  // parts of a row, one TMA box per part and k-block. The part length is
+  // the longest divisor of OW that is a multiple of 16, at most 128 and
+  // leaves at most one eighth of the tile unused.
+  int seg_len = 0;
+  for (int parts = 1; parts * 16 <= OW && !seg_len; ++parts) {
+    const int len = OW / parts;
+    if (OW % parts || len % 16 || len > kBM)
+      continue;
+    if ((2 * kBM / len) * len * 8 >= 7 * 2 * kBM)
+      seg_len = len;
+  }
   int row_segs = 0;
-  if (two && OW % 16 == 0 && OW <= 128 && (2 * kBM / OW) * OW * 8 >= 7 * 2 * kBM)
-    row_segs = 2 * kBM / OW;
+  bool two = false;
+  // Measured on B200: 256x256 tiles for long K at N >= 256; 256x128 and
+  // 256x64 tiles for N of 128 / 64; N = 48 and short-K N >= 256 layers keep
+  // 128-row tiles of 16/32-pixel segments.
+  if (seg_len && ((bn == 256 && num_kb >= 32) || bn == 128 || bn == 64)) {
+    const long long segs = static_cast<long long>(s.batch) * OH * (OW / seg_len);
+    const int per_tile = 2 * kBM / seg_len;
+    const long long tiles = (segs + per_tile - 1) / per_tile * ((s.Co + bn - 1) / bn);
+    if (tiles >= 2LL * sm_count()) {
+      two = true;
+      row_segs = per_tile;
+    }
+  }
+  if (!two) {
+    const long long m_seg = static_cast<long long>(s.batch) * OH *
+                            ((OW + static_cast<int>(seg) - 1) / static_cast<int>(seg)) * seg;
+    two = use_two_halves(bn, num_kb, m_seg, (s.Co + bn - 1) / bn);
+  }
   CUtensorMap ma, mb;
   cuuint64_t da[4] = {static_cast<cuuint64_t>(s.Ci), static_cast<cuuint64_t>(s.W),
                       static_cast<cuuint64_t>(s.H),
@@ -840,7 +891,7 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   cuuint64_t sa[3] = {static_cast<cuuint64_t>(s.Ci) * 2,
                       static_cast<cuuint64_t>(s.W) * s.Ci * 2,
                       static_cast<cuuint64_t>(s.H) * s.W * s.Ci * 2};
-  cuuint32_t ba[4] = {kBK, row_segs ? static_cast<cuuint32_t>(OW) : seg, 1, 1};
+  cuuint32_t ba[4] = {kBK, row_segs ? static_cast<cuuint32_t>(seg_len) : seg, 1, 1};
   cuuint64_t db[3] = {static_cast<cuuint64_t>(s.Ci), static_cast<cuuint64_t>(taps),
                       static_cast<cuuint64_t>(s.Co)};
   cuuint64_t sb[2] = {static_cast<cuuint64_t>(s.Ci) * 2,
@@ -862,6 +913,8 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   Args g{};
   g.seg_log2 = seg_log2;
   g.row_segs = row_segs;
+  g.seg_len = seg_len ? seg_len : 16;
+  g.seg_parts = seg_len ? OW / seg_len : 1;
   g.Wseg = (OW + static_cast<int>(seg) - 1) / static_cast<int>(seg);
   g.OH = OH;
   g.OW = OW;
@@ -874,7 +927,8 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   g.pad_h = s.pad_h;
   g.pad_w = s.pad_w;
   const int bm = two ? 2 * kBM : kBM;
-  g.mt = row_segs ? (s.batch * OH + row_segs - 1) / row_segs : (g.M + bm - 1) / bm;
+  g.mt = row_segs ? (s.batch * OH * g.seg_parts + row_segs - 1) / row_segs
+                  : (g.M + bm - 1) / bm;
   g.nt = (s.Co + bn - 1) / bn;
   g.epi = epi;
   g.err = device_error_word();

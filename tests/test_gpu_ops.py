@@ -76,6 +76,12 @@ CONV_CASES = [
     (316, 3, 80, 512, 512, 3),
     (301, 5, 64, 512, 512, 3),
     (160, 3, 160, 512, 512, 3),
+    # 256-row tiles with double-buffered accumulators (N tile <= 128):
+    (130, 7, 80, 64, 128, 3),   # N 128, partial last tile
+    (40, 6, 80, 128, 512, 3),   # N 512 with a short K loop -> 128-column tiles
+    (64, 12, 128, 64, 64, 3),   # N 64, 128-pixel rows
+    (24, 24, 160, 48, 48, 3),   # N 48 (direct-store epilogue), rows in 2 parts of 80
+    (10, 16, 480, 48, 48, 3),   # rows of 480 in 6 parts of 80
 ]
 
 
@@ -97,14 +103,18 @@ def test_implicit_conv(native, cuda, batch, h, w, ci, co, k):
     assert_close(host(y), want, what=f"conv{k}x{k} {batch}x{h}x{w}x{ci}->{co}")
 
 
-def test_stem_direct_conv(native, cuda):
-    r = rng(3)
-    x = f16(r.uniform(-1, 1, (2, 48, 320, 3)))
-    wt = f16(r.standard_normal((48, 3, 3, 3)) * np.sqrt(2.0 / 27))
-    b = f16(r.normal(0, 0.1, 48))
-    y = torch.empty(2, 24, 160, 48, dtype=torch.float16, device=cuda)
+@pytest.mark.parametrize("batch,h,w,co", [(2, 48, 320, 48), (1, 9, 35, 48), (2, 10, 12, 32), (1, 8, 8, 64)])
+def test_stem_direct_conv(native, cuda, batch, h, w, co):
+    """Stem 3x3 stride-2 conv with 3 input channels (odd output widths
+    leave a single pixel in the last pair)."""
+    r = rng(3 + w)
+    x = f16(r.uniform(-1, 1, (batch, h, w, 3)))
+    wt = f16(r.standard_normal((co, 3, 3, 3)) * np.sqrt(2.0 / 27))
+    b = f16(r.normal(0, 0.1, co))
+    oh, ow = (h + 2 - 3) // 2 + 1, (w + 2 - 3) // 2 + 1
+    y = torch.empty(batch, oh, ow, co, dtype=torch.float16, device=cuda)
     dx, dw, db = dev(x), dev(wt), dev(b)
-    rc = native.ppocr_b200_conv_nhwc(ptr(dx), ptr(dw), ptr(db), ptr(y), 2, 3, 48, 320, 48, 3, 3,
+    rc = native.ppocr_b200_conv_nhwc(ptr(dx), ptr(dw), ptr(db), ptr(y), batch, 3, h, w, co, 3, 3,
                                      2, 2, 1, 1, 1, 1, stream_handle())
     assert rc == 0, native.ppocr_b200_last_error()
     sync()
