@@ -41,7 +41,9 @@ SEED = 20261201
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=None,
+                   help="timed steps (default 20 for c4; 200 for the sub-millisecond c1-c3 steps and the "
+                        "c5 latency distribution)")
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--model", default=MODEL, choices=["rec_b512", "rec_b256", "rec_b64"],
@@ -523,7 +525,6 @@ def config_arm(args):
     r = workloads.rng(SEED)
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
     warm = max(args.warmup, 3)
-    args.steps = max(args.steps, 200)  # sub-millisecond steps: a longer timed region
     extra = {}
 
     if args.config == "c1":
@@ -643,7 +644,7 @@ def config_arm(args):
             pp.enqueue(pages, crops)
         stream.synchronize()
         assert lib.ppocr_b200_device_error() == 0
-        runs = max(args.steps, 100)
+        runs = args.steps
         with ClockSampler(local) as clocks:
             step_ms = _event_steps(stream, runs, lambda i: pp.enqueue(pages, crops), flush)
         bm_h = torch.empty_like(pp.bitmap, device="cpu").pin_memory()
@@ -832,6 +833,8 @@ def _cpu_c5():
 
 def main():
     args = parse()
+    if args.steps is None:
+        args.steps = 20 if args.config == "c4" or args.impl == "reference" else 200
     if args.impl == "reference":
         reference_arm(args)
     elif args.config != "c4":
