@@ -142,21 +142,107 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Few outputs per input pixel with Ci a multiple of 8 (the DB head's last
+// 64 -> 1 upsampling): G = Ci/8 threads share an input pixel, each loading
+// one 16-byte group of 8 channels (a warp reads 512 contiguous bytes) and
+// holding that group's filter rows in registers; the NOUT partial sums are
+// added across the G threads with shuffles and the group-0 thread writes
+// the pixel's KH x KW x Co outputs. Grid-stride over pixels.
+template <int NMAX, int G>
+__global__ void __launch_bounds__(256)
+    deconv_group_kernel(const half *__restrict__ x, const half *__restrict__ w,
+                        const half *__restrict__ bias, half *__restrict__ y,
+                        uint32_t pixels, FastDiv by_w, FastDiv by_h, int Co,
+                        int KH, int KW, int act) {
+  const int nout = KH * KW * Co;
+  const int g = threadIdx.x % G;
+  float wr[8][NMAX]; // this group's 8 channels x outputs
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+#pragma unroll
+    for (int o = 0; o < NMAX; ++o)
+      wr[c][o] = o < nout ? __half2float(w[(g * 8 + c) * nout + o]) : 0.f;
+  const int W = static_cast<int>(by_w.d), H = static_cast<int>(by_h.d);
+  const long long OW = static_cast<long long>(W) * KW;
+  const long long OH = static_cast<long long>(H) * KH;
+  const uint32_t step = gridDim.x * (blockDim.x / G);
+  // The loop bound is uniform across a warp (its first pixel), so every lane
+  // reaches the shuffles; lanes past the last pixel compute zeros.
+  const uint32_t warp_first = blockIdx.x * (blockDim.x / G) + (threadIdx.x & ~31u) / G;
+  for (uint32_t pw = warp_first; pw < pixels; pw += step) {
+    const uint32_t p = pw + (threadIdx.x & 31u) / G;
+    const bool valid = p < pixels;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (valid)
+      u = __ldcs(reinterpret_cast<const uint4 *>(x + static_cast<long long>(p) * G * 8) + g);
+    const half2 *h2 = reinterpret_cast<const half2 *>(&u);
+    float acc[NMAX];
+#pragma unroll
+    for (int o = 0; o < NMAX; ++o)
+      acc[o] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h2[j]);
+#pragma unroll
+      for (int o = 0; o < NMAX; ++o) {
+        acc[o] = fmaf(f.x, wr[2 * j][o], acc[o]);
+        acc[o] = fmaf(f.y, wr[2 * j + 1][o], acc[o]);
+      }
+    }
+#pragma unroll
+    for (int off = G / 2; off; off >>= 1)
+#pragma unroll
+      for (int o = 0; o < NMAX; ++o)
+        acc[o] += __shfl_xor_sync(0xffffffffu, acc[o], off);
+    if (valid && g == 0) {
+      const uint32_t r = by_w.div(p);
+      const int iw = static_cast<int>(p - r * by_w.d);
+      const uint32_t n = by_h.div(r);
+      const int ih = static_cast<int>(r - n * by_h.d);
+#pragma unroll
+      for (int o = 0; o < NMAX; ++o) {
+        if (o >= nout)
+          break;
+        const int co = o % Co, tap = o / Co;
+        const int a = tap / KW, b = tap - a * KW;
+        float v = round_half(acc[o]);
+        if (bias)
+          v += __half2float(bias[co]);
+        y[((static_cast<long long>(n) * OH + ih * KH + a) * OW + iw * KW + b) * Co + co] =
+            __float2half_rn(apply_act(v, act));
+      }
+    }
+  }
+}
+
+// Four float4 loads in flight per thread (16 probabilities), 4-byte stores.
 __global__ void __launch_bounds__(256)
     binarize_kernel(const float *__restrict__ prob, uint8_t *__restrict__ map,
                     size_t n, float thresh) {
-  const size_t i4 = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
-  if (i4 + 4 <= n) {
-    const float4 v = __ldg(reinterpret_cast<const float4 *>(prob + i4));
-    uchar4 o;
-    o.x = v.x > thresh ? 255 : 0;
-    o.y = v.y > thresh ? 255 : 0;
-    o.z = v.z > thresh ? 255 : 0;
-    o.w = v.w > thresh ? 255 : 0;
-    *reinterpret_cast<uchar4 *>(map + i4) = o;
-  } else {
-    for (size_t i = i4; i < n; ++i)
-      map[i] = prob[i] > thresh ? 255 : 0;
+  const size_t nv = n / 4; // whole float4 vectors
+  const size_t v0 = static_cast<size_t>(blockIdx.x) * blockDim.x * 4 + threadIdx.x;
+  float4 v[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const size_t i = v0 + static_cast<size_t>(k) * blockDim.x;
+    if (i < nv)
+      v[k] = __ldcs(reinterpret_cast<const float4 *>(prob) + i);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const size_t i = v0 + static_cast<size_t>(k) * blockDim.x;
+    if (i < nv) {
+      uchar4 o;
+      o.x = v[k].x > thresh ? 255 : 0;
+      o.y = v[k].y > thresh ? 255 : 0;
+      o.z = v[k].z > thresh ? 255 : 0;
+      o.w = v[k].w > thresh ? 255 : 0;
+      reinterpret_cast<uchar4 *>(map)[i] = o;
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x < n - nv * 4) {
+    const size_t i = nv * 4 + threadIdx.x;
+    map[i] = prob[i] > thresh ? 255 : 0;
   }
 }
 
@@ -169,9 +255,10 @@ cudaError_t binarize(const float *prob, uint8_t *map, size_t n, float thresh,
   if ((reinterpret_cast<uintptr_t>(prob) & 15) ||
       (reinterpret_cast<uintptr_t>(map) & 3))
     return cudaErrorInvalidValue;
-  const size_t threads = (n + 3) / 4;
-  binarize_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, s>>>(
-      prob, map, n, thresh);
+  const size_t vectors = n / 4;
+  const size_t blocks = vectors ? (vectors + 1023) / 1024 : 1;
+  binarize_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(prob, map, n,
+                                                                 thresh);
   return cudaGetLastError();
 }
 
@@ -198,6 +285,22 @@ cudaError_t deconv_kxk(const half *x, const half *w, const half *bias, half *y,
     return cudaSuccess;
   const long long pixels = static_cast<long long>(batch) * H * W;
   const int nout = KH * KW * Co;
+  if (nout <= 4 && (Ci == 64 || Ci == 128 || Ci == 256) && pixels < (1LL << 31) &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const int G = Ci / 8; // threads per pixel
+    const long long per_block = 256 / G;
+    long long blocks = (pixels + per_block - 1) / per_block;
+    const long long cap = static_cast<long long>(sm_count()) * 8;
+    if (blocks > cap)
+      blocks = cap;
+    auto k = G == 8 ? deconv_group_kernel<4, 8> : G == 16 ? deconv_group_kernel<4, 16>
+                                                          : deconv_group_kernel<4, 32>;
+    k<<<static_cast<unsigned>(blocks), 256, 0, s>>>(x, w, bias, y,
+                                                    static_cast<uint32_t>(pixels),
+                                                    FastDiv(W), FastDiv(H), Co, KH,
+                                                    KW, act);
+    return cudaGetLastError();
+  }
   const size_t smem = sizeof(float) * static_cast<size_t>(Ci) * nout;
   if (nout <= 16 && pixels < (1LL << 31) && smem <= 48 * 1024) {
     const unsigned blocks = static_cast<unsigned>((pixels + 255) / 256);

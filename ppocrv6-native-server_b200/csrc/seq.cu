@@ -295,53 +295,69 @@ __global__ void __launch_bounds__(256)
 }
 
 // Short-sequence attention (seq <= SMAX, head_dim <= 16), one line per
-// block, one thread per (head, query) row doing the whole row: the K and V
-// of the line are staged in shared memory ([head][key][16], zero-padded);
-// the thread keeps q' = round(q*scale) and its row of scores in registers,
-// S = round(q'.k) (fp16 operands, fp32 sums, two interleaved chains over d),
-// P = round(exp(S - max) * (1/sum)) with exp on the special-function unit,
-// O = round(sum_j P_j v_j) (j ascending, fp32). The K/V reads are warp-wide
-// broadcasts (a warp's rows share a head); every multiply-add is one
-// mixed-precision instruction.
+// block, one thread per (head, query) row doing the whole row: the line's
+// q' = round(q*scale), K and V are staged in shared memory ([head][pos][16],
+// zero-padded) with 16-byte loads where the row layout allows; the thread
+// keeps its q' and its row of scores in registers, S = round(q'.k) (fp16
+// operands, fp32 sums, two interleaved chains over d), P = round(exp(S -
+// max) * (1/sum)) with exp on the special-function unit, O = round(sum_j
+// P_j v_j) (j ascending, fp32). The K/V reads are warp-wide broadcasts (a
+// warp's rows share a head); every multiply-add is one mixed-precision
+// instruction.
 template <int SMAX>
 __global__ void __launch_bounds__(512)
     attention_rows_kernel(const half *__restrict__ qkv, half *__restrict__ out,
                           int seq, int heads, int dh, float scale,
-                          FastDiv by_hd, FastDiv by_dh, FastDiv by_seq) {
+                          FastDiv by_hd, FastDiv by_dh, FastDiv by_seq, int vec) {
   constexpr int DP = 16;
   extern __shared__ uint4 att_smem[];
-  half *ks = reinterpret_cast<half *>(att_smem); // [heads][seq][DP]
+  half *qs = reinterpret_cast<half *>(att_smem); // [heads][seq][DP]
+  half *ks = qs + heads * seq * DP;
   half *vs = ks + heads * seq * DP;
   const int hd = heads * dh;
   const int width = 3 * hd;
   const long long line = blockIdx.x;
   const half *src = qkv + line * seq * width;
   const half zero = __float2half_rn(0.f);
-  for (int e = threadIdx.x; e < heads * seq * DP; e += blockDim.x)
-    ks[e] = vs[e] = zero;
+  if (dh < DP)
+    for (int e = threadIdx.x; e < heads * seq * DP; e += blockDim.x)
+      qs[e] = ks[e] = vs[e] = zero;
   __syncthreads();
-  for (uint32_t e = threadIdx.x; e < static_cast<uint32_t>(seq * hd); e += blockDim.x) {
-    const uint32_t j = by_hd.div(e), c = e - j * hd;
+  auto put = [&](uint32_t c, int j, half q, half k, half v) {
     const uint32_t h = by_dh.div(c), d = c - h * dh;
     const int at = (h * seq + j) * DP + d;
-    ks[at] = src[j * width + hd + c];
-    vs[at] = src[j * width + 2 * hd + c];
+    qs[at] = __float2half_rn(__half2float(q) * scale);
+    ks[at] = k;
+    vs[at] = v;
+  };
+  if (vec) {
+    // hd and the row width are multiples of 8 halves: whole 16-byte groups
+    const int groups = hd >> 3;
+    for (int e = threadIdx.x; e < seq * groups; e += blockDim.x) {
+      const int j = e / groups, c8 = (e - j * groups) * 8;
+      const uint4 *row = reinterpret_cast<const uint4 *>(src + j * width + c8);
+      const uint4 uq = row[0], uk = row[hd >> 3], uv = row[hd >> 2];
+      const half *hq = reinterpret_cast<const half *>(&uq);
+      const half *hk = reinterpret_cast<const half *>(&uk);
+      const half *hv = reinterpret_cast<const half *>(&uv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        put(c8 + i, j, hq[i], hk[i], hv[i]);
+    }
+  } else {
+    for (uint32_t e = threadIdx.x; e < static_cast<uint32_t>(seq * hd); e += blockDim.x) {
+      const uint32_t j = by_hd.div(e), c = e - j * hd;
+      put(c, j, src[j * width + c], src[j * width + hd + c], src[j * width + 2 * hd + c]);
+    }
   }
   __syncthreads();
   const int rows = heads * seq;
   for (int row = threadIdx.x; row < rows; row += blockDim.x) {
     const int h = static_cast<int>(by_seq.div(row));
     const int i = row - h * seq;
-    const half *qr = src + i * width + h * dh;
-    uint32_t q[DP / 2];
-#pragma unroll
-    for (int d2 = 0; d2 < DP / 2; ++d2) {
-      const int d = 2 * d2;
-      const half lo = d < dh ? __float2half_rn(__half2float(qr[d]) * scale) : zero;
-      const half hi = d + 1 < dh ? __float2half_rn(__half2float(qr[d + 1]) * scale) : zero;
-      q[d2] = static_cast<uint32_t>(__half_as_ushort(lo)) |
-              (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
-    }
+    const uint4 *q4 = reinterpret_cast<const uint4 *>(qs + row * DP);
+    const uint4 qa = q4[0], qb = q4[1];
+    const uint32_t q[DP / 2] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
     const uint4 *k4 = reinterpret_cast<const uint4 *>(ks + h * seq * DP);
     float sc[SMAX];
     float m = -INFINITY;
@@ -455,11 +471,12 @@ cudaError_t attention(const half *qkv, half *out, int lines, int seq, int heads,
   if (dh <= 16 && seq <= 64) {
     const int rows = heads * seq;
     const int threads = rows >= 512 ? 512 : (rows + 31) / 32 * 32;
-    const size_t smem = sizeof(half) * 2ull * heads * seq * 16;
+    const size_t smem = sizeof(half) * 3ull * heads * seq * 16;
+    const int vec = (heads * dh) % 8 == 0 && (reinterpret_cast<uintptr_t>(qkv) & 15) == 0;
     if (smem <= 48 * 1024) {
       attention_rows_kernel<64><<<lines, threads, smem, s>>>(
           qkv, out, seq, heads, dh, scale, FastDiv(heads * dh), FastDiv(dh),
-          FastDiv(seq));
+          FastDiv(seq), vec);
       return cudaGetLastError();
     }
   }

@@ -737,8 +737,7 @@ bool use_two_halves(int bn, int num_kb, long long M, int nt) {
          (M + 2 * kBM - 1) / (2 * kBM) * nt >= 4LL * sm_count();
 }
 
-// 256-row tiles exist for N tiles of 64, 128 and 256 in the convolution
-// path and for N = 256 in the GEMM path.
+// 256-row tiles exist for N tiles of 64, 128 and 256.
 template <bool CONV, int EPI>
 cudaError_t dispatch_bn(int bn, bool two_halves, const CUtensorMap &a,
                         const CUtensorMap &b, const CUtensorMap &c,
@@ -755,8 +754,18 @@ cudaError_t dispatch_bn(int bn, bool two_halves, const CUtensorMap &a,
       }
     }
   } else {
-    if (two_halves && bn == 256)
-      return dispatch_act<256, CONV, EPI, 2>(a, b, c, g, s);
+    if (two_halves) {
+      switch (bn) {
+      case 64:
+        return dispatch_act<64, CONV, EPI, 2>(a, b, c, g, s);
+      case 128:
+        return dispatch_act<128, CONV, EPI, 2>(a, b, c, g, s);
+      case 256:
+        return dispatch_act<256, CONV, EPI, 2>(a, b, c, g, s);
+      default:
+        break;
+      }
+    }
   }
   switch (bn) {
   case 48:
@@ -823,7 +832,13 @@ cudaError_t tc_gemm(const half *A, int M, int K, int lda, const half *W, int N,
   g.num_kb = (K + kBK - 1) / kBK;
   g.kb_per_tap = g.num_kb;
   g.KW = 1;
-  const bool two = use_two_halves(bn, g.num_kb, M, (N + bn - 1) / bn);
+  // 256-row tiles: long K at N = 256 (see use_two_halves), or a short K
+  // loop at N <= 128, where the epilogue dominates and 8 epilogue warps with
+  // a double-buffered accumulator drain twice the rows per tile.
+  const int nt = (N + bn - 1) / bn;
+  const bool two = use_two_halves(bn, g.num_kb, M, nt) ||
+                   ((bn == 64 || bn == 128) && g.num_kb <= 4 &&
+                    (M + 2 * kBM - 1) / (2 * kBM) * nt >= 2LL * sm_count());
   const int bm = two ? 2 * kBM : kBM;
   g.mt = (M + bm - 1) / bm;
   g.nt = (N + bn - 1) / bn;
@@ -870,7 +885,7 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   // Measured on B200: 256x256 tiles for long K at N >= 256; 256x128 and
   // 256x64 tiles for N of 128 / 64; N = 48 and short-K N >= 256 layers keep
   // 128-row tiles of 16/32-pixel segments.
-  if (seg_len && ((bn == 256 && num_kb >= 32) || bn == 128 || bn == 64)) {
+  if (seg_len && ((bn == 256 && num_kb >= 16) || bn == 128 || bn == 64)) {
     const long long segs = static_cast<long long>(s.batch) * OH * (OW / seg_len);
     const int per_tile = 2 * kBM / seg_len;
     const long long tiles = (segs + per_tile - 1) / per_tile * ((s.Co + bn - 1) / bn);

@@ -38,6 +38,9 @@ GEMM_CASES = [
     # 256-row tiles (K >= 32 k-blocks, >= 4 tiles per SM), partial last tile
     (40000, 2048, 1024, True, False, 1),
     (37900, 2048, 1024, True, True, 0),
+    # 256-row tiles for short K at N <= 128 (double-buffered accumulator)
+    (76000, 64, 128, True, False, 3),
+    (80000, 120, 64, True, True, 0),
 ]
 
 
@@ -182,7 +185,7 @@ def test_softmax(native, cuda):
 
 
 @pytest.mark.parametrize("lines,seq,heads,dh", [(4, 40, 8, 15), (3, 25, 4, 16), (2, 20, 2, 24), (2, 70, 2, 8),
-                                               (1, 10, 2, 40)])
+                                               (1, 10, 2, 40), (3, 17, 3, 5), (2, 64, 8, 16)])
 def test_attention(native, cuda, lines, seq, heads, dh):
     r = rng(13 + seq)
     qkv = f16(r.standard_normal((lines, seq, 3 * heads * dh)))
@@ -232,6 +235,8 @@ DECONV_CASES = [
     (1, 7, 30, 64, 128, 0, True),     # tensor cores, ragged 16-pixel segments
     (2, 12, 64, 64, 64, 1, False),    # tensor cores, 32-pixel segments, no bias
     (1, 9, 11, 24, 3, 0, True),       # 12 outputs per pixel, Ci not a multiple of 8
+    (1, 5, 7, 128, 1, 4, False),      # 16 threads per input pixel, partial warp at the end
+    (3, 33, 29, 64, 1, 4, True),      # 8 threads per pixel, grid-stride with a ragged tail
 ]
 
 
@@ -251,10 +256,12 @@ def test_deconv(native, cuda, batch, h, w, ci, co, act, bias):
     assert_close(host(y), L.deconv_kxk(x, wt, b, act), what=f"deconv {batch}x{h}x{w}x{ci}->{co}")
 
 
-def test_binarize_bit_exact(native, cuda):
+@pytest.mark.parametrize("n", [960 * 960 + 3, 5, 3, 1, 4096 * 4 + 7])
+def test_binarize_bit_exact(native, cuda, n):
     r = rng(17)
-    p = r.uniform(0, 1, 960 * 960 + 3).astype(np.float32)
-    p[:5] = [0.3, np.nextafter(np.float32(0.3), 1), np.nextafter(np.float32(0.3), 0), 0.0, 1.0]
+    p = r.uniform(0, 1, n).astype(np.float32)
+    edge = [0.3, np.nextafter(np.float32(0.3), 1), np.nextafter(np.float32(0.3), 0), 0.0, 1.0]
+    p[:min(5, n)] = edge[:min(5, n)]
     d = torch.from_numpy(p).cuda()
     m = torch.empty(p.size, dtype=torch.uint8, device=cuda)
     assert native.ppocr_b200_binarize(ptr(d), ptr(m), p.size, 0.3, stream_handle()) == 0
@@ -304,11 +311,12 @@ def test_logits_argmax_and_collapse(native, cuda, oracle_c):
 
 
 @pytest.mark.parametrize("rows,V,offset", [(3, 5, 0), (7, 1, 0), (64, 300, 0), (64, 300, 1),
-                                           (40, 18385, 1), (33, 4099, 0)])
+                                           (40, 18385, 1), (33, 4099, 0), (6, 40001, 0), (5, 40001, 3)])
 def test_logits_argmax_shapes(native, cuda, oracle_c, rows, V, offset):
-    """Row staging edge cases: rows shorter than one 16-byte vector, odd
-    vocabularies (rows start at any 2-byte offset), a base pointer that is
-    not 16-byte aligned (register path), ties (repeated maxima)."""
+    """Edge cases: rows shorter than one 16-byte vector, odd vocabularies
+    (rows start at any 2-byte offset), base pointers that are not 16-byte
+    aligned, ties (repeated maxima), and vocabularies past the cluster form's
+    8 x 4088 columns (shared-memory staged and register forms)."""
     r = rng(30 + V + offset)
     logits = r.standard_normal((rows, V)).astype(np.float16)
     logits[::3, V // 2] = 8.0
