@@ -31,6 +31,22 @@ int ppocr_b200_conv_nhwc(const void *x, const void *w, const void *bias,
                          int pad_w, int groups, int activation,
                          cudaStream_t stream);
 
+// The stem form of Runtime::conv (runtime.cuh:766-815, cuDNN in the
+// reference): 3x3 stride-2 pad-1 conv of a ci <= 4 channels-last image, run
+// on the tensor cores as a 2x2 conv of the image's space-to-depth
+// rearrangement. ppocr_b200_stem_s2d_pack re-lays w [co][3][3][ci] into
+// wp [co][2][2][16] (co * 64 halves, 16-byte aligned) once;
+// ppocr_b200_stem_conv_s2d uses caller-provided scratch of
+// ppocr_b200_stem_s2d_scratch_bytes(batch, h, w) bytes (16-byte aligned).
+// Output [batch][(h+1)/2][(w+1)/2][co]; bias may be null.
+int ppocr_b200_stem_s2d_pack(const void *w, void *wp, int co, int ci,
+                             cudaStream_t stream);
+size_t ppocr_b200_stem_s2d_scratch_bytes(int batch, int h, int w_);
+int ppocr_b200_stem_conv_s2d(const void *x, const void *wp, const void *bias,
+                             void *y, void *scratch, int batch, int ci, int h,
+                             int w_, int co, int activation,
+                             cudaStream_t stream);
+
 // Runtime::gemm_epilogue (runtime.cuh:514-646): y[rows][co] =
 // act(x[rows][ci] . w[co][ci]^T + bias) (+ residual[rows][co]).
 int ppocr_b200_gemm_epilogue(const void *x, const void *w, const void *bias,

@@ -207,6 +207,35 @@ int ppocr_b200_conv_nhwc(const void *x, const void *w, const void *bias,
   return status(e, "conv");
 }
 
+int ppocr_b200_stem_s2d_pack(const void *w, void *wp, int co, int ci,
+                             cudaStream_t stream) {
+  g_error.clear();
+  if (!w || !wp || co <= 0 || co % 8 || ci <= 0 || ci > 4)
+    return fail("invalid stem pack arguments");
+  return status(stem_s2d_pack(H(w), Hm(wp), co, ci, stream), "stem pack");
+}
+
+size_t ppocr_b200_stem_s2d_scratch_bytes(int batch, int h, int w_) {
+  if (batch <= 0 || h <= 0 || w_ <= 0)
+    return 0;
+  return stem_s2d_scratch_bytes(batch, h, w_);
+}
+
+int ppocr_b200_stem_conv_s2d(const void *x, const void *wp, const void *bias,
+                             void *y, void *scratch, int batch, int ci, int h,
+                             int w_, int co, int act, cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !wp || !y || !scratch || batch <= 0 || h <= 0 || w_ <= 0 ||
+      ci <= 0 || ci > 4 || co <= 0 || co % 8)
+    return fail("invalid stem conv arguments");
+  if ((reinterpret_cast<uintptr_t>(scratch) | reinterpret_cast<uintptr_t>(wp) |
+       reinterpret_cast<uintptr_t>(y)) & 15)
+    return fail("stem conv buffers must be 16-byte aligned");
+  return status(stem_conv_s2d(H(x), H(wp), H(bias), Hm(y), Hm(scratch), batch, ci, h, w_,
+                              co, act, stream),
+                "stem conv");
+}
+
 int ppocr_b200_gemm_epilogue(const void *x, const void *w, const void *bias,
                              const void *residual, void *y, int rows, int ci,
                              int co, int act, cudaStream_t stream) {

@@ -40,6 +40,9 @@ cudaError_t tc_gemm(const half *A, int M, int K, int lda, const half *W, int N,
 // OH = H + 2*pad_h - KH + 1, OW = W + 2*pad_w - KW + 1.
 struct ConvShape {
   int batch, H, W, Ci, Co, KH, KW, pad_h, pad_w;
+  // Output extent; 0 = H + 2*pad_h - KH + 1 (symmetric padding). A smaller
+  // extent drops the bottom/right padding (asymmetric pad).
+  int out_h = 0, out_w = 0;
 };
 cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
                     const GemmEpilogue &epi, cudaStream_t stream);
@@ -86,6 +89,17 @@ cudaError_t depthwise(const half *x, const half *w, const half *bias, half *y,
                       int batch, int C, int H, int W, int OH, int OW, int KH,
                       int KW, int SH, int SW, int PH, int PW, int act,
                       cudaStream_t stream);
+// Stem 3x3 stride-2 pad-1 conv of a Ci <= 4 image on the tensor cores, as a
+// 2x2 stride-1 conv of its space-to-depth rearrangement (16 channels):
+// stem_s2d_pack re-lays w [Co][3][3][Ci] as wp [Co][2][2][16] (once);
+// stem_conv_s2d writes the rearranged image into scratch
+// (stem_s2d_scratch_bytes, 16-byte aligned) and runs the implicit GEMM.
+cudaError_t stem_s2d_pack(const half *w, half *wp, int Co, int Ci,
+                          cudaStream_t s);
+size_t stem_s2d_scratch_bytes(int batch, int H, int W);
+cudaError_t stem_conv_s2d(const half *x, const half *wp, const half *bias,
+                          half *y, half *scratch, int batch, int Ci, int H,
+                          int W, int Co, int act, cudaStream_t s);
 // Generic NHWC direct conv for small Ci (stem): w [Co][KH][KW][Ci].
 cudaError_t direct_conv(const half *x, const half *w, const half *bias,
                         half *y, int batch, int Ci, int H, int W, int Co,

@@ -364,6 +364,224 @@ cudaError_t launch_dw_tma(const half *x, const half *w, const half *bias,
   return cudaGetLastError();
 }
 
+// Multi-row tiled form: a block computes TH output rows x TW output columns
+// x CB (<= 64) channels. One 4-D TMA box brings all the input it needs,
+// ((TH-1)*SH + KH) rows x ((TW-1)*SW + KW) columns x CB channels (zero-filled
+// outside the image: the padding), so each input row leaves HBM once per
+// block instead of once per output row; the filter slice is staged tap-major
+// beside it. A thread owns PIX consecutive output columns x 8 channels and
+// walks the block's TH output rows; per input row it loads its strip of
+// (PIX-1)*SW + KW 16-byte vectors once and reuses it for all KW taps. Sums
+// follow the reference's tap order with one mixed-precision FMA per
+// multiply-add (bit-identical to the other forms). The host sizes TW to
+// divide the output width evenly (OW = 80 is one tile of 80 columns).
+template <int KH, int KW, int SH, int SW, int PIX, int ACT>
+__global__ void __launch_bounds__(256)
+    depthwise_tile_kernel(const __grid_constant__ CUtensorMap xmap,
+                          const half *__restrict__ w,
+                          const half *__restrict__ bias, half *__restrict__ y,
+                          int C, int H, int OH, int OW, int PH, int PW, int CB,
+                          int TH, int TW, int tiles_h, int tiles_w, int chunks,
+                          int act, int *err) {
+  constexpr int TAPS = KH * KW;
+  constexpr int NCOL = (PIX - 1) * SW + KW;
+  extern __shared__ __align__(128) uint8_t dwt_smem[];
+  __shared__ uint64_t bar;
+  __shared__ int failed;
+  const int twin = (TW - 1) * SW + KW;
+  const int rin = (TH - 1) * SH + KH;
+  half *xs = reinterpret_cast<half *>(dwt_smem); // [rin][twin][CB]
+  half *ws = xs + rin * twin * CB;                // [TAPS][CB]
+  // block -> (n, row tile, column tile, channel chunk)
+  int b = blockIdx.x;
+  const int chunk = b % chunks;
+  b /= chunks;
+  const int tw = b % tiles_w;
+  b /= tiles_w;
+  const int th = b % tiles_h;
+  const int n = b / tiles_h;
+  const int c0 = chunk * CB, ow0 = tw * TW, oh0 = th * TH;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    failed = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bar, static_cast<uint32_t>(rin * twin * CB * 2));
+    tma_load_4d(xs, &xmap, &bar, c0, ow0 * SW - PW, oh0 * SH - PH, n);
+  }
+  // w is [C][KH][KW]: consecutive threads read consecutive filter values.
+  for (int j = threadIdx.x; j < TAPS * CB; j += blockDim.x) {
+    const int c = j / TAPS, tap = j - c * TAPS;
+    ws[tap * CB + c] = w[static_cast<long long>(c0) * TAPS + j];
+  }
+  volatile int no_abort = 0;
+  const bool ok = mbar_wait(&bar, 0, &no_abort);
+  if (!ok)
+    failed = 1;
+  __syncthreads();
+  if (failed) {
+    if (!ok)
+      mbar_wait(&bar, 0, &no_abort);
+    if (threadIdx.x == 0 && err)
+      atomicCAS(err, 0, 7);
+    return;
+  }
+  const int groups = CB >> 3;
+  const int g = threadIdx.x % groups;
+  const int t = threadIdx.x / groups;
+  if (t * PIX >= TW)
+    return;
+  const int col0 = t * PIX * SW;
+  float bv[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    bv[j] = bias ? __half2float(bias[c0 + g * 8 + j]) : 0.f;
+  for (int rr = 0; rr < TH; ++rr) {
+    const int oh = oh0 + rr;
+    if (oh >= OH)
+      break;
+    float acc[PIX][8];
+#pragma unroll
+    for (int p = 0; p < PIX; ++p)
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        acc[p][j] = 0.f;
+#pragma unroll
+    for (int a = 0; a < KH; ++a) {
+      // Rows outside the image (zero in shared memory) are skipped, as the
+      // reference does.
+      const int r = oh * SH - PH + a;
+      if (r < 0 || r >= H)
+        continue;
+      const uint4 *row =
+          reinterpret_cast<const uint4 *>(xs + ((rr * SH + a) * twin + col0) * CB) + g;
+      uint4 strip[NCOL];
+#pragma unroll
+      for (int k = 0; k < NCOL; ++k)
+        strip[k] = row[k * groups];
+#pragma unroll
+      for (int bq = 0; bq < KW; ++bq) {
+        const uint4 wt = reinterpret_cast<const uint4 *>(ws + (a * KW + bq) * CB)[g];
+#pragma unroll
+        for (int p = 0; p < PIX; ++p) {
+          const uint4 xv = strip[p * SW + bq];
+          fma2_h(acc[p][0], acc[p][1], xv.x, wt.x);
+          fma2_h(acc[p][2], acc[p][3], xv.y, wt.y);
+          fma2_h(acc[p][4], acc[p][5], xv.z, wt.z);
+          fma2_h(acc[p][6], acc[p][7], xv.w, wt.w);
+        }
+      }
+    }
+    half *yrow = y + (static_cast<long long>(n) * OH + oh) * OW * C + c0 + g * 8;
+#pragma unroll
+    for (int p = 0; p < PIX; ++p) {
+      const int ow = ow0 + t * PIX + p;
+      if (ow >= OW)
+        break;
+      Pack8 o;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float v0 = round_half(acc[p][2 * j]);
+        float v1 = round_half(acc[p][2 * j + 1]);
+        if (bias) {
+          v0 = act_t<ACT>(v0 + bv[2 * j], act);
+          v1 = act_t<ACT>(v1 + bv[2 * j + 1], act);
+        }
+        o.h[j] = __floats2half2_rn(v0, v1);
+      }
+      *reinterpret_cast<uint4 *>(yrow + static_cast<long long>(ow) * C) = o.u;
+    }
+  }
+}
+
+// Tile shape for depthwise_tile_kernel: the fewest column tiles of at most
+// tw_max columns (TW a multiple of PIX, split evenly), then the most output
+// rows whose input box fits smem_max bytes, split evenly over the row tiles.
+struct DwTile {
+  int CB = 0, TW = 0, TH = 0, tiles_w = 0, tiles_h = 0, threads = 0;
+  size_t smem = 0;
+};
+
+inline DwTile pick_dw_tile(int C, int OH, int OW, int KH, int KW, int SH, int SW,
+                           int PIX, int tw_req, int th_req) {
+  DwTile t;
+  t.CB = C % 64 == 0 ? 64 : (C <= 64 ? C : 0);
+  if (!t.CB)
+    return t;
+  const int groups = t.CB / 8;
+  const int tw_max = tw_req > 0 ? tw_req : std::min(256 / groups * PIX, 96);
+  t.tiles_w = (OW + tw_max - 1) / tw_max;
+  t.TW = ((OW + t.tiles_w - 1) / t.tiles_w + PIX - 1) / PIX * PIX;
+  t.threads = groups * (t.TW / PIX);
+  const int twin = (t.TW - 1) * SW + KW;
+  if (t.threads > 256 || twin > 256) {
+    t.CB = 0;
+    return t;
+  }
+  const size_t row_bytes = static_cast<size_t>(twin) * t.CB * 2;
+  const size_t wbytes = static_cast<size_t>(KH) * KW * t.CB * 2;
+  const size_t smem_max = 76 * 1024;
+  int th = th_req > 0 ? th_req : 1;
+  if (th_req <= 0)
+    while (th < OH && th < 16 &&
+           static_cast<size_t>(th * SH + KH) * row_bytes + wbytes <= smem_max)
+      ++th;
+  t.tiles_h = (OH + th - 1) / th;
+  t.TH = (OH + t.tiles_h - 1) / t.tiles_h;
+  const int rin = (t.TH - 1) * SH + KH;
+  if (rin > 256) {
+    t.CB = 0;
+    return t;
+  }
+  t.smem = rin * row_bytes + wbytes;
+  return t;
+}
+
+template <int KH, int KW, int SH, int SW>
+cudaError_t launch_dw_tile(const half *x, const half *w, const half *bias,
+                           half *y, int batch, int C, int H, int W, int OH,
+                           int OW, int PH, int PW, int act, cudaStream_t s,
+                           bool *handled, int tw_req = 0, int th_req = 0) {
+  *handled = false;
+  constexpr int PIX = 4;
+  if (reinterpret_cast<uintptr_t>(x) & 15)
+    return cudaSuccess;
+  const DwTile t = pick_dw_tile(C, OH, OW, KH, KW, SH, SW, PIX, tw_req, th_req);
+  if (!t.CB || t.smem > 200 * 1024)
+    return cudaSuccess;
+  const int chunks = C / t.CB;
+  const long long blocks =
+      static_cast<long long>(batch) * t.tiles_h * t.tiles_w * chunks;
+  if (blocks >= (1LL << 31))
+    return cudaSuccess;
+  const int twin = (t.TW - 1) * SW + KW;
+  const int rin = (t.TH - 1) * SH + KH;
+  CUtensorMap map;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(C), static_cast<cuuint64_t>(W),
+                        static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(C) * 2,
+                           static_cast<cuuint64_t>(W) * C * 2,
+                           static_cast<cuuint64_t>(H) * W * C * 2};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(t.CB), static_cast<cuuint32_t>(twin),
+                       static_cast<cuuint32_t>(rin), 1};
+  if (!encode_fp16_map(&map, x, 4, dims, strides, box, false))
+    return cudaSuccess;
+  auto kernel = act == kActRelu        ? depthwise_tile_kernel<KH, KW, SH, SW, PIX, kActRelu>
+                : act == kActHardSwish ? depthwise_tile_kernel<KH, KW, SH, SW, PIX, kActHardSwish>
+                                       : depthwise_tile_kernel<KH, KW, SH, SW, PIX, -1>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(t.smem));
+  if (e != cudaSuccess)
+    return e;
+  *handled = true;
+  kernel<<<static_cast<unsigned>(blocks), t.threads, t.smem, s>>>(
+      map, w, bias, y, C, H, OH, OW, PH, PW, t.CB, t.TH, t.TW, t.tiles_h,
+      t.tiles_w, chunks, act, device_error_word());
+  return cudaGetLastError();
+}
+
 template <int KH, int KW, int SH, int SW>
 cudaError_t launch_dw(const half *x, const half *w, const half *bias, half *y,
                       int batch, int C, int H, int W, int OH, int OW, int PH,
@@ -1031,9 +1249,13 @@ cudaError_t depthwise(const half *x, const half *w, const half *bias, half *y,
 #define PB2_DW(kh, kw, sh, sw)                                                 \
   if (KH == kh && KW == kw && SH == sh && SW == sw) {                          \
     bool handled = false;                                                      \
-    cudaError_t e = launch_dw_tma<kh, kw, sh, sw>(x, w, bias, y, batch, C, H,  \
-                                                  W, OH, OW, PH, PW, act, s,   \
-                                                  &handled);                   \
+    cudaError_t e = launch_dw_tile<kh, kw, sh, sw>(x, w, bias, y, batch, C, H, \
+                                                   W, OH, OW, PH, PW, act, s,  \
+                                                   &handled);                  \
+    if (handled || e != cudaSuccess)                                           \
+      return e;                                                                \
+    e = launch_dw_tma<kh, kw, sh, sw>(x, w, bias, y, batch, C, H, W, OH, OW,   \
+                                      PH, PW, act, s, &handled);               \
     if (handled || e != cudaSuccess)                                           \
       return e;                                                                \
     return launch_dw<kh, kw, sh, sw>(x, w, bias, y, batch, C, H, W, OH, OW,    \
@@ -1051,6 +1273,100 @@ cudaError_t depthwise(const half *x, const half *w, const half *bias, half *y,
   depthwise_generic_kernel<<<blocks_for(total), kBlock, 0, s>>>(
       x, w, bias, y, batch, C, H, W, OH, OW, KH, KW, SH, SW, PH, PW, act);
   return cudaGetLastError();
+}
+
+// Stem on the tensor cores: a 3x3 stride-2 pad-1 convolution of a Ci <= 4
+// image equals a 2x2 stride-1 convolution (pad 1 at the top/left) of its
+// space-to-depth rearrangement: block pixel (R, C) holds the 2x2 input
+// pixels (2R + dr, 2C + dc) as channel (dr*2 + dc)*4 + c (16 channels, 32
+// bytes, zero past Ci and past the image edge). Filter tap (kh, kw) of the
+// 3x3 conv becomes tap (a, b) = ((kh + 1) / 2, (kw + 1) / 2) of the 2x2 conv
+// at sub-pixel (dr, dc) = ((kh + 1) % 2, (kw + 1) % 2).
+namespace {
+__global__ void __launch_bounds__(kBlock)
+    space_to_depth2_kernel(const half *__restrict__ x, uint4 *__restrict__ y,
+                           int Ci, int H, int W, int H2, int W2, uint32_t total,
+                           FastDiv by_w2, FastDiv by_h2) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total)
+    return;
+  const uint32_t r = by_w2.div(i);
+  const int bc = static_cast<int>(i - r * by_w2.d);
+  const uint32_t n = by_h2.div(r);
+  const int br = static_cast<int>(r - n * by_h2.d);
+  half v[16];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int row = 2 * br + (q >> 1), col = 2 * bc + (q & 1);
+    const bool in = row < H && col < W;
+    const half *px = x + ((static_cast<long long>(n) * H + row) * W + col) * Ci;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      v[q * 4 + c] = in && c < Ci ? px[c] : __float2half_rn(0.f);
+  }
+  const uint4 *vv = reinterpret_cast<const uint4 *>(v);
+  y[2ull * i] = vv[0];
+  y[2ull * i + 1] = vv[1];
+}
+
+__global__ void __launch_bounds__(kBlock)
+    stem_s2d_pack_kernel(const half *__restrict__ w, half *__restrict__ wp,
+                         int Co, int Ci) {
+  // wp [Co][2][2][16] from w [Co][3][3][Ci] (OHWI)
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= Co * 64)
+    return;
+  const int co = i / 64, rem = i % 64;
+  const int tap = rem / 16, ch = rem % 16;
+  const int a = tap >> 1, b = tap & 1, q = ch >> 2, c = ch & 3;
+  const int dr = q >> 1, dc = q & 1;
+  const int kh = 2 * a + dr - 1, kw = 2 * b + dc - 1;
+  const bool ok = kh >= 0 && kh < 3 && kw >= 0 && kw < 3 && c < Ci;
+  wp[i] = ok ? w[((static_cast<long long>(co) * 3 + kh) * 3 + kw) * Ci + c]
+             : __float2half_rn(0.f);
+}
+
+} // namespace
+
+cudaError_t stem_s2d_pack(const half *w, half *wp, int Co, int Ci,
+                          cudaStream_t s) {
+  if (Co <= 0 || Ci <= 0 || Ci > 4)
+    return cudaErrorInvalidValue;
+  stem_s2d_pack_kernel<<<blocks_for(static_cast<long long>(Co) * 64), kBlock, 0, s>>>(
+      w, wp, Co, Ci);
+  return cudaGetLastError();
+}
+
+size_t stem_s2d_scratch_bytes(int batch, int H, int W) {
+  return static_cast<size_t>(batch) * ((H + 1) / 2) * ((W + 1) / 2) * 32;
+}
+
+cudaError_t stem_conv_s2d(const half *x, const half *wp, const half *bias,
+                          half *y, half *scratch, int batch, int Ci, int H,
+                          int W, int Co, int act, cudaStream_t s) {
+  if (batch <= 0 || H <= 0 || W <= 0)
+    return cudaSuccess;
+  if (Ci <= 0 || Ci > 4 || Co % 8 || !al16(scratch) || !al16(wp))
+    return cudaErrorInvalidValue;
+  const int H2 = (H + 1) / 2, W2 = (W + 1) / 2;
+  const long long total = static_cast<long long>(batch) * H2 * W2;
+  if (total >= (1LL << 31))
+    return cudaErrorInvalidValue;
+  space_to_depth2_kernel<<<blocks_for(total), kBlock, 0, s>>>(
+      x, reinterpret_cast<uint4 *>(scratch), Ci, H, W, H2, W2,
+      static_cast<uint32_t>(total), FastDiv(W2), FastDiv(H2));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return e;
+  GemmEpilogue epi;
+  epi.bias = bias;
+  epi.out = y;
+  epi.ldo = Co;
+  epi.act = act;
+  ConvShape cs{batch, H2, W2, 16, Co, 2, 2, 1, 1};
+  cs.out_h = H2;
+  cs.out_w = W2;
+  return tc_conv(scratch, wp, cs, epi, s);
 }
 
 cudaError_t direct_conv(const half *x, const half *w, const half *bias,

@@ -851,16 +851,18 @@ cudaError_t tc_gemm(const half *A, int M, int K, int lda, const half *W, int N,
 
 cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
                     const GemmEpilogue &epi, cudaStream_t stream) {
-  const int OH = s.H + 2 * s.pad_h - s.KH + 1;
-  const int OW = s.W + 2 * s.pad_w - s.KW + 1;
+  const int OH = s.out_h ? s.out_h : s.H + 2 * s.pad_h - s.KH + 1;
+  const int OW = s.out_w ? s.out_w : s.W + 2 * s.pad_w - s.KW + 1;
   if (s.batch <= 0 || OH <= 0 || OW <= 0)
     return cudaSuccess;
+  if (OH > s.H + 2 * s.pad_h - s.KH + 1 || OW > s.W + 2 * s.pad_w - s.KW + 1)
+    return cudaErrorInvalidValue;
   if (s.Ci % 8 || s.Co % 8 || epi.ldo % 8 || !aligned16(x) || !aligned16(w) ||
       !aligned16(epi.out) || (epi.bias && !aligned16(epi.bias)) ||
       (epi.residual && (!aligned16(epi.residual) || epi.ldr % 8)) ||
       s.KH * s.KW > 256)
     return cudaErrorInvalidValue;
-  const int bn = pick_bn(s.Co);
+  int bn = pick_bn(s.Co);
   const int taps = s.KH * s.KW;
   // Segment length: 32 pixels when it divides the output width (fewer TMA
   // boxes per stage), else 16.
@@ -880,11 +882,19 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
     if ((2 * kBM / len) * len * 8 >= 7 * 2 * kBM)
       seg_len = len;
   }
+  // Co = 48 with whole-row segments runs as 64-wide tiles of 256 rows: the
+  // extra 16 columns cost idle MMA cycles, but a 256-row tile needs 3-4 TMA
+  // boxes per k-block where 128-row tiles of 16-pixel segments need 9 (the
+  // single producer thread was the limit); columns past Co are neither
+  // loaded (zero-filled weights) nor stored.
+  if (bn == 48 && seg_len)
+    bn = 64;
   int row_segs = 0;
   bool two = false;
   // Measured on B200: 256x256 tiles for long K at N >= 256; 256x128 and
-  // 256x64 tiles for N of 128 / 64; N = 48 and short-K N >= 256 layers keep
-  // 128-row tiles of 16/32-pixel segments.
+  // 256x64 tiles for N of 128 / 64 (and 48, above); short-K N >= 256 layers
+  // and widths without a long segment keep 128-row tiles of 16/32-pixel
+  // segments.
   if (seg_len && ((bn == 256 && num_kb >= 16) || bn == 128 || bn == 64)) {
     const long long segs = static_cast<long long>(s.batch) * OH * (OW / seg_len);
     const int per_tile = 2 * kBM / seg_len;

@@ -41,6 +41,9 @@ SIGNATURES = {
     "ppocr_b200_logits_argmax_prob": (I, [V, I, I, V, V, V, I, V]),
     "ppocr_b200_ctc_collapse": (I, [V, V, I, I, I, V, V, V, V]),
     "ppocr_b200_conv_nhwc": (I, [V, V, V, V, I, I, I, I, I, I, I, I, I, I, I, I, I, V]),
+    "ppocr_b200_stem_s2d_pack": (I, [V, V, I, I, V]),
+    "ppocr_b200_stem_s2d_scratch_bytes": (S, [I, I, I]),
+    "ppocr_b200_stem_conv_s2d": (I, [V, V, V, V, V, I, I, I, I, I, I, V]),
     "ppocr_b200_gemm_epilogue": (I, [V, V, V, V, V, I, I, I, I, V]),
     "ppocr_b200_matmul": (I, [V, V, V, I, I, I, I, V]),
     "ppocr_b200_layernorm": (I, [V, V, V, V, I, I, F, V]),

@@ -125,6 +125,34 @@ def test_stem_direct_conv(native, cuda, batch, h, w, co):
     assert_close(host(y), want, what="stem")
 
 
+@pytest.mark.parametrize("batch,h,w,ci,co,act", [(2, 48, 320, 3, 48, 1), (1, 9, 35, 3, 48, 1),
+                                                 (3, 10, 12, 3, 32, 0), (1, 7, 8, 1, 64, 1),
+                                                 (40, 48, 320, 3, 48, 1)])
+def test_stem_space_to_depth(native, cuda, batch, h, w, ci, co, act):
+    """Stem 3x3 stride-2 pad-1 conv on the tensor cores through the
+    space-to-depth image (odd heights/widths leave zero sub-pixels; 40 lines
+    are enough for 256-row tiles)."""
+    r = rng(5 + w + ci)
+    x = f16(r.uniform(-1, 1, (batch, h, w, ci)))
+    wt = f16(r.standard_normal((co, 3, 3, ci)) * np.sqrt(2.0 / (9 * ci)))
+    b = f16(r.normal(0, 0.1, co))
+    oh, ow = (h + 1) // 2, (w + 1) // 2
+    y = torch.empty(batch, oh, ow, co, dtype=torch.float16, device=cuda)
+    wp = torch.empty(co * 64, dtype=torch.float16, device=cuda)
+    nbytes = native.ppocr_b200_stem_s2d_scratch_bytes(batch, h, w)
+    assert nbytes == batch * oh * ow * 32
+    scratch = torch.empty(nbytes // 2, dtype=torch.float16, device=cuda)
+    dx, dw, db = dev(x), dev(wt), dev(b)
+    assert native.ppocr_b200_stem_s2d_pack(ptr(dw), ptr(wp), co, ci, stream_handle()) == 0
+    rc = native.ppocr_b200_stem_conv_s2d(ptr(dx), ptr(wp), ptr(db), ptr(y), ptr(scratch), batch, ci, h, w, co,
+                                         act, stream_handle())
+    assert rc == 0, native.ppocr_b200_last_error()
+    sync()
+    check_device_error(native)
+    want = L.conv_nhwc(x, wt, b, (2, 2), (1, 1), 1, act)
+    assert_close(host(y), want, what=f"stem s2d {batch}x{h}x{w}x{ci}->{co}")
+
+
 # ------------------------------------------------------------ depthwise
 DW_CASES = [
     # batch, h, w, c, kh, kw, sh, sw, act
@@ -311,12 +339,15 @@ def test_logits_argmax_and_collapse(native, cuda, oracle_c):
 
 
 @pytest.mark.parametrize("rows,V,offset", [(3, 5, 0), (7, 1, 0), (64, 300, 0), (64, 300, 1),
-                                           (40, 18385, 1), (33, 4099, 0), (6, 40001, 0), (5, 40001, 3)])
+                                           (40, 18385, 1), (33, 4099, 0), (6, 40001, 0), (5, 40001, 3),
+                                           (9, 4088, 1), (5, 8185, 3), (7, 18424, 1), (4, 20473, 0),
+                                           (3, 32760, 5), (3, 32761, 0)])
 def test_logits_argmax_shapes(native, cuda, oracle_c, rows, V, offset):
     """Edge cases: rows shorter than one 16-byte vector, odd vocabularies
     (rows start at any 2-byte offset), base pointers that are not 16-byte
-    aligned, ties (repeated maxima), and vocabularies past the cluster form's
-    8 x 4088 columns (shared-memory staged and register forms)."""
+    aligned, ties (repeated maxima), vocabularies at both sides of each
+    register-resident row form's capacity, and vocabularies past the largest
+    one (the looping register form)."""
     r = rng(30 + V + offset)
     logits = r.standard_normal((rows, V)).astype(np.float16)
     logits[::3, V // 2] = 8.0
