@@ -3,6 +3,7 @@
 // (include/ppocr_b200_ops.h). Thin argument checks + kernels.h launchers.
 #include "../../include/ppocr_b200_head.h"
 #include "../../include/ppocr_b200_ops.h"
+#include "../../include/ppocr_b200_preprocess.h"
 #include "kernels.h"
 #include <mutex>
 #include <string>
@@ -408,6 +409,80 @@ int ppocr_b200_binarize(const float *prob, uint8_t *map, size_t n, float thresh,
   if (!prob || !map)
     return fail("invalid binarize arguments");
   return status(binarize(prob, map, n, thresh, stream), "binarize");
+}
+
+int ppocr_b200_detector_preprocess(const void *src, size_t src_step,
+                                   int src_rows, int src_cols,
+                                   size_t src_image_bytes, int images,
+                                   void *dst, int dst_h, int dst_w,
+                                   int content_h, int content_w,
+                                   int source_is_bgr, int format,
+                                   cudaStream_t stream) {
+  g_error.clear();
+  if (content_h <= 0 || content_w <= 0 || content_h > dst_h ||
+      content_w > dst_w || src == nullptr || src_rows <= 0 || src_cols <= 0 ||
+      src_step < static_cast<size_t>(src_cols) * 3 || dst == nullptr ||
+      dst_h <= 0 || dst_w <= 0 || images < 0 ||
+      (images > 1 && src_image_bytes < src_step * src_rows) ||
+      (format != PPOCR_B200_PREP_F32_NCHW && format != PPOCR_B200_PREP_F16_NHWC))
+    return fail("invalid detector preprocess arguments");
+  return status(detector_preprocess(static_cast<const uint8_t *>(src), src_rows,
+                                    src_cols, static_cast<long long>(src_step),
+                                    static_cast<long long>(src_image_bytes),
+                                    images, dst, dst_h, dst_w, content_h,
+                                    content_w, source_is_bgr ? 1 : 0, format,
+                                    stream),
+                "detector preprocess");
+}
+
+int ppocr_b200_resize_normalize_detector_padded(
+    const void *src, size_t src_step, int src_rows, int src_cols,
+    float *dst_nchw, int dst_h, int dst_w, int content_h, int content_w,
+    int source_is_bgr, cudaStream_t stream) {
+  return ppocr_b200_detector_preprocess(src, src_step, src_rows, src_cols, 0, 1,
+                                        dst_nchw, dst_h, dst_w, content_h,
+                                        content_w, source_is_bgr,
+                                        PPOCR_B200_PREP_F32_NCHW, stream);
+}
+
+int ppocr_b200_resize_normalize_detector(const void *src, size_t src_step,
+                                         int src_rows, int src_cols,
+                                         float *dst_nchw, int dst_h, int dst_w,
+                                         int source_is_bgr,
+                                         cudaStream_t stream) {
+  return ppocr_b200_resize_normalize_detector_padded(
+      src, src_step, src_rows, src_cols, dst_nchw, dst_h, dst_w, dst_h, dst_w,
+      source_is_bgr, stream);
+}
+
+int ppocr_b200_roi_warp(const void *src, size_t src_step, int src_rows,
+                        int src_cols, const float *d_m_invs,
+                        const int *d_crop_widths, void *dst, int batch,
+                        int dst_h, int dst_w, int output_bgr, int format,
+                        cudaStream_t stream) {
+  g_error.clear();
+  if (batch <= 0)
+    return 0;
+  if (src == nullptr || src_rows <= 0 || src_cols <= 0 ||
+      src_step < static_cast<size_t>(src_cols) * 3 || !d_m_invs ||
+      !d_crop_widths || !dst || dst_h < 0 || dst_w < 0 ||
+      (format != PPOCR_B200_PREP_F32_NCHW && format != PPOCR_B200_PREP_F16_NHWC))
+    return fail("invalid roi warp arguments");
+  return status(roi_warp(static_cast<const uint8_t *>(src), src_rows, src_cols,
+                         static_cast<long long>(src_step), d_m_invs,
+                         d_crop_widths, dst, batch, dst_h, dst_w,
+                         output_bgr ? 1 : 0, format, stream),
+                "roi warp");
+}
+
+int ppocr_b200_batch_roi_warp(const void *src, size_t src_step, int src_rows,
+                              int src_cols, const float *d_m_invs,
+                              const int *d_crop_widths, float *d_dst_batch,
+                              int batch, int dst_h, int dst_w, int output_bgr,
+                              cudaStream_t stream) {
+  return ppocr_b200_roi_warp(src, src_step, src_rows, src_cols, d_m_invs,
+                             d_crop_widths, d_dst_batch, batch, dst_h, dst_w,
+                             output_bgr, PPOCR_B200_PREP_F32_NCHW, stream);
 }
 
 int ppocr_b200_device_free(void *p) {

@@ -218,4 +218,26 @@ cudaError_t deconv_kxk(const half *x, const half *w, const half *bias, half *y,
                        int batch, int H, int W, int Ci, int Co, int KH, int KW,
                        int act, cudaStream_t stream);
 
+// -------------------------------------------------- page / line preprocess
+// Output formats of the preprocessing kernels.
+enum PrepFormat { PREP_F32_NCHW = 0, PREP_F16_NHWC = 1 };
+// Detector resize + normalize of `images` u8 HWC (3-channel) pages, each
+// src_h x src_w with row pitch src_step bytes, image i at
+// src + i * src_image_bytes, into [images][3][dst_h][dst_w] f32 or
+// [images][dst_h][dst_w][3] fp16; content_h x content_w is the resized
+// page's rectangle, the rest of the canvas is white.
+cudaError_t detector_preprocess(const uint8_t *src, int src_h, int src_w,
+                                long long src_step, long long src_image_bytes,
+                                int images, void *dst, int dst_h, int dst_w,
+                                int content_h, int content_w, int source_is_bgr,
+                                int fmt, cudaStream_t stream);
+// Batched perspective ROI warp of one u8 HWC page: crop b samples the page
+// at m_invs[9b..9b+8] (inverse homography, row-major 3x3) for x <
+// crop_widths[b]; [batch][3][dst_h][dst_w] f32 or [batch][dst_h][dst_w][3]
+// fp16, values v/127.5 - 1.
+cudaError_t roi_warp(const uint8_t *src, int src_h, int src_w, long long src_step,
+                     const float *m_invs, const int *crop_widths, void *dst,
+                     int batch, int dst_h, int dst_w, int out_bgr, int fmt,
+                     cudaStream_t stream);
+
 } // namespace pb2

@@ -30,7 +30,8 @@ COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
           "-Xcompiler", "-fvisibility=default", "--expt-relaxed-constexpr"]
 
 LIB_SOURCES = ["common.cu", "tc_gemm.cu", "spatial.cu", "seq.cu", "head.cu",
-               "detect.cu", "runtime.cu", "capi.cu", "head_noalloc.cu"]
+               "detect.cu", "preprocess.cu", "runtime.cu", "capi.cu",
+               "head_noalloc.cu"]
 
 
 def _run(cmd: list[str]) -> None:

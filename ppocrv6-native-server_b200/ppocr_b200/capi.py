@@ -25,8 +25,8 @@ def lib_path() -> Path:
     return LIB_DIR / "libppocr_b200.so"
 
 
-# (name, restype, argtypes) for every function in include/ppocr_b200_head.h
-# and include/ppocr_b200_ops.h.
+# (name, restype, argtypes) for every function in include/ppocr_b200_head.h,
+# include/ppocr_b200_ops.h and include/ppocr_b200_preprocess.h.
 V, I, F, S, L = c_void_p, c_int, c_float, c_size_t, c_longlong
 PI, PF = POINTER(c_int), POINTER(c_float)
 SIGNATURES = {
@@ -62,7 +62,14 @@ SIGNATURES = {
     "ppocr_b200_device_free": (I, [V]),
     "ppocr_b200_f32_to_f16": (I, [V, V, S, S, V]),
     "ppocr_b200_f16_to_f32": (I, [V, V, S, V]),
+    # include/ppocr_b200_preprocess.h
+    "ppocr_b200_resize_normalize_detector_padded": (I, [V, S, I, I, V, I, I, I, I, I, V]),
+    "ppocr_b200_resize_normalize_detector": (I, [V, S, I, I, V, I, I, I, V]),
+    "ppocr_b200_detector_preprocess": (I, [V, S, I, I, S, I, V, I, I, I, I, I, I, V]),
+    "ppocr_b200_batch_roi_warp": (I, [V, S, I, I, V, V, V, I, I, I, I, V]),
+    "ppocr_b200_roi_warp": (I, [V, S, I, I, V, V, V, I, I, I, I, I, V]),
 }
+PREP_F32_NCHW, PREP_F16_NHWC = 0, 1
 
 MODEL_SIGNATURES = {
     "ppocr_model_info": (c_void_p, []),
