@@ -49,9 +49,10 @@ def parse():
     p.add_argument("--model", default=MODEL, choices=["rec_b512", "rec_b256", "rec_b64"],
                    help="compiled recognizer shape of the c4 run (rec_b512 = the benchmark; the smaller "
                         "shapes exist for profiling captures and are named in the output's config)")
-    p.add_argument("--config", default="c4", choices=["c1", "c2", "c3", "c4", "c5"],
+    p.add_argument("--config", default="c4", choices=["c1", "c2", "c3", "c4", "c5", "pre"],
                    help="c4 (default) is the headline recognizer benchmark; c1/c2/c3/c5 measure the other "
-                        "BASELINE configurations (CTC head, conv block, neck, page pipeline) on one GPU")
+                        "BASELINE configurations (CTC head, conv block, neck, page pipeline) on one GPU; pre "
+                        "measures the page preprocessing (detector resize/normalize, batched ROI warp)")
     return p.parse_args()
 
 
@@ -431,6 +432,8 @@ CONFIGS = {
     "c3": ("neck lines/sec (C3: SVTR neck, 2 blocks, [256,40,120] FP16)", "lines/s", True),
     "c5": ("page p50 latency ms @960^2 (C5: 8 pages -> detector + binarize, 512 line crops -> recognizer)",
            "ms", False),
+    "pre": ("preprocessed pages/sec (8 decoded 1080x1920 u8 pages -> 960^2 FP16 NHWC detector input, and 64 "
+            "48x320 FP16 NHWC line crops per page by perspective ROI warp)", "pages/s", True),
 }
 
 
@@ -633,6 +636,83 @@ def config_arm(args):
                     if args.config == "c2" else
                     "BASELINE config 3: SVTR neck (2 x [LN -> 8-head MHSA dh 15 -> residual -> LN -> MLP "
                     "120-240-120 swish -> residual]) on FP16 [256,40,120] through the Model ABI v2 shell")
+    elif args.config == "pre":
+        pages = 8
+        src_np = workloads.source_pages(r, pages)
+        sh, sw = src_np.shape[1:3]
+        boxes = [workloads.line_boxes(r, workloads.LINES_PER_PAGE, sh, sw) for _ in range(pages)]
+        src_h = torch.from_numpy(src_np).pin_memory()
+        src = src_h.to(dev)
+        m_invs = torch.from_numpy(np.stack([b[0] for b in boxes])).to(dev)  # [pages, 64, 9]
+        widths = torch.from_numpy(np.stack([b[1] for b in boxes])).to(dev)  # [pages, 64]
+        # aspect-preserving content rectangle on a 960 x 960 canvas
+        S = workloads.PAGE
+        ch, cw = (S * sh // sw, S) if sw >= sh else (S, S * sw // sh)
+        det_in = torch.empty(pages, S, S, 3, dtype=torch.float16, device=dev)
+        crops = torch.empty(pages * workloads.LINES_PER_PAGE, H, W, 3, dtype=torch.float16, device=dev)
+        stream = torch.cuda.Stream(dev)
+        s = ctypes.c_void_p(stream.cuda_stream)
+        page_bytes = sh * sw * 3
+        nb = workloads.LINES_PER_PAGE
+        crop_elems = nb * H * W * 3
+        dev_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(args.steps)]
+        warp_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(args.steps)]
+
+        def prep(i=None, source=src):
+            if i is not None:
+                dev_ev[i][0].record(stream)
+            capi.check(lib.ppocr_b200_detector_preprocess(P(source), sw * 3, sh, sw, page_bytes, pages, P(det_in),
+                                                          S, S, ch, cw, 0, capi.PREP_F16_NHWC, s))
+            if i is not None:
+                dev_ev[i][1].record(stream)
+                warp_ev[i][0].record(stream)
+            for p in range(pages):
+                capi.check(lib.ppocr_b200_roi_warp(
+                    ctypes.c_void_p(source.data_ptr() + p * page_bytes), sw * 3, sh, sw,
+                    ctypes.c_void_p(m_invs.data_ptr() + p * nb * 36), ctypes.c_void_p(widths.data_ptr() + p * nb * 4),
+                    ctypes.c_void_p(crops.data_ptr() + p * crop_elems * 2), nb, H, W, 0, capi.PREP_F16_NHWC, s))
+            if i is not None:
+                warp_ev[i][1].record(stream)
+
+        for _ in range(warm):
+            prep()
+        stream.synchronize()
+        with ClockSampler(local) as clocks:
+            step_ms = _event_steps(stream, args.steps, prep, flush)
+        det_ms = statistics.mean(a.elapsed_time(b) for a, b in dev_ev)
+        warp_ms = statistics.mean(a.elapsed_time(b) for a, b in warp_ev)
+        stage = torch.empty_like(src)
+        det_h = torch.empty_like(det_in, device="cpu").pin_memory()
+        crops_h = torch.empty_like(crops, device="cpu").pin_memory()
+
+        def e2e_body(i):
+            with torch.cuda.stream(stream):
+                stage.copy_(src_h, non_blocking=True)
+            prep(source=stage)
+            with torch.cuda.stream(stream):
+                det_h.copy_(det_in, non_blocking=True)
+                crops_h.copy_(crops, non_blocking=True)
+
+        e2e_ms = _event_steps(stream, args.steps, e2e_body, None)
+        h2d = src_h.numel()
+        d2h = (det_h.numel() + crops_h.numel()) * 2
+        det_bytes = pages * page_bytes + det_in.numel() * 2.0
+        roof = _roofline_for("hbm", det_ms, det_bytes, None, "pre:detector_preprocess", peak_tf, peak_hbm,
+                             peak_kind)
+        warp_bytes = crops.numel() * 2.0 + pages * page_bytes
+        extra["roi_warp"] = _roofline_for("hbm", warp_ms, warp_bytes, None, "pre:roi_warp x8 (one per page)",
+                                          peak_tf, peak_hbm, peak_kind)
+        extra["roi_warp"]["algorithmic"] = "FP16 NHWC crops written + each source page read once"
+        roof["algorithmic"] = "u8 pages read once + FP16 NHWC canvases written"
+        launches = 1 + pages
+        units = pages
+        cpu = _cpu_pre(src_np[0], boxes[0], ch, cw)
+        workload = ("page preprocessing (reference full_page_worker.cpp:345-349, 467-471): 8 decoded u8 RGB "
+                    "1080x1920 pages -> detector resize + normalize into a 960x960 canvas (content 540x960) as "
+                    "FP16 NHWC, and 64 synthetic rotated line boxes per page -> perspective ROI warp to 48x320 "
+                    "FP16 NHWC crops (v/127.5 - 1)")
     else:  # c5
         pp = pipeline.PagePipeline(device=dev)
         pages_np, crops_np = workloads.c5_pages(r)
@@ -797,6 +877,23 @@ def _cpu_graph(name: str, units: int):
             "sample": f"{sample} of the {units} {unit.split('/')[0]} per call, median of {len(times)} calls "
                       f"(oracle torch-CPU fp32 restatement of the same graph and weights; the reference has no "
                       f"CPU layer path)"}
+
+
+def _cpu_pre(page, boxes, ch, cw):
+    """The oracle's numpy restatement of one page's preprocessing (detector
+    canvas + its 64 crops) on the host, scaled to the 8 pages of a step."""
+    import numpy as np
+
+    from oracle import preprocess as OP
+
+    m, widths = boxes
+    t0 = time.perf_counter()
+    OP.detector_preprocess(page, 960, 960, ch, cw, False)
+    OP.roi_warp(page, m, widths, H, W, False)
+    dt = time.perf_counter() - t0
+    return {"value": round(1.0 / dt, 3), "unit": "pages/s", "cores": 1, "kind": "port",
+            "sample": f"1 page + its 64 crops through oracle/preprocess.py (numpy float32, {dt * 1e3:.0f} ms); "
+                      "the reference's preprocessing exists only as CUDA kernels"}
 
 
 def _cpu_c5():

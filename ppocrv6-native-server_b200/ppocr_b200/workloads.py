@@ -4,7 +4,9 @@ No public dataset is involved: each generator draws the shapes and value
 distributions the configuration names (NumPy PCG64, seed given by the
 caller). C1 is the CTC head on materialised logits, C2 the depthwise-
 separable NHWC block, C3 the SVTR neck, C4 the full recognizer, C5 the page
-pipeline (detector + binarize + recognizer on 64 line crops per page).
+pipeline (detector + binarize + recognizer on 64 line crops per page). The
+preprocessing workload (decoded u8 pages and per-crop inverse homographies)
+feeds the device detector resize/normalize and the batched ROI warp.
 """
 
 from __future__ import annotations
@@ -61,3 +63,45 @@ def c5_pages(r: np.random.Generator, pages: int = 8, size: int = PAGE):
     [pages * 64, 48, 320, 3]); both ~ U(-1, 1)."""
     return (uniform_nhwc(r, (pages, size, size, 3)),
             uniform_nhwc(r, (pages * LINES_PER_PAGE, LINE_H, LINE_W, 3)))
+
+
+SOURCE_H, SOURCE_W = 1080, 1920  # decoded page size of the preprocessing workload
+
+
+def source_pages(r: np.random.Generator, pages: int = 8, h: int = SOURCE_H, w: int = SOURCE_W) -> np.ndarray:
+    """Decoded u8 RGB pages [pages, h, w, 3], uniform bytes."""
+    return r.integers(0, 256, (pages, h, w, 3), dtype=np.uint8)
+
+
+def _inverse_homography(quad: np.ndarray, crop_w: int, crop_h: int) -> np.ndarray:
+    """Row-major 3x3 map from crop pixel (x, y) to page coordinates for the
+    quadrilateral `quad` (4 corners clockwise from top-left), solved from the
+    four corner correspondences (the quantity the reference's host computes
+    in compute_crop_transform, native/include/ppocrv6_native/common/
+    perspective.h:50-83)."""
+    dst = np.array([[0, 0], [crop_w - 1, 0], [crop_w - 1, crop_h - 1], [0, crop_h - 1]], np.float64)
+    A, rhs = [], []
+    for (x, y), (u, v) in zip(dst, np.asarray(quad, np.float64)):
+        A += [[x, y, 1, 0, 0, 0, -u * x, -u * y], [0, 0, 0, x, y, 1, -v * x, -v * y]]
+        rhs += [u, v]
+    return np.append(np.linalg.solve(np.array(A), np.array(rhs)), 1.0).astype(np.float32)
+
+
+def line_boxes(r: np.random.Generator, n: int, page_h: int, page_w: int, crop_h: int = LINE_H,
+               bucket_w: int = LINE_W):
+    """n synthetic text-line quadrilaterals on a page (widths 60-600 px,
+    heights 16-48 px, rotated up to +-15 degrees, corners jittered), returned
+    as (m_invs float32 [n, 9], crop_widths int32 [n]) for a crop_h x bucket_w
+    crop: crop width = min(bucket, ceil(crop_h * width / height))."""
+    m, widths = [], []
+    for _ in range(n):
+        wq, hq = r.uniform(60, 600), r.uniform(16, 48)
+        cx, cy = r.uniform(0, page_w - wq), r.uniform(0, page_h - hq)
+        a = np.deg2rad(r.uniform(-15, 15))
+        c, s = np.cos(a), np.sin(a)
+        quad = np.array([[cx + c * dx - s * dy, cy + s * dx + c * dy]
+                         for dx, dy in ((0, 0), (wq, 0), (wq, hq), (0, hq))]) + r.normal(0, 1.5, (4, 2))
+        cw = min(bucket_w, max(1, int(np.ceil(crop_h * wq / hq))))
+        m.append(_inverse_homography(quad, cw, crop_h))
+        widths.append(cw)
+    return np.stack(m), np.array(widths, np.int32)
