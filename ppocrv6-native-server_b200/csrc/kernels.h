@@ -46,6 +46,14 @@ struct ConvShape {
 };
 cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
                     const GemmEpilogue &epi, cudaStream_t stream);
+// Few-channel form of tc_conv (3x3, pad 1, stride 1, Ci a multiple of 16 up
+// to 64, Co a multiple of 16 up to 128, no residual): each input pixel is
+// staged in shared memory once per slab of output rows and read by all nine
+// taps through shifted UMMA descriptors. tc_conv routes such layers here;
+// returns cudaErrorNotSupported for other shapes.
+bool halo_conv_supported(const ConvShape &s, const GemmEpilogue &epi);
+cudaError_t halo_conv(const half *x, const half *w, const ConvShape &s,
+                      const GemmEpilogue &epi, cudaStream_t stream);
 
 // Transposed convolution with kernel == stride (no padding) on the tensor
 // cores, Co a multiple of 64: a 1x1 implicit GEMM over the input pixels with

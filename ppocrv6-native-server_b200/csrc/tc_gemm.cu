@@ -862,6 +862,11 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
       (epi.residual && (!aligned16(epi.residual) || epi.ldr % 8)) ||
       s.KH * s.KW > 256)
     return cudaErrorInvalidValue;
+  if (halo_conv_supported(s, epi)) {
+    const cudaError_t e = halo_conv(x, w, s, epi, stream);
+    if (e != cudaErrorNotSupported)
+      return e;
+  }
   int bn = pick_bn(s.Co);
   const int taps = s.KH * s.KW;
   // Segment length: 32 pixels when it divides the output width (fewer TMA

@@ -106,6 +106,32 @@ def test_implicit_conv(native, cuda, batch, h, w, ci, co, k):
     assert_close(host(y), want, what=f"conv{k}x{k} {batch}x{h}x{w}x{ci}->{co}")
 
 
+HALO_CASES = [
+    # batch, h, w, ci, co, act: few-channel 3x3 convs staged as halo slabs
+    (3, 11, 37, 16, 32, 2),     # Ci 16, N tile 48 for Co 32, runtime activation switch (GELU)
+    (2, 5, 200, 32, 80, 0),     # Co 80 in a 128-wide tile, no activation, width in column blocks
+    (1, 40, 33, 64, 112, 1),    # Ci 64, partial row blocks
+    (5, 1, 300, 48, 48, 1),     # single-row images
+]
+
+
+@pytest.mark.parametrize("batch,h,w,ci,co,act", HALO_CASES)
+def test_halo_conv(native, cuda, batch, h, w, ci, co, act):
+    r = rng(500 + batch + h + w + ci + co)
+    x = f16(r.uniform(-1, 1, (batch, h, w, ci)))
+    wt = f16(r.standard_normal((co, 3, 3, ci)) * np.sqrt(2.0 / (ci * 9)))
+    b = f16(r.normal(0, 0.1, co))
+    y = torch.full((batch, h, w, co), float("nan"), dtype=torch.float16, device=cuda)
+    dx, dw, db = dev(x), dev(wt), dev(b)
+    rc = native.ppocr_b200_conv_nhwc(ptr(dx), ptr(dw), ptr(db), ptr(y), batch, ci, h, w, co, 3, 3,
+                                     1, 1, 1, 1, 1, act, stream_handle())
+    assert rc == 0, native.ppocr_b200_last_error()
+    sync()
+    check_device_error(native)
+    want = L.conv_nhwc(x, wt, b, (1, 1), (1, 1), 1, act)
+    assert_close(host(y), want, what=f"halo conv {batch}x{h}x{w}x{ci}->{co} act {act}")
+
+
 @pytest.mark.parametrize("batch,h,w,co", [(2, 48, 320, 48), (1, 9, 35, 48), (2, 10, 12, 32), (1, 8, 8, 64)])
 def test_stem_direct_conv(native, cuda, batch, h, w, co):
     """Stem 3x3 stride-2 conv with 3 input channels (odd output widths
