@@ -47,6 +47,20 @@ int ppocr_b200_stem_conv_s2d(const void *x, const void *wp, const void *bias,
                              int w_, int co, int activation,
                              cudaStream_t stream);
 
+// Extension: the fused depthwise-separable block that Runtime builds from a
+// same-size depthwise Runtime::conv (runtime.cuh:668-765) followed by the
+// 1x1 Runtime::gemm_epilogue (runtime.cuh:514-646) reading its output:
+// y = act_pw(x_dw . w_pw^T + b_pw), x_dw = act_dw(depthwise(x, w_dw) + b_dw)
+// rounded to fp16 as the stored intermediate would be, never written to
+// memory. x [batch][h][w][c], w_dw [c][k][k], w_pw [co][c],
+// y [batch][h][w][co]; c == 64, k in {3, 5} (stride 1, padding k/2),
+// co in {64, 128}; biases may be null (without b_dw, act_dw is not applied,
+// as in the standalone depthwise form).
+int ppocr_b200_dwpw_block(const void *x, const void *w_dw, const void *b_dw,
+                          int act_dw, const void *w_pw, const void *b_pw,
+                          int act_pw, void *y, int batch, int h, int w_,
+                          int c, int k, int co, cudaStream_t stream);
+
 // Runtime::gemm_epilogue (runtime.cuh:514-646): y[rows][co] =
 // act(x[rows][ci] . w[co][ci]^T + bias) (+ residual[rows][co]).
 int ppocr_b200_gemm_epilogue(const void *x, const void *w, const void *bias,

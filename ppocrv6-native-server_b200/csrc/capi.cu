@@ -403,6 +403,20 @@ int ppocr_b200_deconv_nhwc(const void *x, const void *w, const void *bias,
                 "deconv");
 }
 
+int ppocr_b200_dwpw_block(const void *x, const void *w_dw, const void *b_dw,
+                          int act_dw, const void *w_pw, const void *b_pw,
+                          int act_pw, void *y, int batch, int h, int w_,
+                          int c, int k, int co, cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !w_dw || !w_pw || !y || batch < 0 || h < 0 || w_ < 0)
+    return fail("invalid dwpw block arguments");
+  if (!dwpw_supported(c, k, co))
+    return fail("dwpw block supports c == 64, k in {3, 5}, co in {64, 128}");
+  return status(dwpw_block(H(x), H(w_dw), H(b_dw), act_dw, H(w_pw), H(b_pw),
+                           act_pw, Hm(y), batch, h, w_, c, k, co, stream),
+                "dwpw block");
+}
+
 int ppocr_b200_binarize(const float *prob, uint8_t *map, size_t n, float thresh,
                         cudaStream_t stream) {
   g_error.clear();

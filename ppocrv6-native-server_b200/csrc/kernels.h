@@ -83,6 +83,16 @@ cudaError_t vocab_merge(const float *part_max, const int *part_id,
                         float *prob, float *max_logit, int calc_prob,
                         cudaStream_t stream);
 
+// Fused depthwise-separable block (C == 64, K in {3, 5}, stride 1, same
+// padding; Co in {64, 128}): y = act_pw(pw(act_dw(dw(x) + bdw)) + bpw) with
+// the depthwise output kept on chip. wdw [C][K][K], wpw [Co][C] (K-major),
+// biases may be null (the depthwise activation then is not applied, as in
+// the standalone depthwise kernels).
+bool dwpw_supported(int C, int K, int Co);
+cudaError_t dwpw_block(const half *x, const half *wdw, const half *bdw, int act_dw, const half *wpw,
+                       const half *bpw, int act_pw, half *y, int B, int H, int W, int C, int K, int Co,
+                       cudaStream_t stream);
+
 // NHWC convolution dispatcher used by Runtime::conv and the C entry point
 // (depthwise / 1x1 GEMM / implicit GEMM / direct). Weights OHWI.
 cudaError_t conv_nhwc(const half *x, const half *w, const half *bias, half *y,

@@ -58,6 +58,7 @@ struct Instance {
     r.workspace = static_cast<unsigned char *>(scratch) + kArenaBytes;
     r.workspace_bytes = Runtime::workspace_limit;
     build_model(r);
+    r.reads({OUTPUT_ID}); // the output leaves through the ABI
     // Input staging writes the channels-last input directly when the graph
     // opens with the exporter's NCHW->NHWC transpose of tensor 0.
     if (r.input_nhwc_id >= 0)

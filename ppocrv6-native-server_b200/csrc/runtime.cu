@@ -73,6 +73,30 @@ void Runtime::add(const char *name, std::function<void()> f) {
   op_names.resize(ops.size());
   op_names.emplace_back(name);
   ops.push_back(std::move(f));
+  last_dw_.op = -1;
+}
+
+void Runtime::reads(std::initializer_list<int> ids) {
+  for (size_t i = 0; i < fused_.size();) {
+    bool hit = false;
+    for (int id : ids)
+      hit |= id >= 0 && id == fused_[i].virt;
+    if (!hit) {
+      ++i;
+      continue;
+    }
+    // Split: the depthwise launch (writing its output) then the GEMM.
+    const FusedDw f = fused_[i];
+    fused_.erase(fused_.begin() + static_cast<long>(i));
+    op_names.resize(ops.size());
+    ops[f.op] = f.dw_op;
+    op_names[f.op] = "depthwise";
+    ops.insert(ops.begin() + f.op + 1, f.pw_op);
+    op_names.insert(op_names.begin() + f.op + 1, "gemm_epilogue");
+    for (auto &g : fused_)
+      if (g.op > f.op)
+        ++g.op;
+  }
 }
 
 namespace pb2 {
@@ -148,17 +172,24 @@ void Runtime::conv(int ai, int wi, int yi, Shape xs, Shape ws, Shape ys,
                              shape_str(ws) + " groups=" +
                              std::to_string(groups) + " stride=" +
                              shape_str(stride));
+  reads({ai, wi, bias_id});
   add(name, [=] {
     check(conv_nhwc(t[ai], t[wi], bias_id >= 0 ? t[bias_id] : nullptr, t[yi],
                     B, C, H, W, Co, KH, KW, stride[0], stride[1], pad[0],
                     pad[1], groups, activation, stream),
           name);
   });
+  // A same-size depthwise conv may open a fused depthwise + pointwise block
+  // with the gemm_epilogue that follows it.
+  if (dw && KH == KW && stride == Shape{1, 1} && pad == Shape{KH / 2, KW / 2} &&
+      dwpw_supported(C, KH, 64))
+    last_dw_ = {static_cast<int>(ops.size()) - 1, ai, wi, yi, bias_id, activation, B, C, H, W, KH};
 }
 
 void Runtime::deconv(int ai, int wi, int yi, Shape xs, Shape ws, Shape ys,
                      Shape pad, Shape stride, Shape dilation,
                      bool channels_last, int bias_id, int activation) {
+  reads({ai, wi, bias_id});
   // ONNX ConvTranspose weight [Ci][Co][KH][KW], stored [Ci][KH][KW][Co] after
   // the channels-last pass.
   if (!channels_last || pad != Shape{0, 0} || dilation != Shape{1, 1} ||
@@ -199,7 +230,7 @@ void Runtime::gemm_epilogue(int ai, int wi, int bi, int ri, int yi, int rows,
                             int ci, int co, int activation) {
   if (ci % 8 || co % 8)
     throw std::runtime_error("gemm_epilogue needs ci, co multiples of 8");
-  add("gemm_epilogue", [=] {
+  auto pw = [=] {
     GemmEpilogue e;
     e.bias = bi >= 0 ? t[bi] : nullptr;
     e.residual = ri >= 0 ? t[ri] : nullptr;
@@ -208,10 +239,29 @@ void Runtime::gemm_epilogue(int ai, int wi, int bi, int ri, int yi, int rows,
     e.ldo = co;
     e.act = activation;
     check(tc_gemm(t[ai], rows, ci, ci, t[wi], co, ci, e, stream), "tc_gemm");
-  });
+  };
+  const PendingDw d = last_dw_;
+  if (d.op >= 0 && d.op == static_cast<int>(ops.size()) - 1 && ai == d.yi && ri < 0 && wi != d.yi &&
+      bi != d.yi && rows == d.B * d.H * d.W && ci == d.C && dwpw_supported(d.C, d.K, co)) {
+    // Fused depthwise + pointwise block: the depthwise output stays on chip.
+    reads({wi, bi});
+    fused_.push_back({d.op, d.yi, ops[d.op], pw});
+    ops[d.op] = [=] {
+      check(dwpw_block(t[d.ai], t[d.wi], d.bias_id >= 0 ? t[d.bias_id] : nullptr, d.act, t[wi],
+                       bi >= 0 ? t[bi] : nullptr, activation, t[yi], d.B, d.H, d.W, d.C, d.K, co, stream),
+            "dwpw_block");
+    };
+    op_names.resize(ops.size());
+    op_names[d.op] = "dwpw_block";
+    last_dw_.op = -1;
+    return;
+  }
+  reads({ai, wi, bi, ri});
+  add("gemm_epilogue", pw);
 }
 
 void Runtime::matmul(int a, int b, int y, int batches, int m, int n, int k) {
+  reads({a, b});
   // Constant right-hand side (a linear layer): re-lay [k][n] as K-major
   // [n][k] once, then run it on the tensor-core GEMM.
   if (batches == 1 && k % 8 == 0 && n % 8 == 0 && t[b] &&
@@ -240,6 +290,7 @@ void Runtime::matmul(int a, int b, int y, int batches, int m, int n, int k) {
 
 void Runtime::layernorm(int a, int scale, int bias, int y, int rows, int cols,
                         float epsilon) {
+  reads({a, scale, bias});
   add("layernorm", [=] {
     check(::pb2::layernorm(t[a], t[scale], t[bias], t[y], rows, cols, epsilon,
                            stream),
@@ -248,6 +299,7 @@ void Runtime::layernorm(int a, int scale, int bias, int y, int rows, int cols,
 }
 
 void Runtime::softmax(int a, int y, int rows, int cols) {
+  reads({a});
   add("softmax", [=] {
     check(softmax_rows(t[a], t[y], rows, cols, stream), "softmax");
   });
@@ -255,6 +307,7 @@ void Runtime::softmax(int a, int y, int rows, int cols) {
 
 void Runtime::binary(int a, int b, int y, Shape as, Shape bs, Shape ys,
                      int op) {
+  reads({a, b});
   const Gather ga = broadcast_map(as, ys), gb = broadcast_map(bs, ys);
   const long long n = count(ys);
   add("binary", [=] {
@@ -264,6 +317,7 @@ void Runtime::binary(int a, int b, int y, Shape as, Shape bs, Shape ys,
 
 void Runtime::binary_flat_op(int a, int b, int y, int n, int ad, int am,
                              int bd, int bm, int op) {
+  reads({a, b});
   add("binary_fast", [=] {
     check(binary_flat(t[a], t[b], t[y], n, ad, am, bd, bm, op, stream),
           "binary_fast");
@@ -271,12 +325,14 @@ void Runtime::binary_flat_op(int a, int b, int y, int n, int ad, int am,
 }
 
 void Runtime::unary(int a, int y, int n, int op, float alpha, float beta) {
+  reads({a});
   add("unary", [=] {
     check(::pb2::unary(t[a], t[y], n, op, alpha, beta, stream), "unary");
   });
 }
 
 void Runtime::transpose(int a, int y, Shape xs, Shape ys, Shape perm) {
+  reads({a});
   int batch = 0, rows = 0, cols = 0;
   if (xs.size() == 3 && perm == Shape{0, 2, 1}) {
     batch = xs[0], rows = xs[1], cols = xs[2];
@@ -314,6 +370,7 @@ void Runtime::transpose(int a, int y, Shape xs, Shape ys, Shape perm) {
 }
 
 void Runtime::slice(int a, int y, Shape xs, Shape ys, Shape starts) {
+  reads({a});
   if (xs.size() > 6)
     throw std::runtime_error("unsupported slice rank");
   Gather g;
@@ -330,12 +387,14 @@ void Runtime::slice(int a, int y, Shape xs, Shape ys, Shape starts) {
 }
 
 void Runtime::concat(int a, int b, int y, int rows, int na, int nb) {
+  reads({a, b});
   add("concat", [=] {
     check(concat_rows(t[a], t[b], t[y], rows, na, nb, stream), "concat");
   });
 }
 
 void Runtime::pad(int a, int y, Shape xs, Shape ys, int ph, int pw) {
+  reads({a});
   add("pad", [=] {
     check(pad_nchw(t[a], t[y], xs[0] * xs[1], xs[2], xs[3], ys[2], ys[3], ph,
                    pw, stream),
@@ -344,6 +403,7 @@ void Runtime::pad(int a, int y, Shape xs, Shape ys, int ph, int pw) {
 }
 
 void Runtime::pad_nhwc(int a, int y, Shape xs, Shape ys, int ph, int pw) {
+  reads({a});
   add("pad_nhwc", [=] {
     check(::pb2::pad_nhwc(t[a], t[y], xs[0], xs[1], xs[2], xs[3], ys[2], ys[3],
                           ph, pw, stream),
@@ -353,6 +413,7 @@ void Runtime::pad_nhwc(int a, int y, Shape xs, Shape ys, int ph, int pw) {
 
 void Runtime::pool(int a, int y, Shape xs, Shape ys, Shape k, Shape s, Shape p,
                    bool maximum) {
+  reads({a});
   add("pool", [=] {
     check(pool_nchw(t[a], t[y], xs[0] * xs[1], xs[2], xs[3], ys[2], ys[3],
                     k[0], k[1], s[0], s[1], p[0], p[1], maximum, stream),
@@ -362,6 +423,7 @@ void Runtime::pool(int a, int y, Shape xs, Shape ys, Shape k, Shape s, Shape p,
 
 void Runtime::pool_nhwc(int a, int y, Shape xs, Shape ys, Shape k, Shape s,
                         Shape p, bool maximum) {
+  reads({a});
   add("pool_nhwc", [=] {
     check(::pb2::pool_nhwc(t[a], t[y], xs[0], xs[1], xs[2], xs[3], ys[2],
                            ys[3], k[0], k[1], s[0], s[1], p[0], p[1], maximum,
@@ -371,12 +433,14 @@ void Runtime::pool_nhwc(int a, int y, Shape xs, Shape ys, Shape k, Shape s,
 }
 
 void Runtime::mean(int a, int y, int rows, int cols) {
+  reads({a});
   add("mean", [=] {
     check(mean_rows(t[a], t[y], rows, cols, stream), "mean");
   });
 }
 
 void Runtime::mean_nhwc(int a, int y, int batch, int channels, int spatial) {
+  reads({a});
   add("mean_nhwc", [=] {
     check(::pb2::mean_nhwc(t[a], t[y], batch, channels, spatial, stream),
           "mean_nhwc");
@@ -385,6 +449,7 @@ void Runtime::mean_nhwc(int a, int y, int batch, int channels, int spatial) {
 
 void Runtime::resize_nearest(int a, int y, Shape xs, Shape ys, float sh,
                              float sw) {
+  reads({a});
   add("resize_nearest", [=] {
     check(resize_nearest_nchw(t[a], t[y], xs[0] * xs[1], xs[2], xs[3], ys[2],
                               ys[3], sh, sw, stream),
@@ -394,6 +459,7 @@ void Runtime::resize_nearest(int a, int y, Shape xs, Shape ys, float sh,
 
 void Runtime::resize_nearest_nhwc(int a, int y, Shape xs, Shape ys, float sh,
                                   float sw) {
+  reads({a});
   add("resize_nearest_nhwc", [=] {
     check(::pb2::resize_nearest_nhwc(t[a], nullptr, t[y], xs[0], xs[1], xs[2],
                                      xs[3], ys[2], ys[3], sh, sw, stream),
@@ -403,6 +469,7 @@ void Runtime::resize_nearest_nhwc(int a, int y, Shape xs, Shape ys, float sh,
 
 void Runtime::resize_nearest_add_nhwc(int a, int addend, int y, Shape xs,
                                       Shape ys, float sh, float sw) {
+  reads({a, addend});
   add("resize_add_nhwc", [=] {
     check(::pb2::resize_nearest_nhwc(t[a], t[addend], t[y], xs[0], xs[1],
                                      xs[2], xs[3], ys[2], ys[3], sh, sw,
@@ -413,6 +480,7 @@ void Runtime::resize_nearest_add_nhwc(int a, int addend, int y, Shape xs,
 
 void Runtime::attention(int qkv, int y, int lines, int seq, int heads,
                         int head_dim, float scale) {
+  reads({qkv});
   add("attention", [=] {
     check(::pb2::attention(t[qkv], t[y], lines, seq, heads, head_dim, scale,
                            stream),

@@ -122,6 +122,12 @@ struct Runtime {
 
   // Runs `prepare` once, then ops[first_op..] in order on `stream`.
   void run();
+  // Declares that tensors `ids` are read after the ops recorded so far
+  // (every method calls it for its inputs; the ABI shell calls it for the
+  // model output). A depthwise conv fused into the 1x1 gemm_epilogue that
+  // consumes it does not write its output; a later reader of that tensor
+  // splits the fused op back into the two original launches.
+  void reads(std::initializer_list<int> ids);
   bool prepared = false;
   // When the graph opens with the exporter's channels-last transpose of the
   // model input (t[0] NCHW -> t[input_nhwc_id] NHWC), the ABI shell writes
@@ -130,6 +136,19 @@ struct Runtime {
   int first_op = 0;
 
 private:
+  // The depthwise conv recorded by the last add(), if it can lead a fused
+  // depthwise + pointwise block.
+  struct PendingDw {
+    int op = -1;
+    int ai, wi, yi, bias_id, act, B, C, H, W, K;
+  } last_dw_;
+  // Fused blocks whose depthwise output is not materialised.
+  struct FusedDw {
+    int op;
+    int virt; // tensor id of the depthwise output
+    std::function<void()> dw_op, pw_op;
+  };
+  std::vector<FusedDw> fused_;
   std::vector<void *> owned_; // device buffers owned by this runtime
   void *own(size_t bytes);
   bool is_constant(const Scalar *p, size_t elements) const;

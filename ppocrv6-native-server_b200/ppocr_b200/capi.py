@@ -59,6 +59,7 @@ SIGNATURES = {
     "ppocr_b200_mean_nhwc": (I, [V, V, I, I, I, V]),
     "ppocr_b200_deconv_nhwc": (I, [V, V, V, V, I, I, I, I, I, I, I, I, V]),
     "ppocr_b200_binarize": (I, [V, V, S, F, V]),
+    "ppocr_b200_dwpw_block": (I, [V, V, V, I, V, V, I, V, I, I, I, I, I, I, V]),
     "ppocr_b200_device_free": (I, [V]),
     "ppocr_b200_f32_to_f16": (I, [V, V, S, S, V]),
     "ppocr_b200_f16_to_f32": (I, [V, V, S, V]),

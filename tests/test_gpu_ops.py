@@ -132,6 +132,41 @@ def test_halo_conv(native, cuda, batch, h, w, ci, co, act):
     assert_close(host(y), want, what=f"halo conv {batch}x{h}x{w}x{ci}->{co} act {act}")
 
 
+DWPW_CASES = [
+    # batch, h, w, k, co, act_dw, act_pw, bias
+    (2, 48, 320, 5, 128, 3, 3, True),    # BASELINE config 2's block
+    (3, 7, 100, 5, 128, 3, 3, True),     # odd height, width not a multiple of 64
+    (2, 9, 30, 3, 64, 1, 1, True),       # 3x3, Co 64, ReLU
+    (1, 5, 70, 5, 64, 2, 0, False),      # no biases (depthwise activation not applied), runtime switch
+]
+
+
+@pytest.mark.parametrize("batch,h,w,k,co,act_dw,act_pw,bias", DWPW_CASES)
+def test_dwpw_block(native, cuda, batch, h, w, k, co, act_dw, act_pw, bias):
+    """Fused depthwise + pointwise block against the oracle's two separate
+    operators (depthwise in the reference's tap order, fp16-rounded
+    intermediate, then the GEMM)."""
+    r = rng(600 + h + w + k + co)
+    x = f16(r.uniform(-1, 1, (batch, h, w, 64)))
+    wd = f16(r.normal(0, 0.3, (64, k, k)))
+    bd = f16(r.normal(0, 0.1, 64)) if bias else None
+    wp = f16(r.standard_normal((co, 64)) * np.sqrt(2.0 / 64))
+    bp = f16(r.normal(0, 0.1, co)) if bias else None
+    y = torch.full((batch, h, w, co), float("nan"), dtype=torch.float16, device=cuda)
+    dx, dwd, dwp = dev(x), dev(wd), dev(wp)
+    dbd = dev(bd) if bias else None
+    dbp = dev(bp) if bias else None
+    rc = native.ppocr_b200_dwpw_block(ptr(dx), ptr(dwd), ptr(dbd) if bias else None, act_dw, ptr(dwp),
+                                      ptr(dbp) if bias else None, act_pw, ptr(y), batch, h, w, 64, k, co,
+                                      stream_handle())
+    assert rc == 0, native.ppocr_b200_last_error()
+    sync()
+    check_device_error(native)
+    mid = L.depthwise_exact(x, wd, bd if bias else torch.zeros(64), (1, 1), (k // 2, k // 2), act_dw if bias else 0)
+    want = L.gemm(mid, wp, bp, None, act_pw)
+    assert_close(host(y), want, what=f"dwpw {batch}x{h}x{w} k{k} -> {co}")
+
+
 @pytest.mark.parametrize("batch,h,w,co", [(2, 48, 320, 48), (1, 9, 35, 48), (2, 10, 12, 32), (1, 8, 8, 64)])
 def test_stem_direct_conv(native, cuda, batch, h, w, co):
     """Stem 3x3 stride-2 conv with 3 input channels (odd output widths
