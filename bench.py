@@ -49,10 +49,11 @@ def parse():
     p.add_argument("--model", default=MODEL, choices=["rec_b512", "rec_b256", "rec_b64"],
                    help="compiled recognizer shape of the c4 run (rec_b512 = the benchmark; the smaller "
                         "shapes exist for profiling captures and are named in the output's config)")
-    p.add_argument("--config", default="c4", choices=["c1", "c2", "c3", "c4", "c5", "pre"],
+    p.add_argument("--config", default="c4", choices=["c1", "c2", "c3", "c4", "c5", "pre", "post"],
                    help="c4 (default) is the headline recognizer benchmark; c1/c2/c3/c5 measure the other "
                         "BASELINE configurations (CTC head, conv block, neck, page pipeline) on one GPU; pre "
-                        "measures the page preprocessing (detector resize/normalize, batched ROI warp)")
+                        "measures the page preprocessing (detector resize/normalize, batched ROI warp); post the DB "
+                        "post-processing front end (binarize + connected components with box statistics)")
     return p.parse_args()
 
 
@@ -434,6 +435,8 @@ CONFIGS = {
            "ms", False),
     "pre": ("preprocessed pages/sec (8 decoded 1080x1920 u8 pages -> 960^2 FP16 NHWC detector input, and 64 "
             "48x320 FP16 NHWC line crops per page by perspective ROI warp)", "pages/s", True),
+    "post": ("DB post-processed pages/sec (8 FP32 probability maps 960^2 -> binarize 0.3 -> 8-connected components "
+             "with box statistics, max 3000 candidates per page)", "pages/s", True),
 }
 
 
@@ -713,6 +716,68 @@ def config_arm(args):
                     "1080x1920 pages -> detector resize + normalize into a 960x960 canvas (content 540x960) as "
                     "FP16 NHWC, and 64 synthetic rotated line boxes per page -> perspective ROI warp to 48x320 "
                     "FP16 NHWC crops (v/127.5 - 1)")
+    elif args.config == "post":
+        pages, S, max_comp = 8, workloads.PAGE, 3000
+        probs_h = torch.from_numpy(workloads.db_like_maps(r, pages, S)).pin_memory()
+        probs = probs_h.to(dev)
+        n = probs.numel()
+        bitmap = torch.empty(pages, S, S, dtype=torch.uint8, device=dev)
+        labels = torch.empty(pages, S, S, dtype=torch.int32, device=dev)
+        counts = torch.empty(pages, dtype=torch.int32, device=dev)
+        stats = torch.empty(pages, max_comp, 5, dtype=torch.int32, device=dev)
+        probq = torch.empty(pages, max_comp, dtype=torch.int64, device=dev)
+        ws = torch.empty(lib.ppocr_b200_db_components_workspace(pages, S, S, max_comp), dtype=torch.uint8,
+                         device=dev)
+        stream = torch.cuda.Stream(dev)
+        s = ctypes.c_void_p(stream.cuda_stream)
+        cev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+
+        def post(i=None, src=probs):
+            capi.check(lib.ppocr_b200_binarize(P(src), P(bitmap), n, 0.3, s))
+            if i is not None:
+                cev[i][0].record(stream)
+            capi.check(lib.ppocr_b200_db_components(P(bitmap), P(src), pages, S, S, max_comp, P(labels), P(counts),
+                                                    P(stats), P(probq), P(ws), s))
+            if i is not None:
+                cev[i][1].record(stream)
+
+        for _ in range(warm):
+            post()
+        stream.synchronize()
+        assert lib.ppocr_b200_device_error() == 0
+        with ClockSampler(local) as clocks:
+            step_ms = _event_steps(stream, args.steps, post, flush)
+        comp_ms = statistics.mean(a.elapsed_time(b) for a, b in cev)
+        stage = torch.empty_like(probs)
+        counts_h = torch.empty_like(counts, device="cpu").pin_memory()
+        stats_h = torch.empty_like(stats, device="cpu").pin_memory()
+        probq_h = torch.empty_like(probq, device="cpu").pin_memory()
+
+        def e2e_body(i):
+            with torch.cuda.stream(stream):
+                stage.copy_(probs_h, non_blocking=True)
+            post(src=stage)
+            with torch.cuda.stream(stream):
+                counts_h.copy_(counts, non_blocking=True)
+                stats_h.copy_(stats, non_blocking=True)
+                probq_h.copy_(probq, non_blocking=True)
+
+        e2e_ms = _event_steps(stream, args.steps, e2e_body, None)
+        h2d = probs_h.numel() * 4
+        d2h = counts_h.numel() * 4 + stats_h.numel() * 4 + probq_h.numel() * 8
+        comp_bytes = n * (1.0 + 4.0 + 4.0)  # bitmap + probabilities read, labels written
+        roof = _roofline_for("hbm", comp_ms, comp_bytes, None, "post:db_components (7 launches)", peak_tf,
+                             peak_hbm, peak_kind)
+        roof["algorithmic"] = "u8 bitmap + f32 probabilities read once, int32 labels written once"
+        extra["components_per_page"] = [int(c) for c in counts.cpu().tolist()]
+        launches = 1 + 8
+        units = pages
+        cpu = _cpu_post(probs_h.numpy()[0])
+        workload = ("DB post-processing front end (reference db_postprocess.cpp:183-252: cv::compare, then "
+                    "findContours on the host): 8 synthetic DB-like 960x960 FP32 probability maps (64 rotated "
+                    "text-line blobs per page over speckle) -> binarize 0.3 -> 8-connected components labelled "
+                    "in OpenCV's order with (left, top, width, height, area) and fixed-point probability sums")
     else:  # c5
         pp = pipeline.PagePipeline(device=dev)
         pages_np, crops_np = workloads.c5_pages(r)
@@ -894,6 +959,20 @@ def _cpu_pre(page, boxes, ch, cw):
     return {"value": round(1.0 / dt, 3), "unit": "pages/s", "cores": 1, "kind": "port",
             "sample": f"1 page + its 64 crops through oracle/preprocess.py (numpy float32, {dt * 1e3:.0f} ms); "
                       "the reference's preprocessing exists only as CUDA kernels"}
+
+
+def _cpu_post(prob):
+    """One page through the oracle (numpy binarize + scipy labelling +
+    statistics, the OpenCV-equivalent CPU path) on the host, scaled to 8."""
+    from oracle import components as OC
+    from oracle import layers as L
+
+    t0 = time.perf_counter()
+    bm = L.binarize(prob, 0.3)
+    OC.components(bm, prob)
+    dt = time.perf_counter() - t0
+    return {"value": round(1.0 / dt, 3), "unit": "pages/s", "cores": 1, "kind": "port",
+            "sample": f"1 page of 960^2 through oracle/components.py (numpy + scipy.ndimage, {dt * 1e3:.0f} ms)"}
 
 
 def _cpu_c5():

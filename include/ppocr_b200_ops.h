@@ -133,6 +133,27 @@ int ppocr_b200_deconv_nhwc(const void *x, const void *w, const void *bias,
 // map[i] = prob[i] > thresh ? 255 : 0. prob float32, map uint8.
 int ppocr_b200_binarize(const float *prob, uint8_t *map, size_t n,
                         float thresh, cudaStream_t stream);
+// DB post-processing front end (extension; the reference runs
+// cv::findContours on the host after copying the whole FP32 map back,
+// native/src/detection/db_postprocess.cpp:183-252): 8-connected components
+// of `pages` binarized maps bitmap [pages][h][w] (non-zero = foreground),
+// labelled 1..counts[p] per page (0 = background) into labels
+// [pages][h][w] (int32) in the order OpenCV's
+// connectedComponentsWithStats (connectivity 8) numbers them (each
+// component's first pixel in 2x2-block raster order), with
+// stats [pages][max_components][5] = (left, top, width, height, area) --
+// OpenCV's layout -- and prob_sum_q32 [pages][max_components] = sum over the
+// component's pixels of floor(clamp(prob, 0, 1) * 2^32) (deterministic;
+// prob may be null: sums 0). Components past max_components are labelled
+// and counted but get no stats (zeros). workspace: device memory of
+// ppocr_b200_db_components_workspace() bytes, 256-byte aligned.
+size_t ppocr_b200_db_components_workspace(int pages, int h, int w,
+                                          int max_components);
+int ppocr_b200_db_components(const uint8_t *bitmap, const float *prob,
+                             int pages, int h, int w, int max_components,
+                             int *labels, int *counts, int *stats,
+                             unsigned long long *prob_sum_q32, void *workspace,
+                             cudaStream_t stream);
 // Frees device memory returned by ppocr_model_load_weights (cudaFree).
 int ppocr_b200_device_free(void *device_pointer);
 // copy_input / copy_float_output (native/src/compiled/model_library.cu:15-25).

@@ -499,6 +499,33 @@ int ppocr_b200_batch_roi_warp(const void *src, size_t src_step, int src_rows,
                              output_bgr, PPOCR_B200_PREP_F32_NCHW, stream);
 }
 
+size_t ppocr_b200_db_components_workspace(int pages, int h, int w,
+                                          int max_components) {
+  if (pages <= 0 || h <= 0 || w <= 0 || max_components <= 0)
+    return 0;
+  return db_components_workspace(pages, h, w, max_components);
+}
+
+int ppocr_b200_db_components(const uint8_t *bitmap, const float *prob,
+                             int pages, int h, int w, int max_components,
+                             int *labels, int *counts, int *stats,
+                             unsigned long long *prob_sum_q32, void *workspace,
+                             cudaStream_t stream) {
+  g_error.clear();
+  if (pages < 0 || h < 0 || w < 0)
+    return fail("invalid db components arguments");
+  if (pages == 0 || h == 0 || w == 0)
+    return 0;
+  if (!bitmap || !labels || !counts || !stats || !prob_sum_q32 || !workspace ||
+      max_components <= 0 ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255) ||
+      static_cast<long long>(pages) * h * w >= (1LL << 31))
+    return fail("invalid db components arguments");
+  return status(db_components(bitmap, prob, pages, h, w, max_components, labels,
+                              counts, stats, prob_sum_q32, workspace, stream),
+                "db components");
+}
+
 int ppocr_b200_device_free(void *p) {
   g_error.clear();
   return status(cudaFree(p), "cudaFree");

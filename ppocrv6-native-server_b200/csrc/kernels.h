@@ -222,6 +222,13 @@ cudaError_t selected_class_vs_max(const half *hidden, const half *w,
                                   int class_id, cudaStream_t stream);
 
 // ------------------------------------------------------- detector kernels
+// DB post-processing front end: 8-connected component labelling of
+// binarized maps with (left, top, width, height, area) and fixed-point
+// probability sums per component (see ppocr_b200_db_components).
+size_t db_components_workspace(int pages, int H, int W, int max_comp);
+cudaError_t db_components(const uint8_t *bitmap, const float *prob, int pages, int H, int W, int max_comp,
+                          int *labels, int *counts, int *stats, unsigned long long *probq, void *workspace,
+                          cudaStream_t stream);
 // DB binarize: map[i] = prob[i] > thresh ? 255 : 0.
 cudaError_t binarize(const float *prob, uint8_t *map, size_t n, float thresh,
                      cudaStream_t stream);

@@ -60,6 +60,8 @@ SIGNATURES = {
     "ppocr_b200_deconv_nhwc": (I, [V, V, V, V, I, I, I, I, I, I, I, I, V]),
     "ppocr_b200_binarize": (I, [V, V, S, F, V]),
     "ppocr_b200_dwpw_block": (I, [V, V, V, I, V, V, I, V, I, I, I, I, I, I, V]),
+    "ppocr_b200_db_components_workspace": (S, [I, I, I, I]),
+    "ppocr_b200_db_components": (I, [V, V, I, I, I, I, V, V, V, V, V, V]),
     "ppocr_b200_device_free": (I, [V]),
     "ppocr_b200_f32_to_f16": (I, [V, V, S, S, V]),
     "ppocr_b200_f16_to_f32": (I, [V, V, S, V]),

@@ -105,3 +105,30 @@ def line_boxes(r: np.random.Generator, n: int, page_h: int, page_w: int, crop_h:
         m.append(_inverse_homography(quad, cw, crop_h))
         widths.append(cw)
     return np.stack(m), np.array(widths, np.int32)
+
+
+def db_like_maps(r: np.random.Generator, pages: int = 8, size: int = PAGE, lines: int = LINES_PER_PAGE) -> np.ndarray:
+    """Synthetic DB probability maps float32 [pages, size, size] in [0, 1]:
+    `lines` rotated text-line blobs per page (soft-edged, 8-40 px tall, up to
+    a sixth of the page wide) over a background below the 0.3 threshold with
+    0.05 % isolated speckle pixels above it (~460 one-pixel components per
+    page), the shapes the binarize + component front end sees."""
+    out = np.empty((pages, size, size), np.float32)
+    for p in range(pages):
+        m = r.uniform(0.0, 0.25, (size, size)).astype(np.float32)
+        speck = r.random((size, size)) < 5e-4
+        m[speck] = r.uniform(0.3, 0.5, int(speck.sum())).astype(np.float32)
+        for _ in range(lines):
+            cy, cx = r.uniform(0, size), r.uniform(0, size)
+            a = r.uniform(-0.3, 0.3)
+            lw, lh = r.uniform(10, size / 6), r.uniform(4, 20)
+            ext = int(lw + lh) + 2
+            y0, y1 = max(0, int(cy) - ext), min(size, int(cy) + ext)
+            x0, x1 = max(0, int(cx) - ext), min(size, int(cx) + ext)
+            yy, xx = np.mgrid[y0:y1, x0:x1].astype(np.float32)
+            u = (xx - cx) * np.cos(a) + (yy - cy) * np.sin(a)
+            v = -(xx - cx) * np.sin(a) + (yy - cy) * np.cos(a)
+            blob = np.exp(-((u / lw) ** 8 + (v / lh) ** 2)).astype(np.float32)
+            m[y0:y1, x0:x1] = np.maximum(m[y0:y1, x0:x1], blob)
+        out[p] = m
+    return out

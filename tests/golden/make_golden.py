@@ -6,7 +6,8 @@ this script runs them on small seeded inputs and stores inputs + outputs as
 compressed .npz files, so the CPU tests can pin the oracle against real
 reference outputs without a GPU or the reference tree.
 
-  python tests/golden/make_golden.py cpu            # ctc_collapse.npz (host code)
+  python tests/golden/make_golden.py cpu            # ctc_collapse.npz (host code),
+                                                    # components.npz (OpenCV)
   python tests/golden/make_golden.py gpu [--out D]  # classifier / depthwise /
                                                     # pool / preprocess .npz
                                                     # (reference CUDA kernels,
@@ -19,6 +20,9 @@ Sources of each fixture:
   pool.npz          native/src/compiled/spatial_kernels.cuh pool_nhwc_vec8
   preprocess.npz    native/src/kernels/detector_preprocess.cu:84-101,
                     native/src/kernels/roi_warp.cu:113-131
+  components.npz    OpenCV connectedComponentsWithStats (connectivity 8) on
+                    binarized DB-like maps: the library the reference's
+                    db_postprocess.cpp:183-252 runs on these maps
 """
 
 from __future__ import annotations
@@ -63,6 +67,41 @@ def make_cpu(out: Path) -> None:
                                     o_len.ctypes.data, o_sc.ctypes.data) == 0
     np.savez_compressed(out / "ctc_collapse.npz", ids=ids, scores=scores, blank=np.int32(0),
                         out_ids=o_ids, out_len=o_len, out_score=o_sc)
+    make_components(out)
+
+
+def db_like_map(r, h, w, blobs=40):
+    """float32 [h, w] in [0, 1]: rotated elongated text-line blobs plus
+    speckle, the shapes a DB probability map has."""
+    yy, xx = np.mgrid[0:h, 0:w].astype(np.float32)
+    m = np.zeros((h, w), np.float32)
+    for _ in range(blobs):
+        cy, cx = r.uniform(0, h), r.uniform(0, w)
+        a = r.uniform(-0.4, 0.4)
+        lw, lh = r.uniform(4, w / 3), r.uniform(1.5, 6)
+        u = (xx - cx) * np.cos(a) + (yy - cy) * np.sin(a)
+        v = -(xx - cx) * np.sin(a) + (yy - cy) * np.cos(a)
+        m = np.maximum(m, np.exp(-((u / lw) ** 8 + (v / lh) ** 2)))
+    m += r.uniform(0, 0.35, (h, w)).astype(np.float32)  # speckle around the 0.3 threshold
+    return np.clip(m, 0, 1).astype(np.float32)
+
+
+def make_components(out: Path) -> None:
+    import cv2
+
+    r = np.random.default_rng(SEED + 902)
+    res = {}
+    cases = {"dblike_96x128": db_like_map(r, 96, 128), "dblike_37x53": db_like_map(r, 37, 53, 8)}
+    checker = np.indices((9, 11)).sum(0) % 2  # diagonal-only connectivity
+    cases["checker_9x11"] = checker.astype(np.float32)
+    for name, prob in cases.items():
+        bitmap = (prob > np.float32(0.3)).astype(np.uint8) * 255
+        n, labels, stats, _ = cv2.connectedComponentsWithStats(bitmap, connectivity=8, ltype=cv2.CV_32S)
+        res[f"{name}__prob"] = prob
+        res[f"{name}__bitmap"] = bitmap
+        res[f"{name}__labels"] = labels.astype(np.int32)
+        res[f"{name}__stats"] = stats[1:].astype(np.int32)  # row 0 is the background
+    np.savez_compressed(out / "components.npz", **res)
 
 
 def make_gpu(out: Path) -> None:

@@ -9,6 +9,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import components as OC
 from oracle import layers as L
 from oracle import preprocess as OP
 
@@ -91,7 +92,21 @@ def test_preprocess_golden():
             assert np.all(want[b, :, :, cw:] == 0)
 
 
+def test_components_golden():
+    """8-connected components and (left, top, width, height, area) equal
+    OpenCV's connectedComponentsWithStats (the library the reference's DB
+    post-processing runs on these maps), numbering included."""
+    g = _load("components.npz")
+    names = sorted({k.split("__")[0] for k in g.files})
+    assert len(names) >= 3
+    for n in names:
+        labels, count, stats, _ = OC.components(g[f"{n}__bitmap"], g[f"{n}__prob"])
+        assert count == g[f"{n}__stats"].shape[0]
+        assert np.array_equal(labels, g[f"{n}__labels"]), n
+        assert np.array_equal(stats, g[f"{n}__stats"]), n
+
+
 @pytest.mark.parametrize("fixture", ["ctc_collapse.npz", "classifier.npz", "depthwise.npz", "pool.npz",
-                                     "preprocess.npz"])
+                                     "preprocess.npz", "components.npz"])
 def test_golden_fixtures_are_small(fixture):
     assert (GOLDEN / fixture).stat().st_size < 512 * 1024
