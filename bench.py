@@ -708,6 +708,31 @@ def config_arm(args):
         extra["roi_warp"] = _roofline_for("hbm", warp_ms, warp_bytes, None, "pre:roi_warp x8 (one per page)",
                                           peak_tf, peak_hbm, peak_kind)
         extra["roi_warp"]["algorithmic"] = "FP16 NHWC crops written + each source page read once"
+        # Line tensors (server-side lines path): 512 decoded line images of
+        # random sizes -> [512, 48, 320, 3] FP16 NHWC in one call.
+        lr = workloads.rng(SEED + 5)
+        ims, offs, wsz, hsz = [], [], [], []
+        pos = 0
+        for _ in range(LINES):
+            h_ = int(lr.integers(24, 97))
+            w_ = int(lr.integers(8, W * h_ // 48 + 1))
+            ims.append(lr.integers(0, 256, h_ * w_ * 3, dtype=np.uint8))
+            offs.append(pos)
+            wsz.append(w_)
+            hsz.append(h_)
+            pos += h_ * w_ * 3
+        line_px = torch.from_numpy(np.concatenate(ims)).to(dev)
+        line_out = torch.empty(LINES, H, W, 3, dtype=torch.float16, device=dev)
+        Ln, In = ctypes.c_longlong * LINES, ctypes.c_int * LINES
+        offs_c, w_c, h_c, st_c = Ln(*offs), In(*wsz), In(*hsz), In(*[3 * x for x in wsz])
+        lines_call = lambda i=None: capi.check(lib.ppocr_b200_line_tensors(  # noqa: E731
+            P(line_px), offs_c, w_c, h_c, st_c, LINES, W, P(line_out), capi.PREP_F16_NHWC, s))
+        for _ in range(warm):
+            lines_call()
+        line_ms = statistics.mean(_event_steps(stream, 20, lambda i: lines_call(), flush))
+        extra["line_tensors"] = _roofline_for("hbm", line_ms, float(pos + line_out.numel() * 2), None,
+                                              "pre:line_tensors (512 lines)", peak_tf, peak_hbm, peak_kind)
+        extra["line_tensors"]["algorithmic"] = "decoded u8 line images read once + FP16 NHWC tensor written"
         roof["algorithmic"] = "u8 pages read once + FP16 NHWC canvases written"
         launches = 1 + pages
         units = pages

@@ -72,6 +72,23 @@ int ppocr_b200_roi_warp(const void *src, size_t src_step, int src_rows,
                         int dst_h, int dst_w, int output_bgr, int format,
                         cudaStream_t stream);
 
+// Line tensors for the recognizer (extension; replaces the server's CPU
+// write_line_tensor, server/src/lines.rs:115-135 with server/src/main.rs:
+// 1101-1150): `lines` decoded RGB images in one device buffer `pixels`
+// (image i at byte offsets[i], widths[i] x heights[i], strides[i] bytes per
+// row; the four arrays on the host) -> height 48, width ceil(48 * w / h),
+// pixel-centre bilinear (an image already 48 high and of that width is
+// copied), values (v/255 - 0.5)/0.5 when copied and v/127.5 - 1 when
+// resampled, right-padded with 0 to `bucket` columns. `format`:
+// PPOCR_B200_PREP_F16_NHWC [lines][48][bucket][3] fp16 (the recognizer's
+// ppocr_model_enqueue_nhwc_f16 input) or PPOCR_B200_PREP_F32_NCHW
+// [lines][3][48][bucket] f32 (the server's tensor). A line whose normalized
+// width exceeds the bucket fails the call with the reference's message.
+int ppocr_b200_line_tensors(const void *pixels, const long long *offsets,
+                            const int *widths, const int *heights,
+                            const int *strides, int lines, int bucket,
+                            void *out, int format, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -5,6 +5,7 @@
 #include "../../include/ppocr_b200_ops.h"
 #include "../../include/ppocr_b200_preprocess.h"
 #include "kernels.h"
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -487,6 +488,48 @@ int ppocr_b200_roi_warp(const void *src, size_t src_step, int src_rows,
                          d_crop_widths, dst, batch, dst_h, dst_w,
                          output_bgr ? 1 : 0, format, stream),
                 "roi warp");
+}
+
+int ppocr_b200_line_tensors(const void *pixels, const long long *offsets,
+                            const int *widths, const int *heights,
+                            const int *strides, int lines, int bucket,
+                            void *out, int format, cudaStream_t stream) {
+  g_error.clear();
+  if (lines < 0 || bucket <= 0 || (lines > 0 && (!pixels || !offsets || !widths || !heights || !strides || !out)) ||
+      (format != PPOCR_B200_PREP_F32_NCHW && format != PPOCR_B200_PREP_F16_NHWC))
+    return fail("invalid line tensor arguments");
+  const size_t elem = format == PPOCR_B200_PREP_F16_NHWC ? 2 : 4;
+  for (int c0 = 0; c0 < lines; c0 += kMaxLineBatch) {
+    const int n = std::min(kMaxLineBatch, lines - c0);
+    static thread_local LineBatch lb;
+    for (int k = 0; k < n; ++k) {
+      const int i = c0 + k;
+      const int w = widths[i], h = heights[i];
+      if (w <= 0 || h <= 0)
+        return fail("line dimensions must be positive");
+      if (strides[i] < 3 * w || offsets[i] < 0)
+        return fail("invalid line tensor arguments");
+      const long long natural = (static_cast<long long>(w) * 48 + h - 1) / h;
+      if (natural > bucket)
+        return fail("line normalized width " + std::to_string(natural) + " exceeds maximum " +
+                    std::to_string(bucket) + "; split the line crop");
+      LineGeo &g = lb.line[k];
+      g.offset = offsets[i];
+      g.width = w;
+      g.height = h;
+      g.stride = strides[i];
+      g.resized_width = static_cast<int>(natural);
+      g.scale_x = static_cast<float>(w) / static_cast<float>(natural);
+      g.scale_y = static_cast<float>(h) / 48.0f;
+      g.copy = (w == natural && h == 48) ? 1 : 0;
+    }
+    void *dst = static_cast<char *>(out) + static_cast<size_t>(c0) * 3 * 48 * bucket * elem;
+    const int st = status(line_tensors(static_cast<const uint8_t *>(pixels), lb, n, dst, bucket, format, stream),
+                          "line tensors");
+    if (st)
+      return st;
+  }
+  return 0;
 }
 
 int ppocr_b200_batch_roi_warp(const void *src, size_t src_step, int src_rows,

@@ -244,6 +244,23 @@ cudaError_t deconv_kxk(const half *x, const half *w, const half *bias, half *y,
                        int act, cudaStream_t stream);
 
 // -------------------------------------------------- page / line preprocess
+// One decoded RGB line image of a line-tensor batch (host-computed layout).
+struct LineGeo {
+  long long offset;   // byte offset of the image in the pixel buffer
+  int width, height;  // source size
+  int stride;         // bytes per source row
+  int resized_width;  // ceil(48 * width / height) <= bucket
+  float scale_x, scale_y;
+  int copy;           // 48-high line of exactly resized_width: no resampling
+};
+constexpr int kMaxLineBatch = 512; // lines per launch (kernel parameter space)
+struct LineBatch {
+  LineGeo line[kMaxLineBatch];
+};
+// Line tensors [lines][48][bucket][3] fp16 (PREP_F16_NHWC) or
+// [lines][3][48][bucket] f32 (PREP_F32_NCHW) from the images of `lb`.
+cudaError_t line_tensors(const uint8_t *pixels, const LineBatch &lb, int lines, void *out, int bucket, int fmt,
+                         cudaStream_t stream);
 // Output formats of the preprocessing kernels.
 enum PrepFormat { PREP_F32_NCHW = 0, PREP_F16_NHWC = 1 };
 // Detector resize + normalize of `images` u8 HWC (3-channel) pages, each

@@ -30,7 +30,7 @@ COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
           "-Xcompiler", "-fvisibility=default", "--expt-relaxed-constexpr"]
 
 LIB_SOURCES = ["common.cu", "tc_gemm.cu", "halo_conv.cu", "dwpw.cu", "spatial.cu", "seq.cu", "head.cu",
-               "detect.cu", "components.cu", "preprocess.cu", "runtime.cu", "capi.cu",
+               "detect.cu", "components.cu", "preprocess.cu", "lines.cu", "runtime.cu", "capi.cu",
                "head_noalloc.cu"]
 
 

@@ -71,6 +71,7 @@ SIGNATURES = {
     "ppocr_b200_detector_preprocess": (I, [V, S, I, I, S, I, V, I, I, I, I, I, I, V]),
     "ppocr_b200_batch_roi_warp": (I, [V, S, I, I, V, V, V, I, I, I, I, V]),
     "ppocr_b200_roi_warp": (I, [V, S, I, I, V, V, V, I, I, I, I, I, V]),
+    "ppocr_b200_line_tensors": (I, [V, V, V, V, V, I, I, V, I, V]),
 }
 PREP_F32_NCHW, PREP_F16_NHWC = 0, 1
 
