@@ -179,6 +179,7 @@ __global__ void __launch_bounds__(kDwpwThreads, 1)
     for (int e = 0; e < 8; ++e)
       bv[e] = __half2float(bdw[j * 8 + e]);
     const bool has_bias = g.bdw != nullptr;
+    const uint32_t wdw_s = smem_u32(wdw);
     int it = 0;
     for (int t = blockIdx.x; t < g.tiles; t += gridDim.x, ++it) {
       const int s = it & 1, a = it & 1;
@@ -206,14 +207,11 @@ __global__ void __launch_bounds__(kDwpwThreads, 1)
 #pragma unroll
         for (int q = 0; q < NCOL; ++q) {
           const uint32_t pix = static_cast<uint32_t>((r + kh) * HW + px0 + q);
-          const uint32_t addr = hbase + pix * 128u + ((static_cast<uint32_t>(j) ^ (pix & 7u)) << 4);
-          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(strip[q].x), "=r"(strip[q].y), "=r"(strip[q].z), "=r"(strip[q].w)
-                       : "r"(addr));
+          strip[q] = lds_v4(hbase + pix * 128u + ((static_cast<uint32_t>(j) ^ (pix & 7u)) << 4));
         }
 #pragma unroll
         for (int kw = 0; kw < K; ++kw) {
-          const uint4 wt = reinterpret_cast<const uint4 *>(wdw + (kh * K + kw) * 64)[j];
+          const uint4 wt = lds_v4(wdw_s + static_cast<uint32_t>(((kh * K + kw) * 64 + j * 8) * 2));
 #pragma unroll
           for (int p = 0; p < 4; ++p) {
             const uint4 xv = strip[p + kw];
@@ -242,10 +240,7 @@ __global__ void __launch_bounds__(kDwpwThreads, 1)
           o[e] = *reinterpret_cast<const uint32_t *>(&h);
         }
         const uint32_t m = static_cast<uint32_t>(r * kTileCols + px0 + p); // A row
-        const uint32_t addr = abase + m * 128u + ((static_cast<uint32_t>(j) ^ (m & 7u)) << 4);
-        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(o[0]), "r"(o[1]), "r"(o[2]),
-                     "r"(o[3])
-                     : "memory");
+        sts_v4(abase + m * 128u + ((static_cast<uint32_t>(j) ^ (m & 7u)) << 4), make_uint4(o[0], o[1], o[2], o[3]));
       }
       fence_async_smem(); // generic-proxy writes -> tensor-core reads
       mbar_arrive(&afull[a]);

@@ -119,6 +119,12 @@ cudaError_t stem_conv_s2d(const half *x, const half *wp, const half *bias,
                           half *y, half *scratch, int batch, int Ci, int H,
                           int W, int Co, int act, cudaStream_t s);
 // Generic NHWC direct conv for small Ci (stem): w [Co][KH][KW][Ci].
+// Stem 3x3 / stride 2 / pad 1 convolution of a 3-channel NHWC image on the
+// tensor cores (im2col rows built in shared memory, K = 27 -> 32).
+// cudaErrorNotSupported for shapes it does not take (Co not 16/32/48/64,
+// rows not a multiple of 16 bytes).
+cudaError_t stem_conv_tc(const half *x, const half *w, const half *bias, half *y, int B, int H, int W, int Co,
+                         int act, cudaStream_t stream);
 cudaError_t direct_conv(const half *x, const half *w, const half *bias,
                         half *y, int batch, int Ci, int H, int W, int Co,
                         int OH, int OW, int KH, int KW, int SH, int SW, int PH,

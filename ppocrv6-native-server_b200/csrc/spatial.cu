@@ -1380,6 +1380,13 @@ cudaError_t direct_conv(const half *x, const half *w, const half *bias,
     return cudaErrorInvalidValue;
   const long long pixels = static_cast<long long>(batch) * OH * OW;
   const long long pairs = static_cast<long long>(batch) * OH * ((OW + 1) / 2);
+  // The HGNet stem (3x3 / s2 / p1 over 3 channels) runs on the tensor cores.
+  if (Ci == 3 && KH == 3 && KW == 3 && SH == 2 && SW == 2 && PH == 1 && PW == 1 && OH == (H + 1) / 2 &&
+      OW == (W + 1) / 2) {
+    const cudaError_t e = stem_conv_tc(x, w, bias, y, batch, H, W, Co, act, s);
+    if (e != cudaErrorNotSupported)
+      return e;
+  }
   if (Ci <= 4 && (Co == 16 || Co == 32 || Co == 48) && pairs < (1LL << 31)) {
     const int per_row = (OW + 1) / 2;
 #define PB2_STEM2(co)                                                          \

@@ -29,7 +29,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
           "-Xcompiler", "-fvisibility=default", "--expt-relaxed-constexpr"]
 
-LIB_SOURCES = ["common.cu", "tc_gemm.cu", "halo_conv.cu", "dwpw.cu", "spatial.cu", "seq.cu", "head.cu",
+LIB_SOURCES = ["common.cu", "tc_gemm.cu", "halo_conv.cu", "dwpw.cu", "stem_tc.cu", "spatial.cu", "seq.cu", "head.cu",
                "detect.cu", "components.cu", "preprocess.cu", "lines.cu", "runtime.cu", "capi.cu",
                "head_noalloc.cu"]
 

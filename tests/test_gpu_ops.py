@@ -167,10 +167,14 @@ def test_dwpw_block(native, cuda, batch, h, w, k, co, act_dw, act_pw, bias):
     assert_close(host(y), want, what=f"dwpw {batch}x{h}x{w} k{k} -> {co}")
 
 
-@pytest.mark.parametrize("batch,h,w,co", [(2, 48, 320, 48), (1, 9, 35, 48), (2, 10, 12, 32), (1, 8, 8, 64)])
-def test_stem_direct_conv(native, cuda, batch, h, w, co):
-    """Stem 3x3 stride-2 conv with 3 input channels (odd output widths
-    leave a single pixel in the last pair)."""
+@pytest.mark.parametrize("batch,h,w,co,act", [(2, 48, 320, 48, 1), (1, 9, 35, 48, 1), (2, 10, 12, 32, 1),
+                                             (1, 8, 8, 64, 0), (3, 50, 96, 16, 3), (2, 47, 64, 32, 1),
+                                             (600, 48, 320, 48, 1), (4, 48, 320, 48, 0), (2, 32, 64, 64, 5)])
+def test_stem_direct_conv(native, cuda, batch, h, w, co, act):
+    """Stem 3x3 stride-2 conv with 3 input channels: the tensor-core form
+    (rows a multiple of 16 bytes: odd heights, partial units, many images)
+    and the SIMT form (odd output widths leave a single pixel in the last
+    pair)."""
     r = rng(3 + w)
     x = f16(r.uniform(-1, 1, (batch, h, w, 3)))
     wt = f16(r.standard_normal((co, 3, 3, 3)) * np.sqrt(2.0 / 27))
@@ -179,11 +183,11 @@ def test_stem_direct_conv(native, cuda, batch, h, w, co):
     y = torch.empty(batch, oh, ow, co, dtype=torch.float16, device=cuda)
     dx, dw, db = dev(x), dev(wt), dev(b)
     rc = native.ppocr_b200_conv_nhwc(ptr(dx), ptr(dw), ptr(db), ptr(y), batch, 3, h, w, co, 3, 3,
-                                     2, 2, 1, 1, 1, 1, stream_handle())
+                                     2, 2, 1, 1, 1, act, stream_handle())
     assert rc == 0, native.ppocr_b200_last_error()
     sync()
-    want = L.conv_nhwc(x, wt, b, (2, 2), (1, 1), 1, 1)
-    assert_close(host(y), want, what="stem")
+    want = L.conv_nhwc(x, wt, b, (2, 2), (1, 1), 1, act)
+    assert_close(host(y), want, what=f"stem {batch}x{h}x{w} -> {co} act {act}")
 
 
 @pytest.mark.parametrize("batch,h,w,ci,co,act", [(2, 48, 320, 3, 48, 1), (1, 9, 35, 3, 48, 1),
