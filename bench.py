@@ -7,7 +7,8 @@ the head C-ABI. Each GPU runs an independent replica (request-batch data
 parallelism, no collective on the hot path; torch.distributed only
 synchronises the timing). `value` is the whole-job lines/s with inputs
 resident in HBM; `e2e` repeats the measurement with the pinned-host input
-copied in and the decoded tokens copied out every step.
+copied in and the decoded tokens copied out every step, through the
+double-buffered LineStream (the copy of step k+1 runs during step k).
 
 `--impl reference` times the CPU restatement of the same forward (the
 reference has no CPU implementation of its layer path; the oracle port in
@@ -293,15 +294,16 @@ def b200_arm(args):
     total_ms = max_over_ranks(sum(step_ms))
     value = world * LINES * args.steps / (total_ms / 1e3)
 
-    # ---- end to end: pinned host in, tokens out, every step
-    out_ids = torch.empty(LINES, rec.T, dtype=torch.int32).pin_memory()
-    out_len = torch.empty(LINES, dtype=torch.int32).pin_memory()
-    out_sc = torch.empty(LINES, dtype=torch.float32).pin_memory()
-    x_stage = torch.empty_like(x_dev)
-    for _ in range(2):
-        with torch.cuda.stream(stream):
-            x_stage.copy_(x_host, non_blocking=True)
-        rec.enqueue(x_stage)
+    # ---- end to end: pinned host in, tokens out, every step, through the
+    # double-buffered LineStream (the copy of step k+1 overlaps step k)
+    outs = [(torch.empty(LINES, rec.T, dtype=torch.int32).pin_memory(),
+             torch.empty(LINES, dtype=torch.int32).pin_memory(),
+             torch.empty(LINES, dtype=torch.float32).pin_memory()) for _ in range(2)]
+    out_ids = outs[0][0]
+    out_len = outs[0][1]
+    out_sc = outs[0][2]
+    streamer = pipeline.LineStream(rec)
+    streamer.enqueue([x_host] * 2, outs)
     stream.synchronize()
     barrier()
     torch.cuda.synchronize(dev)
@@ -309,14 +311,7 @@ def b200_arm(args):
     e1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         e0.record(stream)
-    for _ in range(args.steps):
-        with torch.cuda.stream(stream):
-            x_stage.copy_(x_host, non_blocking=True)
-        rec.enqueue(x_stage)
-        with torch.cuda.stream(stream):
-            out_ids.copy_(rec.out_ids, non_blocking=True)
-            out_len.copy_(rec.out_len, non_blocking=True)
-            out_sc.copy_(rec.out_score, non_blocking=True)
+    streamer.enqueue([x_host] * args.steps, [outs[i % 2] for i in range(args.steps)])
     with torch.cuda.stream(stream):
         e1.record(stream)
     stream.synchronize()

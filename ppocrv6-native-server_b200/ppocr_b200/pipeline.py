@@ -136,6 +136,65 @@ class LineRecognizer:
         self.model.close()
 
 
+class LineStream:
+    """Host batches in, decoded lines out, with the host->device copy of batch
+    k+1 running on a copy stream while the recognizer works on batch k.
+
+    The reference's worker copies each batch and then enqueues the model on
+    one stream (recognition_worker.cpp:700-746), so the copy and the forward
+    take turns; here two device staging buffers alternate: batch k+1 is
+    copied into one while batch k is read from the other, and a copy into a
+    buffer waits for the forward that last read it. Results go back on the
+    recognizer's stream right after each batch's collapse.
+    """
+
+    def __init__(self, rec: LineRecognizer):
+        self.rec = rec
+        with torch.cuda.device(rec.device):
+            self.copy_stream = torch.cuda.Stream(rec.device)
+            b, c, h, w = rec.model.input_shape
+            self.stage = [torch.empty(b, h, w, c, dtype=torch.float16, device=rec.device) for _ in range(2)]
+            self.copied = [torch.cuda.Event() for _ in range(2)]
+            self.consumed = [torch.cuda.Event() for _ in range(2)]
+        self._used = [False, False]
+
+    def enqueue(self, batches, outputs) -> None:
+        """Asynchronous. batches[k]: pinned FP16 NHWC host tensor [n_k, 48,
+        W, 3] (n_k <= the compiled batch); outputs[k]: pinned host tensors
+        (ids [>=n_k, T] int32, lengths [>=n_k] int32, scores [>=n_k] f32)
+        written once the recognizer's stream reaches them. Copies start after
+        all work already queued on the recognizer's stream."""
+        if len(batches) != len(outputs):
+            raise ValueError("one output triple per batch")
+        rec = self.rec
+        self.copy_stream.wait_stream(rec.stream)
+
+        def copy_in(k: int) -> None:
+            s = k % 2
+            if self._used[s]:
+                self.copy_stream.wait_event(self.consumed[s])
+            with torch.cuda.stream(self.copy_stream):
+                self.stage[s][: batches[k].shape[0]].copy_(batches[k], non_blocking=True)
+                self.copied[s].record(self.copy_stream)
+
+        if batches:
+            copy_in(0)
+        for k, host in enumerate(batches):
+            s = k % 2
+            if k + 1 < len(batches):
+                copy_in(k + 1)
+            n = host.shape[0]
+            rec.stream.wait_event(self.copied[s])
+            rec.enqueue(self.stage[s][:n])
+            self.consumed[s].record(rec.stream)
+            self._used[s] = True
+            ids, lens, scores = outputs[k]
+            with torch.cuda.stream(rec.stream):
+                ids[:n].copy_(rec.out_ids[:n], non_blocking=True)
+                lens[:n].copy_(rec.out_len[:n], non_blocking=True)
+                scores[:n].copy_(rec.out_score[:n], non_blocking=True)
+
+
 class PagePipeline:
     """Full-page path on one GPU: detector graph -> DB binarize -> recognizer
     over the page's line crops -> fused head -> device collapse, all on one

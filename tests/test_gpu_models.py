@@ -155,3 +155,31 @@ def test_line_recognizer_tokens(cuda):
         assert lens.shape == (2,) and np.all(lens <= rec.T)
     finally:
         rec.close()
+
+
+def test_line_stream_matches_serial(cuda):
+    """Double-buffered host stream (copy of batch k+1 during batch k) decodes
+    every batch, short ones included, exactly as a serial copy + enqueue."""
+    from ppocr_b200 import pipeline
+
+    rec = pipeline.LineRecognizer("rec_b2", cuda)
+    try:
+        sizes = [2, 1, 2, 2, 1]
+        batches = [torch.from_numpy(rng(40 + k).uniform(-1, 1, (n, 48, 320, 3)).astype(np.float16)).pin_memory()
+                   for k, n in enumerate(sizes)]
+        want = []
+        for b in batches:
+            rec.enqueue(b.cuda())
+            want.append(rec.results(b.shape[0]))
+        outs = [(torch.full((2, rec.T), -1, dtype=torch.int32).pin_memory(),
+                 torch.full((2,), -1, dtype=torch.int32).pin_memory(),
+                 torch.full((2,), -1.0, dtype=torch.float32).pin_memory()) for _ in sizes]
+        stream = pipeline.LineStream(rec)
+        stream.enqueue(batches, outs)
+        rec.stream.synchronize()
+        for (ids, lens, scores), (wi, wl, ws), n in zip(outs, want, sizes):
+            assert np.array_equal(ids[:n].numpy(), wi) and np.array_equal(lens[:n].numpy(), wl)
+            assert np.array_equal(scores[:n].numpy(), ws)
+            assert np.all(lens[n:].numpy() == -1)
+    finally:
+        rec.close()
