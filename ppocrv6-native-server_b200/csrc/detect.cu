@@ -142,74 +142,87 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Few outputs per input pixel with Ci a multiple of 8 (the DB head's last
-// 64 -> 1 upsampling): G = Ci/8 threads share an input pixel, each loading
-// one 16-byte group of 8 channels (a warp reads 512 contiguous bytes) and
-// holding that group's filter rows in registers; the NOUT partial sums are
-// added across the G threads with shuffles and the group-0 thread writes
-// the pixel's KH x KW x Co outputs. Grid-stride over pixels.
-template <int NMAX, int G>
+// Four or fewer outputs per input pixel with Ci = 8*G (the DB head's last
+// 64 -> 1 upsampling): G threads share an input pixel, each loading one
+// 16-byte group of 8 channels (a warp reads 32/G pixels = 512 contiguous
+// bytes per load) and holding that group's filter rows in registers. A warp
+// issues the loads of U such pixel sets before any arithmetic. The four
+// partial sums are reduce-scattered across the G lanes (two halving
+// exchanges, then a plain butterfly: the same pairwise sums as a full
+// butterfly of every output), leaving output o on the lanes whose group
+// bits (G/2, G/4) spell o; the lowest of those lanes stores it.
+// Grid-stride over pixels.
+template <int G, int U>
 __global__ void __launch_bounds__(256)
     deconv_group_kernel(const half *__restrict__ x, const half *__restrict__ w,
                         const half *__restrict__ bias, half *__restrict__ y,
                         uint32_t pixels, FastDiv by_w, FastDiv by_h, int Co,
                         int KH, int KW, int act) {
+  constexpr int NOUT = 4;
+  constexpr uint32_t PPW = 32 / G; // pixels per warp per load
   const int nout = KH * KW * Co;
-  const int g = threadIdx.x % G;
-  float wr[8][NMAX]; // this group's 8 channels x outputs
+  const int lane = threadIdx.x & 31, g = lane % G;
+  float wr[8][NOUT]; // this group's 8 channels x outputs
 #pragma unroll
   for (int c = 0; c < 8; ++c)
 #pragma unroll
-    for (int o = 0; o < NMAX; ++o)
+    for (int o = 0; o < NOUT; ++o)
       wr[c][o] = o < nout ? __half2float(w[(g * 8 + c) * nout + o]) : 0.f;
+  const bool hi1 = (g & (G / 2)) != 0, hi2 = (g & (G / 4)) != 0;
+  const int mine = (hi1 ? 2 : 0) + (hi2 ? 1 : 0); // the output this lane ends with
+  const bool writer = (g & (G / 4 - 1)) == 0 && mine < nout;
+  const int co = mine % Co, tap = mine / Co;
+  const int ta = tap / KW, tb = tap - ta * KW;
+  const float bv = bias && mine < nout ? __half2float(bias[co]) : 0.f;
   const int W = static_cast<int>(by_w.d), H = static_cast<int>(by_h.d);
   const long long OW = static_cast<long long>(W) * KW;
   const long long OH = static_cast<long long>(H) * KH;
-  const uint32_t step = gridDim.x * (blockDim.x / G);
-  // The loop bound is uniform across a warp (its first pixel), so every lane
-  // reaches the shuffles; lanes past the last pixel compute zeros.
-  const uint32_t warp_first = blockIdx.x * (blockDim.x / G) + (threadIdx.x & ~31u) / G;
-  for (uint32_t pw = warp_first; pw < pixels; pw += step) {
-    const uint32_t p = pw + (threadIdx.x & 31u) / G;
-    const bool valid = p < pixels;
-    uint4 u = make_uint4(0, 0, 0, 0);
-    if (valid)
-      u = __ldcs(reinterpret_cast<const uint4 *>(x + static_cast<long long>(p) * G * 8) + g);
-    const half2 *h2 = reinterpret_cast<const half2 *>(&u);
-    float acc[NMAX];
+  const uint32_t warps = gridDim.x * (blockDim.x / 32);
+  const uint32_t step = warps * PPW * U;
+  // The loop bound is uniform across a warp, so every lane reaches the
+  // shuffles; lanes past the last pixel compute zeros and store nothing.
+  for (uint32_t pw = (blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5)) * PPW * U; pw < pixels;
+       pw += step) {
+    uint4 u[U];
 #pragma unroll
-    for (int o = 0; o < NMAX; ++o)
-      acc[o] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = __half22float2(h2[j]);
-#pragma unroll
-      for (int o = 0; o < NMAX; ++o) {
-        acc[o] = fmaf(f.x, wr[2 * j][o], acc[o]);
-        acc[o] = fmaf(f.y, wr[2 * j + 1][o], acc[o]);
-      }
+    for (int k = 0; k < U; ++k) {
+      const uint32_t p = pw + k * PPW + lane / G;
+      u[k] = p < pixels ? __ldcs(reinterpret_cast<const uint4 *>(x + static_cast<long long>(p) * G * 8) + g)
+                        : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int off = G / 2; off; off >>= 1)
+    for (int k = 0; k < U; ++k) {
+      const uint32_t p = pw + k * PPW + lane / G;
+      const half2 *h2 = reinterpret_cast<const half2 *>(&u[k]);
+      float acc[NOUT] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int o = 0; o < NMAX; ++o)
-        acc[o] += __shfl_xor_sync(0xffffffffu, acc[o], off);
-    if (valid && g == 0) {
-      const uint32_t r = by_w.div(p);
-      const int iw = static_cast<int>(p - r * by_w.d);
-      const uint32_t n = by_h.div(r);
-      const int ih = static_cast<int>(r - n * by_h.d);
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h2[j]);
 #pragma unroll
-      for (int o = 0; o < NMAX; ++o) {
-        if (o >= nout)
-          break;
-        const int co = o % Co, tap = o / Co;
-        const int a = tap / KW, b = tap - a * KW;
-        float v = round_half(acc[o]);
+        for (int o = 0; o < NOUT; ++o) {
+          acc[o] = fmaf(f.x, wr[2 * j][o], acc[o]);
+          acc[o] = fmaf(f.y, wr[2 * j + 1][o], acc[o]);
+        }
+      }
+      // Reduce-scatter: keep {0,1} or {2,3}, then one of the pair.
+      const float s0 = __shfl_xor_sync(0xffffffffu, hi1 ? acc[0] : acc[2], G / 2);
+      const float s1 = __shfl_xor_sync(0xffffffffu, hi1 ? acc[1] : acc[3], G / 2);
+      const float k0 = (hi1 ? acc[2] : acc[0]) + s0;
+      const float k1 = (hi1 ? acc[3] : acc[1]) + s1;
+      float v = (hi2 ? k1 : k0) + __shfl_xor_sync(0xffffffffu, hi2 ? k0 : k1, G / 4);
+#pragma unroll
+      for (int off = G / 8; off; off >>= 1)
+        v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (writer && p < pixels) {
+        const uint32_t r = by_w.div(p);
+        const int iw = static_cast<int>(p - r * by_w.d);
+        const uint32_t n = by_h.div(r);
+        const int ih = static_cast<int>(r - n * by_h.d);
+        float o = round_half(v);
         if (bias)
-          v += __half2float(bias[co]);
-        y[((static_cast<long long>(n) * OH + ih * KH + a) * OW + iw * KW + b) * Co + co] =
-            __float2half_rn(apply_act(v, act));
+          o += bv;
+        y[((static_cast<long long>(n) * OH + ih * KH + ta) * OW + iw * KW + tb) * Co + co] =
+            __float2half_rn(apply_act(o, act));
       }
     }
   }
@@ -288,13 +301,14 @@ cudaError_t deconv_kxk(const half *x, const half *w, const half *bias, half *y,
   if (nout <= 4 && (Ci == 64 || Ci == 128 || Ci == 256) && pixels < (1LL << 31) &&
       (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
     const int G = Ci / 8; // threads per pixel
-    const long long per_block = 256 / G;
+    constexpr int U = 4;   // pixel sets loaded per warp before arithmetic
+    const long long per_block = 256 / G * U;
     long long blocks = (pixels + per_block - 1) / per_block;
     const long long cap = static_cast<long long>(sm_count()) * 8;
     if (blocks > cap)
       blocks = cap;
-    auto k = G == 8 ? deconv_group_kernel<4, 8> : G == 16 ? deconv_group_kernel<4, 16>
-                                                          : deconv_group_kernel<4, 32>;
+    auto k = G == 8 ? deconv_group_kernel<8, U> : G == 16 ? deconv_group_kernel<16, U>
+                                                          : deconv_group_kernel<32, U>;
     k<<<static_cast<unsigned>(blocks), 256, 0, s>>>(x, w, bias, y,
                                                     static_cast<uint32_t>(pixels),
                                                     FastDiv(W), FastDiv(H), Co, KH,

@@ -254,14 +254,18 @@ def test_depthwise_bit_exact(native, cuda, batch, h, w, c, kh, kw, sh, sw, act):
 
 
 # ------------------------------------------------------------ sequence ops
-def test_layernorm(native, cuda):
-    r = rng(11)
-    x = f16(r.standard_normal((10240, 120)) * 2 + 0.5)
-    s = f16(r.normal(1, 0.1, 120))
-    b = f16(r.normal(0, 0.1, 120))
-    y = torch.empty(10240, 120, dtype=torch.float16, device=cuda)
+@pytest.mark.parametrize("rows,cols", [(10240, 120), (77, 120), (33, 40), (129, 64), (50, 200), (9, 256),
+                                       (31, 100), (5, 24)])
+def test_layernorm(native, cuda, rows, cols):
+    """Vectorised lane-group form (cols a multiple of 8 in (32, 256], ragged
+    row counts) and the scalar form (other widths)."""
+    r = rng(11 + cols)
+    x = f16(r.standard_normal((rows, cols)) * 2 + 0.5)
+    s = f16(r.normal(1, 0.1, cols))
+    b = f16(r.normal(0, 0.1, cols))
+    y = torch.empty(rows, cols, dtype=torch.float16, device=cuda)
     dx, ds, dbb = dev(x), dev(s), dev(b)
-    assert native.ppocr_b200_layernorm(ptr(dx), ptr(ds), ptr(dbb), ptr(y), 10240, 120, 1e-6,
+    assert native.ppocr_b200_layernorm(ptr(dx), ptr(ds), ptr(dbb), ptr(y), rows, cols, 1e-6,
                                        stream_handle()) == 0
     sync()
     assert_close(host(y), L.layernorm(x, s, b, 1e-6), what="layernorm")
@@ -278,7 +282,8 @@ def test_softmax(native, cuda):
 
 
 @pytest.mark.parametrize("lines,seq,heads,dh", [(4, 40, 8, 15), (3, 25, 4, 16), (2, 20, 2, 24), (2, 70, 2, 8),
-                                               (1, 10, 2, 40), (3, 17, 3, 5), (2, 64, 8, 16)])
+                                               (1, 10, 2, 40), (3, 17, 3, 5), (2, 64, 8, 16),
+                                               (5, 40, 3, 7), (2, 40, 12, 16), (600, 40, 8, 15)])
 def test_attention(native, cuda, lines, seq, heads, dh):
     r = rng(13 + seq)
     qkv = f16(r.standard_normal((lines, seq, 3 * heads * dh)))
@@ -330,6 +335,8 @@ DECONV_CASES = [
     (1, 9, 11, 24, 3, 0, True),       # 12 outputs per pixel, Ci not a multiple of 8
     (1, 5, 7, 128, 1, 4, False),      # 16 threads per input pixel, partial warp at the end
     (3, 33, 29, 64, 1, 4, True),      # 8 threads per pixel, grid-stride with a ragged tail
+    (1, 6, 10, 256, 1, 4, True),      # 32 threads per pixel (a whole warp per input pixel)
+    (3, 240, 240, 64, 1, 4, True),    # more pixels than the capped grid covers in one pass
 ]
 
 
@@ -347,6 +354,24 @@ def test_deconv(native, cuda, batch, h, w, ci, co, act, bias):
     sync()
     check_device_error(native)
     assert_close(host(y), L.deconv_kxk(x, wt, b, act), what=f"deconv {batch}x{h}x{w}x{ci}->{co}")
+
+
+@pytest.mark.parametrize("kh,kw,ci", [(1, 2, 64), (2, 1, 128), (1, 1, 64)])
+def test_deconv_fewer_taps(native, cuda, kh, kw, ci):
+    """Kernel == stride with fewer than four outputs per input pixel: the
+    grouped kernel's lanes that own no output store nothing."""
+    r = rng(40 + kh * 3 + kw)
+    batch, h, w, co = 2, 9, 13, 1
+    x = f16(r.uniform(-1, 1, (batch, h, w, ci)))
+    wt = f16(r.standard_normal((ci, kh, kw, co)) * np.sqrt(2.0 / (kh * kw * ci)))
+    b = f16(r.normal(0, 0.1, co))
+    y = torch.full((batch, kh * h, kw * w, co), float("nan"), dtype=torch.float16, device=cuda)
+    dx, dw, db = dev(x), dev(wt), dev(b)
+    assert native.ppocr_b200_deconv_nhwc(ptr(dx), ptr(dw), ptr(db), ptr(y), batch, h, w, ci, co, kh, kw, 4,
+                                         stream_handle()) == 0, native.ppocr_b200_last_error()
+    sync()
+    check_device_error(native)
+    assert_close(host(y), L.deconv_kxk(x, wt, b, 4), what=f"deconv {kh}x{kw} {ci}->1")
 
 
 @pytest.mark.parametrize("n", [960 * 960 + 3, 5, 3, 1, 4096 * 4 + 7])
@@ -406,13 +431,15 @@ def test_logits_argmax_and_collapse(native, cuda, oracle_c):
 @pytest.mark.parametrize("rows,V,offset", [(3, 5, 0), (7, 1, 0), (64, 300, 0), (64, 300, 1),
                                            (40, 18385, 1), (33, 4099, 0), (6, 40001, 0), (5, 40001, 3),
                                            (9, 4088, 1), (5, 8185, 3), (7, 18424, 1), (4, 20473, 0),
-                                           (3, 32760, 5), (3, 32761, 0)])
+                                           (3, 32760, 5), (3, 32761, 0), (300, 18385, 1), (445, 9001, 3),
+                                           (1000, 18432, 0), (297, 8185, 5), (296, 18433, 0)])
 def test_logits_argmax_shapes(native, cuda, oracle_c, rows, V, offset):
     """Edge cases: rows shorter than one 16-byte vector, odd vocabularies
     (rows start at any 2-byte offset), base pointers that are not 16-byte
     aligned, ties (repeated maxima), vocabularies at both sides of each
-    register-resident row form's capacity, and vocabularies past the largest
-    one (the looping register form)."""
+    register-resident row form's capacity, vocabularies past the largest
+    one (the looping register form), and enough rows for the streaming form
+    (one CTA per SM, two rows in flight) at both sides of its capacity."""
     r = rng(30 + V + offset)
     logits = r.standard_normal((rows, V)).astype(np.float16)
     logits[::3, V // 2] = 8.0
