@@ -253,20 +253,11 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Register-resident span reduction (the row form): columns [c0, c1) of one
-// row (lr = row pointer) are reduced by a block of
-// THREADS threads holding up to THREADS x VPT 16-byte vectors in registers,
-// every load issued before any arithmetic; the up to 7 columns before the
-// first 16-byte boundary and after the last whole vector are one per
-// thread. Returns, in thread 0, the span's max, the lowest column holding
-// it and sum exp(l - max) (0 without calc_prob); an empty span gives
-// (-inf, INT_MAX, 0).
-struct Partial {
-  float m;
-  float s;
-  int id;
-};
-
+// Register-resident row spans: columns [c0, c1) of one row (lr = row
+// pointer) held by a block of THREADS threads as up to THREADS x VPT
+// 16-byte vectors, every load issued before any arithmetic; the up to 7
+// columns before the first 16-byte boundary and after the last whole vector
+// are one per thread. Padding vector lanes hold -inf.
 // A span's loads in flight: whole 16-byte vectors in u[], the head and tail
 // columns one per thread.
 template <int VPT>
@@ -295,123 +286,131 @@ __device__ __forceinline__ void load_span(SpanRegs<VPT> &r, const half *__restri
   r.xt = r.t0 + tid < c1 ? __half2float(lr[r.t0 + tid]) : -INFINITY;
 }
 
+// Single-barrier row reduction over register-resident spans. Each warp
+// reduces its own columns to (warp max m_w, lowest column holding m_w,
+// sum exp(l - m_w)); after one barrier warp 0 merges the warps:
+// M = max m_w, id = lowest column among warps with m_w == M,
+// sum = sum_w s_w * exp(m_w - M). Per logit: half a packed fp16 max, one
+// conversion, half a packed fp32 FMA (l*log2e - m_w*log2e), one ex2 on the
+// special-function unit and half a packed fp32 add; padding lanes hold -inf
+// and contribute exp(-inf) = 0, so the vector loop has no bounds checks.
+// Only lanes whose own max equals their warp's max scan their values for
+// its first column. `slot` is THREADS/32 shared entries; a caller that
+// reuses it for the next row alternates two sets (the barrier of row i+1
+// orders warp 0's reads of row i before any write of row i+2).
+struct WarpPart {
+  float m, s;
+  int id;
+};
+
+__device__ __forceinline__ void fadd2(float2 &acc, float2 v) {
+  uint64_t d = (static_cast<uint64_t>(__float_as_uint(acc.y)) << 32) | __float_as_uint(acc.x);
+  const uint64_t x = (static_cast<uint64_t>(__float_as_uint(v.y)) << 32) | __float_as_uint(v.x);
+  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(d) : "l"(x));
+  acc.x = __uint_as_float(static_cast<uint32_t>(d));
+  acc.y = __uint_as_float(static_cast<uint32_t>(d >> 32));
+}
+
 template <int THREADS, int VPT>
-__device__ __forceinline__ Partial reduce_loaded(const SpanRegs<VPT> &r, int c0, int c1,
-                                                 int calc_prob) {
-  __shared__ float red_f[THREADS / 32];
-  __shared__ int red_i[THREADS / 32];
+__device__ __forceinline__ void reduce_row_regs(const SpanRegs<VPT> &r, int V, int calc_prob,
+                                                WarpPart *slot, long long row, int *ids,
+                                                float *prob, float *max_logit) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const bool has_head = tid < r.head;
-  const bool has_tail = r.t0 + tid < c1;
-  // pass 1: max (padding lanes hold -inf; fp16 max is exact)
   half2 m2 = vec_max(r.u[0]);
 #pragma unroll
   for (int k = 1; k < VPT; ++k)
     m2 = __hmax2(m2, vec_max(r.u[k]));
-  float m = fmaxf(fmaxf(__low2float(m2), __high2float(m2)), fmaxf(r.xh, r.xt));
+  const float mt = fmaxf(fmaxf(__low2float(m2), __high2float(m2)), fmaxf(r.xh, r.xt));
+  float mw = mt;
 #pragma unroll
   for (int o = 16; o; o >>= 1)
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if (lane == 0)
-    red_f[warp] = m;
-  __syncthreads();
-  float M = red_f[0];
+    mw = fmaxf(mw, __shfl_xor_sync(0xffffffffu, mw, o));
+  float sw = 0.f;
+  if (calc_prob) {
+    // A warp without columns has m_w = -inf: shift by 0 so every term is
+    // exp(-inf) = 0 rather than NaN.
+    const float mL = mw == -INFINITY ? 0.f : mw * kLog2e;
+    const float2 l2 = make_float2(kLog2e, kLog2e);
+    float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-  for (int w = 1; w < THREADS / 32; ++w)
-    M = fmaxf(M, red_f[w]);
-  __syncthreads();
-  // pass 2: sum of exponentials, first column holding the max
-  const half Mh = __float2half_rn(M);
-  const float mL = M * kLog2e;
-  float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < VPT; ++k) {
+      const uint32_t w[4] = {r.u[k].x, r.u[k].y, r.u[k].z, r.u[k].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 t = make_float2(-mL, -mL);
+        ffma2(t, __half22float2(*reinterpret_cast<const half2 *>(&w[j])), l2);
+        fadd2(acc[j & 1], make_float2(ex2_ftz(t.x), ex2_ftz(t.y)));
+      }
+    }
+    sw = ((acc[0].x + acc[0].y) + (acc[1].x + acc[1].y)) +
+         (ex2_ftz(fmaf(r.xh, kLog2e, -mL)) + ex2_ftz(fmaf(r.xt, kLog2e, -mL)));
+#pragma unroll
+    for (int o = 16; o; o >>= 1)
+      sw += __shfl_xor_sync(0xffffffffu, sw, o);
+  }
+  // Lowest column holding the warp max: head column, then the vectors in
+  // column order, then the tail column of this thread.
   int best = INT_MAX;
-  if (has_head) {
-    sacc[0] += ex2_ftz(fmaf(r.xh, kLog2e, -mL));
-    if (r.xh == M)
-      best = c0 + tid;
-  }
+  if (mt == mw && mw != -INFINITY) {
+    const half Mh = __float2half_rn(mw); // exact: mw is an fp16 value
+    // Compile-time indices only (r.u stays in registers).
+    if (r.xt == mw)
+      best = r.t0 + tid;
 #pragma unroll
-  for (int k = 0; k < VPT; ++k) {
-    const int v = tid + k * THREADS;
-    if (v < r.nvec) {
-      if (calc_prob) {
-        const uint32_t w[4] = {r.u[k].x, r.u[k].y, r.u[k].z, r.u[k].w};
+    for (int k = VPT - 1; k >= 0; --k) {
+      const half *hv = reinterpret_cast<const half *>(&r.u[k]);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 f = __half22float2(*reinterpret_cast<const half2 *>(&w[j]));
-          sacc[j] += ex2_ftz(fmaf(f.x, kLog2e, -mL)) + ex2_ftz(fmaf(f.y, kLog2e, -mL));
-        }
-      }
-      const half2 vm = vec_max(r.u[k]);
-      if (best == INT_MAX && (__heq(__high2half(vm), Mh) || __heq(__low2half(vm), Mh))) {
-        const half *hv = reinterpret_cast<const half *>(&r.u[k]);
-        for (int j = 0; j < 8; ++j)
-          if (__heq(hv[j], Mh)) {
-            best = c0 + r.head + (v << 3) + j;
-            break;
-          }
-      }
+      for (int j = 7; j >= 0; --j)
+        if (__heq(hv[j], Mh))
+          best = r.head + ((tid + k * THREADS) << 3) + j;
     }
+    if (r.xh == mw)
+      best = tid;
   }
-  if (has_tail) {
-    sacc[1] += ex2_ftz(fmaf(r.xt, kLog2e, -mL));
-    if (r.xt == M)
-      best = min(best, r.t0 + tid);
-  }
-  float sum = (sacc[0] + sacc[1]) + (sacc[2] + sacc[3]);
 #pragma unroll
-  for (int o = 16; o; o >>= 1) {
-    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  for (int o = 16; o; o >>= 1)
     best = min(best, __shfl_xor_sync(0xffffffffu, best, o));
-  }
-  if (lane == 0) {
-    red_f[warp] = sum;
-    red_i[warp] = best;
-  }
+  if (lane == 0)
+    slot[warp] = {mw, sw, best};
   __syncthreads();
-  Partial p;
-  p.m = c1 > c0 ? M : -INFINITY;
-  p.s = 0.f;
-  p.id = INT_MAX;
-  if (tid == 0) {
-    float t = 0.f;
-    int b = INT_MAX;
+  if (warp == 0) {
+    constexpr int NW = THREADS / 32;
+    const WarpPart e = lane < NW ? slot[lane] : WarpPart{-INFINITY, 0.f, INT_MAX};
+    float M = e.m;
 #pragma unroll
-    for (int w = 0; w < THREADS / 32; ++w) {
-      t += red_f[w];
-      b = min(b, red_i[w]);
+    for (int o = 16; o; o >>= 1)
+      M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    int b = e.m == M ? e.id : INT_MAX;
+    float t = e.s == 0.f ? 0.f : e.s * ex2_ftz((e.m - M) * kLog2e);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      b = min(b, __shfl_xor_sync(0xffffffffu, b, o));
+      t += __shfl_xor_sync(0xffffffffu, t, o);
     }
-    p.s = c1 > c0 && calc_prob ? t : 0.f;
-    p.id = b;
+    if (lane == 0) {
+      ids[row] = b;
+      max_logit[row] = M;
+      prob[row] = calc_prob ? 1.f / t : 1.f;
+    }
   }
-  // The reduction buffers are reused by the next span of this block.
-  __syncthreads();
-  return p;
-}
-
-template <int THREADS, int VPT>
-__device__ __forceinline__ Partial reduce_span(const half *__restrict__ lr, int c0,
-                                               int c1, int calc_prob) {
-  SpanRegs<VPT> r;
-  load_span<THREADS, VPT>(r, lr, c0, c1);
-  return reduce_loaded<THREADS, VPT>(r, c0, c1, calc_prob);
 }
 
 // Row form: one block per row, the whole row in registers (V <= 8 x THREADS
-// x VPT - 8).
+// x VPT - 8), one barrier.
 template <int THREADS, int VPT>
 __global__ void __launch_bounds__(THREADS)
     logits_argmax_row_kernel(const half *__restrict__ logits, int V,
                              int *__restrict__ ids, float *__restrict__ prob,
                              float *__restrict__ max_logit, int calc_prob) {
+  __shared__ WarpPart slot[THREADS / 32];
   const long long row = blockIdx.x;
-  const Partial p = reduce_span<THREADS, VPT>(logits + row * V, 0, V, calc_prob);
-  if (threadIdx.x == 0) {
-    ids[row] = p.id;
-    max_logit[row] = p.m;
-    prob[row] = calc_prob ? 1.f / p.s : 1.f;
-  }
+  SpanRegs<VPT> r;
+  load_span<THREADS, VPT>(r, logits + row * V, 0, V);
+  reduce_row_regs<THREADS, VPT>(r, V, calc_prob, slot, row, ids, prob, max_logit);
 }
+
+
+
 
 } // namespace
 
@@ -423,10 +422,13 @@ cudaError_t logits_argmax_prob(const half *logits, int rows, int V, int *ids,
   if (V <= 0 || !ids || !prob || !max_logit)
     return cudaErrorInvalidValue;
   // Row form: the whole row in one block's registers, every load issued
-  // before any arithmetic (measured on B200 at BASELINE config 1: 18.4 us
-  // for 1,280 x 18,385 logits, against 24.6 us for a persistent
-  // shared-memory ring of bulk copies and 32.8 us for a row split over a
-  // thread-block cluster).
+  // before any arithmetic, one barrier (measured on B200 at BASELINE config
+  // 1, 1,280 x 18,385 logits: 16.4 us by CUDA events, 13.3 us of device
+  // time under ncu; the three-barrier form took 19.3 us, persistent forms
+  // with the next row's loads in flight 20.7 us (two CTAs per SM, register
+  // buffers) and 24.6 us (shared-memory ring of bulk copies), a row split
+  // over a thread-block cluster 32.8 us, and computing a quarter of the
+  // exponentials on the FMA pipe 17.9 us).
   auto row_form = [&](auto kernel, int threads) {
     kernel<<<rows, threads, 0, s>>>(logits, V, ids, prob, max_logit, calc_prob);
     return cudaGetLastError();

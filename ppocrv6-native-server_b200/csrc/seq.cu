@@ -55,6 +55,77 @@ __global__ void __launch_bounds__(256)
                             __half2float(bias[j]));
 }
 
+// Vectorised LayerNorm for cols = 8 * v8 with v8 <= LPR: a row is held in
+// registers as 16-byte vectors by a group of LPR lanes (a warp holds 32/LPR
+// rows), every warp loading RPW row groups before any arithmetic. Same
+// formula as layernorm_kernel (fp32 mean, then the mean of squared
+// deviations, y = (x - mean) * rsqrt(var + eps) * scale + bias, one fp16
+// rounding); only the order of the fp32 sums differs.
+template <int LPR, int RPW>
+__global__ void __launch_bounds__(256)
+    layernorm_vec_kernel(const half *__restrict__ x, const half *__restrict__ scale,
+                         const half *__restrict__ bias, half *__restrict__ y,
+                         int rows, int cols, float eps) {
+  constexpr int GPW = 32 / LPR; // row groups per warp
+  const int lane = threadIdx.x & 31;
+  const int sub = lane / LPR, l = lane % LPR;
+  const bool on = l < (cols >> 3);
+  const long long row0 = (static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5)) * GPW * RPW;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  uint4 u[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const long long row = row0 + r * GPW + sub;
+    u[r] = on && row < rows ? __ldg(reinterpret_cast<const uint4 *>(x + row * cols) + l) : zero;
+  }
+  const uint4 su = on ? __ldg(reinterpret_cast<const uint4 *>(scale) + l) : zero;
+  const uint4 bu = on ? __ldg(reinterpret_cast<const uint4 *>(bias) + l) : zero;
+  const half2 *sh = reinterpret_cast<const half2 *>(&su);
+  const half2 *bh = reinterpret_cast<const half2 *>(&bu);
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const long long row = row0 + r * GPW + sub;
+    const half2 *xh = reinterpret_cast<const half2 *>(&u[r]);
+    float f[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 t = __half22float2(xh[e]);
+      f[2 * e] = t.x;
+      f[2 * e + 1] = t.y;
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      s += f[e];
+#pragma unroll
+    for (int o = LPR / 2; o; o >>= 1)
+      s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s / cols;
+    float v = 0.f;
+    if (on)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = f[e] - mean;
+        v += d * d;
+      }
+#pragma unroll
+    for (int o = LPR / 2; o; o >>= 1)
+      v += __shfl_xor_sync(0xffffffffu, v, o);
+    const float inv = rsqrtf(v / cols + eps);
+    if (on && row < rows) {
+      uint4 o;
+      half2 *oh = reinterpret_cast<half2 *>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 sc = __half22float2(sh[e]), bi = __half22float2(bh[e]);
+        oh[e] = __floats2half2_rn((f[2 * e] - mean) * inv * sc.x + bi.x,
+                                  (f[2 * e + 1] - mean) * inv * sc.y + bi.y);
+      }
+      *(reinterpret_cast<uint4 *>(y + row * cols) + l) = o;
+    }
+  }
+}
+
 __global__ void __launch_bounds__(256)
     softmax_kernel(const half *__restrict__ x, half *__restrict__ y, int rows,
                    int cols) {
@@ -294,6 +365,125 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Fixed-length attention (seq == SEQ, head_dim <= 16), one line per block,
+// one thread per (head, query) row: the same arithmetic as
+// attention_rows_kernel below (q' = round(q*scale); S = round(q'.k) with the
+// even and odd dimensions summed in two fp32 chains; P = round(exp(S - max)
+// * (1/sum)); O = round(sum_j P_j v_j), j ascending), with q', K and V
+// staged once in shared memory as fp32 ([head][pos][16], zero-padded) so
+// every multiply-add pair is one packed fp32 FMA (fma.rn.f32x2 rounds each
+// lane like fmaf: bit-identical results) fed by 16-byte shared loads, and
+// the score row a fixed-size register array. The line's rows are read with
+// 16-byte loads when the row width allows.
+template <int SEQ>
+__global__ void __launch_bounds__(512)
+    attention_f32_kernel(const half *__restrict__ qkv, half *__restrict__ out,
+                         int heads, int dh, float scale, FastDiv by_dh, int vec) {
+  constexpr int DP = 16;
+  extern __shared__ float4 att32_smem[];
+  float *qs = reinterpret_cast<float *>(att32_smem); // [heads][SEQ][DP]
+  float *ks = qs + heads * SEQ * DP;
+  float *vs = ks + heads * SEQ * DP;
+  const int hd = heads * dh;
+  const int width = 3 * hd;
+  const long long line = blockIdx.x;
+  const half *src = qkv + line * SEQ * width;
+  const int tid = threadIdx.x;
+  // Padding dimensions d in [dh, 16) of q', K and V are zero.
+  for (int e = tid; e < 3 * heads * SEQ * (DP - dh); e += blockDim.x) {
+    const int r = e / (DP - dh);
+    qs[r * DP + dh + (e - r * (DP - dh))] = 0.f;
+  }
+  auto put = [&](int c, int j, float v) {
+    const int sec = c >= 2 * hd ? 2 : c >= hd ? 1 : 0;
+    const uint32_t cc = static_cast<uint32_t>(c - sec * hd);
+    const uint32_t h = by_dh.div(cc), d = cc - h * dh;
+    if (sec == 0)
+      v = round_half(v * scale);
+    qs[sec * heads * SEQ * DP + (h * SEQ + j) * DP + d] = v;
+  };
+  if (vec) {
+    // width is a multiple of 8: whole 16-byte groups of one row
+    const int groups = width >> 3;
+    for (int e = tid; e < SEQ * groups; e += blockDim.x) {
+      const int j = e / groups, c8 = (e - j * groups) * 8;
+      const uint4 u = __ldg(reinterpret_cast<const uint4 *>(src + j * width + c8));
+      const half2 *h2 = reinterpret_cast<const half2 *>(&u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h2[i]);
+        put(c8 + 2 * i, j, f.x);
+        put(c8 + 2 * i + 1, j, f.y);
+      }
+    }
+  } else {
+    for (int e = tid; e < SEQ * width; e += blockDim.x) {
+      const int j = e / width;
+      put(e - j * width, j, __half2float(src[e]));
+    }
+  }
+  __syncthreads();
+  const int row = tid;
+  if (row >= heads * SEQ)
+    return;
+  const int h = row / SEQ, i = row - h * SEQ;
+  const float4 *q4 = reinterpret_cast<const float4 *>(qs + row * DP);
+  float2 q[8];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const float4 v = q4[t];
+    q[2 * t] = make_float2(v.x, v.y);
+    q[2 * t + 1] = make_float2(v.z, v.w);
+  }
+  const float4 *k4 = reinterpret_cast<const float4 *>(ks + h * SEQ * DP);
+  float sc[SEQ];
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < SEQ; ++j) {
+    float2 e = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float4 kv = k4[j * 4 + t];
+      ffma2(e, q[2 * t], make_float2(kv.x, kv.y));
+      ffma2(e, q[2 * t + 1], make_float2(kv.z, kv.w));
+    }
+    sc[j] = round_half(e.x + e.y);
+    m = fmaxf(m, sc[j]);
+  }
+  const float mL = m * kLog2e;
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < SEQ; ++j) {
+    sc[j] = ex2_ftz(fmaf(sc[j], kLog2e, -mL));
+    sum += sc[j];
+  }
+  const float inv = 1.f / sum;
+  float2 o[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t)
+    o[t] = make_float2(0.f, 0.f);
+  const float4 *v4 = reinterpret_cast<const float4 *>(vs + h * SEQ * DP);
+#pragma unroll
+  for (int j = 0; j < SEQ; ++j) {
+    const float p = round_half(sc[j] * inv);
+    const float2 pp = make_float2(p, p);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float4 vv = v4[j * 4 + t];
+      ffma2(o[2 * t], pp, make_float2(vv.x, vv.y));
+      ffma2(o[2 * t + 1], pp, make_float2(vv.z, vv.w));
+    }
+  }
+  half *dst = out + (line * SEQ + i) * hd + h * dh;
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    if (2 * t < dh)
+      dst[2 * t] = __float2half_rn(o[t].x);
+    if (2 * t + 1 < dh)
+      dst[2 * t + 1] = __float2half_rn(o[t].y);
+  }
+}
+
 // Short-sequence attention (seq <= SMAX, head_dim <= 16), one line per
 // block, one thread per (head, query) row doing the whole row: the line's
 // q' = round(q*scale), K and V are staged in shared memory ([head][pos][16],
@@ -424,6 +614,23 @@ cudaError_t layernorm(const half *x, const half *scale, const half *bias,
                       half *y, int rows, int cols, float eps, cudaStream_t s) {
   if (rows <= 0)
     return cudaSuccess;
+  const bool vec = cols % 8 == 0 && cols > 32 && cols <= 256 &&
+                   ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+                     reinterpret_cast<uintptr_t>(scale) | reinterpret_cast<uintptr_t>(bias)) & 15) == 0;
+  if (vec) {
+    constexpr int RPW = 4;
+    auto launch = [&](auto kernel, int lpr) {
+      const long long per_block = 8LL * (32 / lpr) * RPW;
+      kernel<<<static_cast<unsigned>((rows + per_block - 1) / per_block), 256, 0, s>>>(
+          x, scale, bias, y, rows, cols, eps);
+      return cudaGetLastError();
+    };
+    if (cols <= 64)
+      return launch(layernorm_vec_kernel<8, RPW>, 8);
+    if (cols <= 128)
+      return launch(layernorm_vec_kernel<16, RPW>, 16);
+    return launch(layernorm_vec_kernel<32, RPW>, 32);
+  }
   layernorm_kernel<<<rows_blocks(rows), 256, 0, s>>>(x, scale, bias, y, rows,
                                                      cols, eps);
   return cudaGetLastError();
@@ -468,6 +675,21 @@ cudaError_t attention(const half *qkv, half *out, int lines, int seq, int heads,
                       int dh, float scale, cudaStream_t s) {
   if (lines <= 0)
     return cudaSuccess;
+  if (dh <= 16 && seq == 40 && heads * 40 <= 512) {
+    const int threads = (heads * 40 + 31) / 32 * 32;
+    const size_t smem = sizeof(float) * 3ull * heads * 40 * 16;
+    const int vec = (3 * heads * dh) % 8 == 0 && (reinterpret_cast<uintptr_t>(qkv) & 15) == 0;
+    if (smem <= 200 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(attention_f32_kernel<40>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+      if (e != cudaSuccess)
+        return e;
+      attention_f32_kernel<40><<<lines, threads, smem, s>>>(qkv, out, heads, dh, scale,
+                                                            FastDiv(dh), vec);
+      return cudaGetLastError();
+    }
+  }
   if (dh <= 16 && seq <= 64) {
     const int rows = heads * seq;
     const int threads = rows >= 512 ? 512 : (rows + 31) / 32 * 32;
