@@ -463,6 +463,8 @@ def op_bytes(g, index: int) -> float:
         if k in ("in", "w", "b", "scale", "bias", "add", "a") or (k == "res" and v >= 0):
             if isinstance(v, int) and v >= 0:
                 ids.add(v)
+            elif isinstance(v, list):
+                ids.update(i for i in v if isinstance(i, int) and i >= 0)
     ids.add(layer["out"])
     total = 0
     for i in ids:

@@ -107,6 +107,14 @@ int ppocr_b200_resize_nearest_nhwc(const void *x, const void *addend, void *y,
 // Runtime::concat (runtime.cuh:901-915): y[r] = [a[r] | b[r]].
 int ppocr_b200_concat(const void *a, const void *b, void *y, long long rows,
                       int na, int nb, cudaStream_t stream);
+// The FPN tail of the DB detector (export.py emits it as Resize (nearest,
+// runtime.cuh:461-468) per pyramid level followed by a chain of Concat ops,
+// runtime.cuh:901-915) in one pass: y[n][h][w][:] = concat over k of
+// srcs[k] nearest-upsampled from heights[k] x widths[k] to oh x ow (same
+// asymmetric/floor mapping), channels[k] multiples of 8, 1..8 sources.
+int ppocr_b200_upsample_concat_nhwc(const void *const *srcs, const int *channels,
+                                    const int *heights, const int *widths, int nsrc, void *y,
+                                    int batch, int oh, int ow, cudaStream_t stream);
 // Runtime::transpose fast path (runtime.cuh:838-885): [batch][rows][cols] ->
 // [batch][cols][rows].
 int ppocr_b200_transpose(const void *x, void *y, int batch, int rows, int cols,

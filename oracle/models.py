@@ -56,6 +56,16 @@ def run_graph(g, x_nchw: np.ndarray, output_id: int, capture: set | None = None)
             y = L.resize_nearest_nhwc(get(layer["in"]), out_shape[1], out_shape[2], *layer["scale"])
         elif op == "concat":
             y = torch.cat([get(layer["a"]), get(layer["b"])], dim=-1)
+        elif op == "upsample_concat":
+            # Runtime::upsample_concat_nhwc: each source nearest-resized to
+            # the output size (resize_nhwc_kernel mapping), then concatenated.
+            oh, ow = g.tensors[layer["out"]].shape[1:3]
+            parts = []
+            for i in layer["in"]:
+                x = get(i)
+                parts.append(L.resize_nearest_nhwc(x, oh, ow, np.float32(oh) / np.float32(x.shape[1]),
+                                                   np.float32(ow) / np.float32(x.shape[2])))
+            y = torch.cat(parts, dim=-1)
         elif op == "deconv":
             y = L.deconv_kxk(get(layer["in"]), _w(g, layer["w"]), _w(g, layer["b"]), layer["act"])
         else:

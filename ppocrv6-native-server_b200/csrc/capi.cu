@@ -338,6 +338,28 @@ int ppocr_b200_concat(const void *a, const void *b, void *y, long long rows,
   return status(concat_rows(H(a), H(b), Hm(y), rows, na, nb, stream), "concat");
 }
 
+int ppocr_b200_upsample_concat_nhwc(const void *const *srcs, const int *channels,
+                                    const int *heights, const int *widths, int nsrc, void *y,
+                                    int batch, int oh, int ow, cudaStream_t stream) {
+  g_error.clear();
+  if (!srcs || !channels || !heights || !widths || !y || nsrc < 1 || nsrc > kUpcatMax ||
+      batch < 0 || oh <= 0 || ow <= 0)
+    return fail("invalid upsample_concat arguments");
+  UpcatArgs a{};
+  a.n = nsrc;
+  for (int k = 0; k < nsrc; ++k) {
+    if (heights[k] <= 0 || widths[k] <= 0)
+      return fail("invalid upsample_concat source size");
+    a.src[k] = H(srcs[k]);
+    a.C[k] = channels[k];
+    a.H[k] = heights[k];
+    a.W[k] = widths[k];
+    a.sh[k] = static_cast<float>(oh) / heights[k];
+    a.sw[k] = static_cast<float>(ow) / widths[k];
+  }
+  return status(upsample_concat_nhwc(a, Hm(y), batch, oh, ow, stream), "upsample_concat");
+}
+
 int ppocr_b200_transpose(const void *x, void *y, int batch, int rows, int cols,
                          cudaStream_t stream) {
   g_error.clear();

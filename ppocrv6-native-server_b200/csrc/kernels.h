@@ -141,6 +141,17 @@ cudaError_t pad_nchw(const half *x, half *y, int planes, int H, int W, int OH,
                      int OW, int PH, int PW, cudaStream_t stream);
 // Nearest-neighbour resize (asymmetric coordinates, floor), optional fused add
 // of `addend` (same shape as y): y = round(round(resize(x)) + addend).
+// Up to kUpcatMax NHWC sources, each nearest-upsampled (resize mapping) to
+// OH x OW and concatenated along channels into y (channels multiples of 8).
+constexpr int kUpcatMax = 8;
+struct UpcatArgs {
+  const half *src[kUpcatMax];
+  int C[kUpcatMax], H[kUpcatMax], W[kUpcatMax];
+  float sh[kUpcatMax], sw[kUpcatMax];
+  int n;
+};
+cudaError_t upsample_concat_nhwc(const UpcatArgs &a, half *y, int batch, int OH, int OW,
+                                 cudaStream_t s);
 cudaError_t resize_nearest_nhwc(const half *x, const half *addend, half *y,
                                 int batch, int C, int H, int W, int OH, int OW,
                                 float scale_h, float scale_w,

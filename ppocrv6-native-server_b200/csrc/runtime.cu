@@ -467,6 +467,39 @@ void Runtime::resize_nearest_nhwc(int a, int y, Shape xs, Shape ys, float sh,
   });
 }
 
+void Runtime::upsample_concat_nhwc(std::vector<int> srcs, int y, std::vector<Shape> xs,
+                                   Shape ys) {
+  if (srcs.empty() || srcs.size() != xs.size() || static_cast<int>(srcs.size()) > pb2::kUpcatMax ||
+      ys.size() != 4)
+    throw std::runtime_error("upsample_concat_nhwc: 1.." + std::to_string(pb2::kUpcatMax) +
+                             " sources with one shape each");
+  int ctot = 0;
+  for (size_t k = 0; k < srcs.size(); ++k) {
+    const Shape &x = xs[k];
+    if (x.size() != 4 || x[0] != ys[0] || x[1] % 8 || x[2] <= 0 || x[3] <= 0)
+      throw std::runtime_error("upsample_concat_nhwc: source " + std::to_string(k) + " shape " +
+                               shape_str(x));
+    ctot += x[1];
+  }
+  if (ctot != ys[1])
+    throw std::runtime_error("upsample_concat_nhwc: channels do not add up to " + shape_str(ys));
+  for (int id : srcs)
+    reads({id});
+  add("upsample_concat_nhwc", [=] {
+    pb2::UpcatArgs a{};
+    a.n = static_cast<int>(srcs.size());
+    for (int k = 0; k < a.n; ++k) {
+      a.src[k] = t[srcs[k]];
+      a.C[k] = xs[k][1];
+      a.H[k] = xs[k][2];
+      a.W[k] = xs[k][3];
+      a.sh[k] = static_cast<float>(ys[2]) / xs[k][2];
+      a.sw[k] = static_cast<float>(ys[3]) / xs[k][3];
+    }
+    check(pb2::upsample_concat_nhwc(a, t[y], ys[0], ys[2], ys[3], stream), "upsample_concat_nhwc");
+  });
+}
+
 void Runtime::resize_nearest_add_nhwc(int a, int addend, int y, Shape xs,
                                       Shape ys, float sh, float sw) {
   reads({a, addend});

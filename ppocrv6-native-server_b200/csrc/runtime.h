@@ -17,7 +17,7 @@
 // Extensions (not in the reference API): activation codes 3..6 on conv and
 // gemm_epilogue (kernels.h / ptx.cuh), conv bias/activation for every conv
 // kind (the reference honours them for depthwise only), deconv bias and
-// activation, attention(), resize_nearest_add_nhwc().
+// activation, attention(), resize_nearest_add_nhwc(), upsample_concat_nhwc().
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -119,6 +119,10 @@ struct Runtime {
   // FPN step: y = nearest_resize(a) + addend (NHWC, logical NCHW shapes).
   void resize_nearest_add_nhwc(int a, int addend, int y, Shape xs, Shape ys,
                                float sh, float sw);
+  // FPN tail: y = concat over channels of each source nearest-upsampled to
+  // ys (scale = ys / xs per source), the resize_nearest_nhwc + concat chain
+  // in one pass (NHWC, logical NCHW shapes, channels multiples of 8).
+  void upsample_concat_nhwc(std::vector<int> srcs, int y, std::vector<Shape> xs, Shape ys);
 
   // Runs `prepare` once, then ops[first_op..] in order on `stream`.
   void run();

@@ -1033,6 +1033,80 @@ __global__ void __launch_bounds__(kBlock)
   }
 }
 
+// FPN tail in one pass: y[n, h, w, :] = [src_0(n, h, w) | src_1 up | ...],
+// each source nearest-upsampled by its own scale with the resize kernel's
+// mapping (src = min(floor(dst / scale), n - 1)), so the result equals the
+// chain of resize_nearest_nhwc + concat launches bit for bit while the
+// concatenated tensor is written once and no intermediate is. Thread = one
+// 16-byte group of 8 output channels; consecutive threads walk a pixel's
+// channel groups.
+__global__ void __launch_bounds__(kBlock)
+    upsample_concat_kernel(const __grid_constant__ UpcatArgs a, half *__restrict__ y,
+                           uint32_t total, FastDiv by_groups, FastDiv by_ow, FastDiv by_oh) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total)
+    return;
+  const uint32_t p = by_groups.div(i);
+  int c = static_cast<int>(i - p * by_groups.d) * 8;
+  const uint32_t r = by_ow.div(p);
+  const int ow = static_cast<int>(p - r * by_ow.d);
+  const uint32_t n = by_oh.div(r);
+  const int oh = static_cast<int>(r - n * by_oh.d);
+  // Source selection with compile-time parameter indices only (a lane-
+  // dependent index into the parameter block serialises the warp).
+  const half *base = a.src[0];
+  int C = a.C[0], H = a.H[0], W = a.W[0];
+  float sh = a.sh[0], sw = a.sw[0];
+#pragma unroll
+  for (int k = 1; k < kUpcatMax; ++k)
+    if (k < a.n && c >= C) {
+      c -= C;
+      base = a.src[k];
+      C = a.C[k];
+      H = a.H[k];
+      W = a.W[k];
+      sh = a.sh[k];
+      sw = a.sw[k];
+    }
+  const int sr = min(static_cast<int>(floorf(oh / sh)), H - 1);
+  const int sc = min(static_cast<int>(floorf(ow / sw)), W - 1);
+  const half *src = base + ((static_cast<long long>(n) * H + sr) * W + sc) * C + c;
+  reinterpret_cast<uint4 *>(y)[i] = __ldg(reinterpret_cast<const uint4 *>(src));
+}
+
+// 32-bit-index form of resize_nhwc_kernel for 16-byte channel groups
+// (total < 2^31): the pixel/row/image split by multiply-shift division
+// instead of 64-bit divides; same source mapping and arithmetic.
+__global__ void __launch_bounds__(kBlock)
+    resize_nhwc_vec_kernel(const half *__restrict__ x, const half *__restrict__ addend,
+                           half *__restrict__ y, uint32_t total, int C, int H, int W,
+                           FastDiv by_groups, FastDiv by_ow, FastDiv by_oh, float sh, float sw) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total)
+    return;
+  const uint32_t p = by_groups.div(i);
+  const int g = static_cast<int>(i - p * by_groups.d);
+  const uint32_t rr = by_ow.div(p);
+  const int ow = static_cast<int>(p - rr * by_ow.d);
+  const uint32_t n = by_oh.div(rr);
+  const int oh = static_cast<int>(rr - n * by_oh.d);
+  const int r = min(static_cast<int>(floorf(oh / sh)), H - 1);
+  const int c = min(static_cast<int>(floorf(ow / sw)), W - 1);
+  const long long src = ((static_cast<long long>(n) * H + r) * W + c) * C;
+  Pack8 v;
+  v.u = __ldg(reinterpret_cast<const uint4 *>(x + src + g * 8));
+  if (addend) {
+    Pack8 a;
+    a.u = __ldg(reinterpret_cast<const uint4 *>(addend) + i);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __half22float2(v.h[j]), e = __half22float2(a.h[j]);
+      v.h[j] = __floats2half2_rn(f.x + e.x, f.y + e.y);
+    }
+  }
+  reinterpret_cast<uint4 *>(y)[i] = v.u;
+}
+
 __global__ void __launch_bounds__(kBlock)
     resize_nchw_kernel(const half *__restrict__ x, half *__restrict__ y,
                        long long total, int H, int W, int OH, int OW, float sh,
@@ -1489,8 +1563,37 @@ cudaError_t resize_nearest_nhwc(const half *x, const half *addend, half *y,
       C % 8 == 0 && al16(x) && al16(y) && (!addend || al16(addend));
   const long long total =
       static_cast<long long>(batch) * OH * OW * (vec ? C / 8 : C);
+  if (vec && total < (1LL << 31)) {
+    resize_nhwc_vec_kernel<<<blocks_for(total), kBlock, 0, s>>>(
+        x, addend, y, static_cast<uint32_t>(total), C, H, W,
+        FastDiv(static_cast<uint32_t>(C / 8)), FastDiv(static_cast<uint32_t>(OW)),
+        FastDiv(static_cast<uint32_t>(OH)), sh, sw);
+    return cudaGetLastError();
+  }
   resize_nhwc_kernel<<<blocks_for(total), kBlock, 0, s>>>(
       x, addend, y, total, C, H, W, OH, OW, sh, sw, vec);
+  return cudaGetLastError();
+}
+
+cudaError_t upsample_concat_nhwc(const UpcatArgs &a, half *y, int batch, int OH, int OW,
+                                 cudaStream_t s) {
+  if (a.n < 1 || a.n > kUpcatMax || !al16(y))
+    return cudaErrorInvalidValue;
+  long long ctot = 0;
+  for (int k = 0; k < a.n; ++k) {
+    if (!a.src[k] || a.C[k] <= 0 || a.C[k] % 8 || !al16(a.src[k]) || a.H[k] <= 0 || a.W[k] <= 0 ||
+        !(a.sh[k] > 0.f) || !(a.sw[k] > 0.f))
+      return cudaErrorInvalidValue;
+    ctot += a.C[k];
+  }
+  if (batch <= 0 || OH <= 0 || OW <= 0)
+    return cudaSuccess;
+  const long long total = static_cast<long long>(batch) * OH * OW * (ctot / 8);
+  if (total >= (1LL << 31))
+    return cudaErrorInvalidValue;
+  upsample_concat_kernel<<<blocks_for(total), kBlock, 0, s>>>(
+      a, y, static_cast<uint32_t>(total), FastDiv(static_cast<uint32_t>(ctot / 8)),
+      FastDiv(static_cast<uint32_t>(OW)), FastDiv(static_cast<uint32_t>(OH)));
   return cudaGetLastError();
 }
 

@@ -53,6 +53,7 @@ SIGNATURES = {
     "ppocr_b200_pad_nhwc": (I, [V, V, I, I, I, I, I, I, I, I, V]),
     "ppocr_b200_resize_nearest_nhwc": (I, [V, V, V, I, I, I, I, I, I, F, F, V]),
     "ppocr_b200_concat": (I, [V, V, V, L, I, I, V]),
+    "ppocr_b200_upsample_concat_nhwc": (I, [V, V, V, V, I, V, I, I, I, V]),
     "ppocr_b200_transpose": (I, [V, V, I, I, I, V]),
     "ppocr_b200_unary": (I, [V, V, L, I, F, F, V]),
     "ppocr_b200_binary_flat": (I, [V, V, V, L, I, I, I, I, I, V]),

@@ -402,7 +402,7 @@ def build_neck(spec: dict, batch: int, seed: int):
     return g, x
 
 
-def build_detector(spec: dict, batch: int, size: int, seed: int):
+def build_detector(spec: dict, batch: int, size: int, seed: int, fused_fpn_tail: bool = True):
     """Backbone at strides 2..32 + FPN(256) + DB head -> sigmoid map [B,1,S,S]."""
     g = Graph((batch, 3, size, size))
     bd = Builder(g, Init(seed))
@@ -434,24 +434,36 @@ def build_detector(spec: dict, batch: int, size: int, seed: int):
              {"op": "resize_add", "in": td[i + 1], "add": lat[i], "out": y, "scale": [sh, sw]})
         td[i] = y
     outs = [bd.conv_bn_act(t, fpn // 4, 3, act="none") for t in td]
-    # Upsample each level to the finest and concatenate channels.
+    # Upsample each level to the finest and concatenate channels. The
+    # exporter writes this as one Resize per level and a chain of Concats;
+    # with fused_fpn_tail the graph carries the Runtime extension that does
+    # both in one pass (the same values; no intermediate tensors).
     b, h0, w0, c0 = g.tensors[outs[0]].shape
-    ups = [outs[0]]
-    for o in outs[1:]:
-        _, h, w, c = g.tensors[o].shape
-        y = g.act(bd._name("up"), (b, h0, w0, c))
-        g.op([o], y, f"r.resize_nearest_nhwc({o},{y},{vec((b, c, h, w))},{vec((b, c, h0, w0))},"
-                     f"{flit(h0 / h)},{flit(w0 / w)});",
-             {"op": "resize", "in": o, "out": y, "scale": [h0 / h, w0 / w]})
-        ups.append(y)
-    cat = ups[0]
-    width = c0
-    for u in ups[1:]:
-        cu = g.tensors[u].shape[-1]
-        y = g.act(bd._name("cat"), (b, h0, w0, width + cu))
-        g.op([cat, u], y, f"r.concat({cat},{u},{y},{b * h0 * w0},{width},{cu});",
-             {"op": "concat", "a": cat, "b": u, "out": y})
-        cat, width = y, width + cu
+    if fused_fpn_tail:
+        shapes = [g.tensors[o].shape for o in outs]
+        ctot = sum(sh[-1] for sh in shapes)
+        cat = g.act(bd._name("upcat"), (b, h0, w0, ctot))
+        srcs = "{" + ",".join(str(o) for o in outs) + "}"
+        xs = "{" + ",".join(vec((b, sh[3], sh[1], sh[2])) for sh in shapes) + "}"
+        g.op(list(outs), cat, f"r.upsample_concat_nhwc({srcs},{cat},{xs},{vec((b, ctot, h0, w0))});",
+             {"op": "upsample_concat", "in": list(outs), "out": cat})
+    else:
+        ups = [outs[0]]
+        for o in outs[1:]:
+            _, h, w, c = g.tensors[o].shape
+            y = g.act(bd._name("up"), (b, h0, w0, c))
+            g.op([o], y, f"r.resize_nearest_nhwc({o},{y},{vec((b, c, h, w))},{vec((b, c, h0, w0))},"
+                         f"{flit(h0 / h)},{flit(w0 / w)});",
+                 {"op": "resize", "in": o, "out": y, "scale": [h0 / h, w0 / w]})
+            ups.append(y)
+        cat = ups[0]
+        width = c0
+        for u in ups[1:]:
+            cu = g.tensors[u].shape[-1]
+            y = g.act(bd._name("cat"), (b, h0, w0, width + cu))
+            g.op([cat, u], y, f"r.concat({cat},{u},{y},{b * h0 * w0},{width},{cu});",
+                 {"op": "concat", "a": cat, "b": u, "out": y})
+            cat, width = y, width + cu
     head = spec["head"]
     x = bd.conv_bn_act(cat, head, 3)
     for i, (co, act) in enumerate([(head, "relu"), (1, "sigmoid")]):

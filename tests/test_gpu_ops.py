@@ -309,6 +309,20 @@ def test_pools(native, cuda):
     assert torch.equal(host(y2), L.pool_nhwc(x, (2, 2), (1, 1), (0, 0), True))
 
 
+@pytest.mark.parametrize("b,c,h,w,oh,ow", [(1, 24, 13, 7, 32, 20), (3, 16, 5, 5, 40, 35), (2, 8, 9, 9, 9, 9)])
+def test_resize_nearest_shapes(native, cuda, b, c, h, w, oh, ow):
+    """Non-integer and identity scales through the 16-byte-group form."""
+    r = rng(80 + oh)
+    x = f16(r.uniform(-1, 1, (b, h, w, c)))
+    y = torch.empty(b, oh, ow, c, dtype=torch.float16, device=cuda)
+    sh, sw = float(np.float32(oh) / np.float32(h)), float(np.float32(ow) / np.float32(w))
+    dx = dev(x)
+    assert native.ppocr_b200_resize_nearest_nhwc(ptr(dx), None, ptr(y), b, c, h, w, oh, ow, sh, sw,
+                                                 stream_handle()) == 0
+    sync()
+    assert torch.equal(host(y), L.resize_nearest_nhwc(x, oh, ow, sh, sw))
+
+
 def test_resize_add_and_concat(native, cuda):
     r = rng(15)
     x = f16(r.uniform(-1, 1, (2, 15, 15, 64)))
@@ -324,6 +338,32 @@ def test_resize_add_and_concat(native, cuda):
     sync()
     want = torch.cat([a.reshape(-1, 64), L.resize_nearest_nhwc(x, 30, 30, 2.0, 2.0, addend=a).reshape(-1, 64)], 1)
     assert torch.equal(host(c), want)
+
+
+@pytest.mark.parametrize("batch,oh,ow,levels", [
+    (2, 48, 40, [(64, 1), (64, 2), (64, 4), (64, 8)]),   # the DB FPN tail: four levels, factors 1..8
+    (1, 30, 30, [(16, 1), (8, 3), (32, 2)]),             # mixed channel counts, a factor of 3
+    (3, 17, 11, [(8, 1)]),                               # one source: a plain copy
+])
+def test_upsample_concat(native, cuda, batch, oh, ow, levels):
+    """The fused FPN tail equals the chain of nearest resizes + concats bit
+    for bit (same index mapping, pure copies)."""
+    r = rng(70 + oh)
+    xs = [f16(r.uniform(-1, 1, (batch, oh // f, ow // f, c))) for c, f in levels]
+    ds = [dev(x) for x in xs]
+    ctot = sum(c for c, _ in levels)
+    y = torch.full((batch, oh, ow, ctot), float("nan"), dtype=torch.float16, device=cuda)
+    n = len(levels)
+    srcs = (ctypes.c_void_p * n)(*[d.data_ptr() for d in ds])
+    chans = (ctypes.c_int * n)(*[c for c, _ in levels])
+    hs = (ctypes.c_int * n)(*[x.shape[1] for x in xs])
+    ws = (ctypes.c_int * n)(*[x.shape[2] for x in xs])
+    assert native.ppocr_b200_upsample_concat_nhwc(srcs, chans, hs, ws, n, ptr(y), batch, oh, ow,
+                                                  stream_handle()) == 0, native.ppocr_b200_last_error()
+    sync()
+    want = torch.cat([L.resize_nearest_nhwc(x, oh, ow, np.float32(oh) / np.float32(x.shape[1]),
+                                            np.float32(ow) / np.float32(x.shape[2])) for x in xs], -1)
+    assert torch.equal(host(y), want)
 
 
 DECONV_CASES = [
