@@ -1043,6 +1043,22 @@ __global__ void __launch_bounds__(kBlock)
 __global__ void __launch_bounds__(kBlock)
     upsample_concat_kernel(const __grid_constant__ UpcatArgs a, half *__restrict__ y,
                            uint32_t total, FastDiv by_groups, FastDiv by_ow, FastDiv by_oh) {
+  // The source table goes to shared memory once per block: lanes of a warp
+  // pick different sources, and lane-dependent indices into the parameter
+  // block (or selecting through all of it per thread) stall on its loads.
+  __shared__ const half *s_src[kUpcatMax];
+  __shared__ int s_dim[3][kUpcatMax];
+  __shared__ float s_scale[2][kUpcatMax];
+  if (threadIdx.x < kUpcatMax && static_cast<int>(threadIdx.x) < a.n) {
+    const int k = threadIdx.x;
+    s_src[k] = a.src[k];
+    s_dim[0][k] = a.C[k];
+    s_dim[1][k] = a.H[k];
+    s_dim[2][k] = a.W[k];
+    s_scale[0][k] = a.sh[k];
+    s_scale[1][k] = a.sw[k];
+  }
+  __syncthreads();
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total)
     return;
@@ -1052,25 +1068,15 @@ __global__ void __launch_bounds__(kBlock)
   const int ow = static_cast<int>(p - r * by_ow.d);
   const uint32_t n = by_oh.div(r);
   const int oh = static_cast<int>(r - n * by_oh.d);
-  // Source selection with compile-time parameter indices only (a lane-
-  // dependent index into the parameter block serialises the warp).
-  const half *base = a.src[0];
-  int C = a.C[0], H = a.H[0], W = a.W[0];
-  float sh = a.sh[0], sw = a.sw[0];
-#pragma unroll
-  for (int k = 1; k < kUpcatMax; ++k)
-    if (k < a.n && c >= C) {
-      c -= C;
-      base = a.src[k];
-      C = a.C[k];
-      H = a.H[k];
-      W = a.W[k];
-      sh = a.sh[k];
-      sw = a.sw[k];
-    }
-  const int sr = min(static_cast<int>(floorf(oh / sh)), H - 1);
-  const int sc = min(static_cast<int>(floorf(ow / sw)), W - 1);
-  const half *src = base + ((static_cast<long long>(n) * H + sr) * W + sc) * C + c;
+  int k = 0;
+  while (k + 1 < a.n && c >= s_dim[0][k]) {
+    c -= s_dim[0][k];
+    ++k;
+  }
+  const int C = s_dim[0][k], H = s_dim[1][k], W = s_dim[2][k];
+  const int sr = min(static_cast<int>(floorf(oh / s_scale[0][k])), H - 1);
+  const int sc = min(static_cast<int>(floorf(ow / s_scale[1][k])), W - 1);
+  const half *src = s_src[k] + ((static_cast<long long>(n) * H + sr) * W + sc) * C + c;
   reinterpret_cast<uint4 *>(y)[i] = __ldg(reinterpret_cast<const uint4 *>(src));
 }
 
