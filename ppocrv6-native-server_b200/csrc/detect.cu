@@ -194,16 +194,18 @@ __global__ void __launch_bounds__(256)
     for (int k = 0; k < U; ++k) {
       const uint32_t p = pw + k * PPW + lane / G;
       const half2 *h2 = reinterpret_cast<const half2 *>(&u[k]);
-      float acc[NOUT] = {0.f, 0.f, 0.f, 0.f};
+      // Outputs (0, 1) and (2, 3) as two packed fp32 chains: each lane of
+      // fma.rn.f32x2 rounds like fmaf, so the sums are the scalar ones.
+      float2 a01 = make_float2(0.f, 0.f), a23 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 f = __half22float2(h2[j]);
-#pragma unroll
-        for (int o = 0; o < NOUT; ++o) {
-          acc[o] = fmaf(f.x, wr[2 * j][o], acc[o]);
-          acc[o] = fmaf(f.y, wr[2 * j + 1][o], acc[o]);
-        }
+        ffma2(a01, make_float2(f.x, f.x), make_float2(wr[2 * j][0], wr[2 * j][1]));
+        ffma2(a23, make_float2(f.x, f.x), make_float2(wr[2 * j][2], wr[2 * j][3]));
+        ffma2(a01, make_float2(f.y, f.y), make_float2(wr[2 * j + 1][0], wr[2 * j + 1][1]));
+        ffma2(a23, make_float2(f.y, f.y), make_float2(wr[2 * j + 1][2], wr[2 * j + 1][3]));
       }
+      const float acc[NOUT] = {a01.x, a01.y, a23.x, a23.y};
       // Reduce-scatter: keep {0,1} or {2,3}, then one of the pair.
       const float s0 = __shfl_xor_sync(0xffffffffu, hi1 ? acc[0] : acc[2], G / 2);
       const float s1 = __shfl_xor_sync(0xffffffffu, hi1 ? acc[1] : acc[3], G / 2);
