@@ -449,12 +449,73 @@ cudaError_t logits_argmax_prob(const half *logits, int rows, int V, int *ids,
   return cudaGetLastError();
 }
 
+namespace {
+// Merge of the vocabulary partials with four threads per row: thread (r, q)
+// of a 256-thread block takes row blockIdx.x * 64 + r and tiles q, q + 4,
+// ... (loads coalesced across the block's 64 rows), then the four partial
+// (max, lowest id) and, with the row max known, the four partial
+// sum_t s_t * exp(m_t - max) are combined through shared memory. Same
+// formula as vocab_merge_kernel; only the order of the fp32 sum differs.
+__global__ void __launch_bounds__(256)
+    vocab_merge4_kernel(const float *__restrict__ pm, const int *__restrict__ pi,
+                        const float *__restrict__ ps, int rows, int tiles,
+                        int *__restrict__ ids, float *__restrict__ prob,
+                        float *__restrict__ max_logit, int calc_prob) {
+  __shared__ float sm[4][64];
+  __shared__ int si[4][64];
+  const int r = threadIdx.x & 63, q = threadIdx.x >> 6;
+  const int row = blockIdx.x * 64 + r;
+  float m = -FLT_MAX;
+  int id = INT_MAX;
+  if (row < rows)
+    for (int t = q; t < tiles; t += 4) {
+      const float v = pm[static_cast<long long>(t) * rows + row];
+      const int i = pi[static_cast<long long>(t) * rows + row];
+      if (v > m || (v == m && i < id)) {
+        m = v;
+        id = i;
+      }
+    }
+  sm[q][r] = m;
+  si[q][r] = id;
+  __syncthreads();
+  float M = sm[0][r];
+  int I = si[0][r];
+#pragma unroll
+  for (int k = 1; k < 4; ++k)
+    if (sm[k][r] > M || (sm[k][r] == M && si[k][r] < I)) {
+      M = sm[k][r];
+      I = si[k][r];
+    }
+  float s = 0.f;
+  if (calc_prob && row < rows)
+    for (int t = q; t < tiles; t += 4) {
+      const float ts = ps[static_cast<long long>(t) * rows + row];
+      s += ts == 0.f ? 0.f : ts * __expf(pm[static_cast<long long>(t) * rows + row] - M);
+    }
+  __syncthreads();
+  sm[q][r] = s;
+  __syncthreads();
+  if (q == 0 && row < rows) {
+    const float tot = (sm[0][r] + sm[1][r]) + (sm[2][r] + sm[3][r]);
+    ids[row] = I;
+    max_logit[row] = M;
+    prob[row] = calc_prob ? 1.f / tot : 1.f;
+  }
+}
+} // namespace
+
 cudaError_t vocab_merge(const float *part_max, const int *part_id,
                         const float *part_sum, int rows, int tiles, int *ids,
                         float *prob, float *max_logit, int calc_prob,
                         cudaStream_t s) {
   if (rows <= 0)
     return cudaSuccess;
+  if (tiles >= 8) {
+    vocab_merge4_kernel<<<(rows + 63) / 64, 256, 0, s>>>(part_max, part_id, part_sum, rows, tiles,
+                                                       ids, prob, max_logit, calc_prob);
+    return cudaGetLastError();
+  }
   vocab_merge_kernel<<<(rows + 255) / 256, 256, 0, s>>>(
       part_max, part_id, part_sum, rows, tiles, ids, prob, max_logit,
       calc_prob);
