@@ -889,18 +889,34 @@ __global__ void __launch_bounds__(kBlock)
 template <int KH, int KW, int SH, int SW, bool MAXIMUM>
 __global__ void __launch_bounds__(kBlock)
     pool_fixed_kernel(const half *__restrict__ x, half *__restrict__ y,
-                      int batch, int C, int H, int W, int OH, int OW) {
+                      int batch, int C, int H, int W, int OH, int OW,
+                      FastDiv by_groups, FastDiv by_ow, FastDiv by_oh) {
   const int groups = C >> 3;
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(batch) * OH * OW * groups;
   if (i >= total)
     return;
-  const int g = static_cast<int>(i % groups);
-  long long t = i / groups;
-  const int ow = static_cast<int>(t % OW);
-  t /= OW;
-  const int oh = static_cast<int>(t % OH);
-  const long long n = t / OH;
+  int g, ow, oh;
+  long long n;
+  if (total < (1LL << 31)) {
+    // 32-bit multiply-shift division (a 64-bit divide costs dozens of
+    // instructions per 16-byte output).
+    const uint32_t i32 = static_cast<uint32_t>(i);
+    const uint32_t p = by_groups.div(i32);
+    g = static_cast<int>(i32 - p * by_groups.d);
+    const uint32_t r = by_ow.div(p);
+    ow = static_cast<int>(p - r * by_ow.d);
+    const uint32_t q = by_oh.div(r);
+    oh = static_cast<int>(r - q * by_oh.d);
+    n = q;
+  } else {
+    g = static_cast<int>(i % groups);
+    long long t = i / groups;
+    ow = static_cast<int>(t % OW);
+    t /= OW;
+    oh = static_cast<int>(t % OH);
+    n = t / OH;
+  }
   const half *base = x + ((n * H + oh * SH) * W + ow * SW) * C + g * 8;
   Pack8 v[KH * KW];
 #pragma unroll
@@ -1514,12 +1530,14 @@ cudaError_t pool_nhwc(const half *x, half *y, int batch, int C, int H, int W,
     const long long total = static_cast<long long>(batch) * OH * OW * (C / 8);
     if (!maximum && KH == 3 && KW == 2 && SH == 3 && SW == 2) {
       pool_fixed_kernel<3, 2, 3, 2, false><<<blocks_for(total), kBlock, 0, s>>>(
-          x, y, batch, C, H, W, OH, OW);
+          x, y, batch, C, H, W, OH, OW, FastDiv(static_cast<uint32_t>(C / 8)),
+          FastDiv(static_cast<uint32_t>(OW)), FastDiv(static_cast<uint32_t>(OH)));
       return cudaGetLastError();
     }
     if (maximum && KH == 2 && KW == 2 && SH == 1 && SW == 1) {
       pool_fixed_kernel<2, 2, 1, 1, true><<<blocks_for(total), kBlock, 0, s>>>(
-          x, y, batch, C, H, W, OH, OW);
+          x, y, batch, C, H, W, OH, OW, FastDiv(static_cast<uint32_t>(C / 8)),
+          FastDiv(static_cast<uint32_t>(OW)), FastDiv(static_cast<uint32_t>(OH)));
       return cudaGetLastError();
     }
   }
