@@ -1,18 +1,30 @@
-"""Benchmark: recognized lines/sec (48x320 FP16) of the full recognizer.
+"""Benchmark: recognized lines/sec (48x320 FP16) and page p50 latency @960^2.
 
 One step = one forward of BASELINE config 4 on a batch of 512 synthetic line
 images per GPU (HGNet-style backbone, SVTR neck, fused CTC vocabulary
 projection + argmax, device CTC collapse) through the Model ABI v2 shell and
 the head C-ABI. Each GPU runs an independent replica (request-batch data
 parallelism, no collective on the hot path; torch.distributed only
-synchronises the timing). `value` is the whole-job lines/s with inputs
-resident in HBM; `e2e` repeats the measurement with the pinned-host input
-copied in and the decoded tokens copied out every step, through the
-double-buffered LineStream (the copy of step k+1 runs during step k).
+synchronises the timing and gathers per-rank figures). `value` is the
+whole-job lines/s with inputs resident in HBM; `e2e` repeats the measurement
+with the pinned-host input copied in and the decoded tokens copied out every
+step, through the double-buffered LineStream (the copy of step k+1 runs
+during step k).
 
-`--impl reference` times the CPU restatement of the same forward (the
-reference has no CPU implementation of its layer path; the oracle port in
-oracle/ is the CPU baseline) on rank 0 only.
+The second half of the BASELINE metric, page p50 latency, follows on every
+rank (`page_p50_ms`, the max over ranks of each rank's p50 over
+--page-runs runs of config 5: 8 pages of 960^2 through the detector +
+binarize and 512 line crops through the recognizer + head + collapse; pages
+sharded: each GPU serves its own 8). `--scaling strong` keeps 512 lines in
+total (512/N per GPU) instead of 512 per GPU. `per_rank` lists each rank's
+step time, median SM clock and page p50, to name a straggler.
+
+The CPU baseline (`cpu_baseline`, the oracle's CPU restatement on the host
+cores) is timed on rank 0 before the ranks join the process group.
+`--impl reference` times the same CPU restatement (the reference has no CPU
+implementation of its layer path; the oracle port in oracle/ is the CPU
+baseline) on rank 0 only. `--config c1|c2|c3|c5|pre|post` measures the other
+configurations on one GPU.
 """
 
 from __future__ import annotations
@@ -50,6 +62,12 @@ def parse():
     p.add_argument("--model", default=MODEL, choices=["rec_b512", "rec_b256", "rec_b64"],
                    help="compiled recognizer shape of the c4 run (rec_b512 = the benchmark; the smaller "
                         "shapes exist for profiling captures and are named in the output's config)")
+    p.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                   help="c4: weak = 512 lines per GPU (rec_b512 on every rank); strong = 512 lines in total split "
+                        "over the GPUs (rec_b512/256/128/64 at N = 1/2/4/8)")
+    p.add_argument("--no-pages", action="store_true",
+                   help="c4: skip the page-latency half of the metric (C5 on every rank after the line timing)")
+    p.add_argument("--page-runs", type=int, default=100, help="c4: timed C5 runs per rank for page_p50_ms")
     p.add_argument("--config", default="c4", choices=["c1", "c2", "c3", "c4", "c5", "pre", "post"],
                    help="c4 (default) is the headline recognizer benchmark; c1/c2/c3/c5 measure the other "
                         "BASELINE configurations (CTC head, conv block, neck, page pipeline) on one GPU; pre "
@@ -157,9 +175,9 @@ class CpuRecognizer:
         self.x = np.random.default_rng(SEED).uniform(-1, 1, (2, 3, H, W)).astype(np.float32)
         spec = models.spec("recognizer")
         hidden, vocab = spec["neck"]["dim"], spec["vocab"]
-        init = modelgen.Init(models.SEED + 1)  # the device head's weights (pipeline.Classifier)
-        self.w = L.rh(torch.from_numpy(init.xavier((hidden, vocab), hidden, vocab)))
-        self.b = L.rh(torch.from_numpy(init.normal((vocab,), 0.0, 0.01)))
+        w, b = models.head_weights(hidden, vocab)  # the device head's weights (pipeline.Classifier)
+        self.w = L.rh(torch.from_numpy(w))
+        self.b = L.rh(torch.from_numpy(b))
         self.lib = ctypes.CDLL(str(REPO / "oracle" / "_build" / "liboracle.so"))
         Pv = ctypes.c_void_p
         self.lib.oracle_ctc_collapse.argtypes = [Pv, Pv, ctypes.c_long, ctypes.c_int, ctypes.c_int, Pv, Pv, Pv]
@@ -232,6 +250,9 @@ def reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+STRONG_MODELS = {1: "rec_b512", 2: "rec_b256", 4: "rec_b128", 8: "rec_b64"}
+
+
 def b200_arm(args):
     import numpy as np
     import torch
@@ -240,6 +261,18 @@ def b200_arm(args):
     from ppocr_b200 import capi, pipeline
 
     rank, world, local = dist_env()
+    # The CPU baselines run first, on rank 0, before any rank joins the
+    # process group: the other ranks wait in the rendezvous (no GPU work, no
+    # busy barrier), so the host cores are not shared with spinning ranks.
+    cpu = cpu_pages = None
+    if rank == 0:
+        cpu_value, cpu_lines, cores = cpu_port_forward(8)
+        cpu = {"value": round(cpu_value, 3), "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"{cpu_lines} lines of the batch through the oracle's CPU restatement "
+                         f"(torch fp32, same graph and weights, vocabulary projection, argmax, collapse), "
+                         f"timed before the GPU ranks start"}
+        if not args.no_pages:
+            cpu_pages = _cpu_c5()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -258,8 +291,22 @@ def b200_arm(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.item()
 
+    def gather(values: list[float]) -> list[list[float]]:
+        t = torch.tensor(values, dtype=torch.float64, device=dev)
+        if world == 1:
+            return [t.tolist()]
+        out = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        return [o.tolist() for o in out]
+
     lib = capi.load()
-    model_name = args.model
+    strong = args.scaling == "strong"
+    if strong:
+        if world not in STRONG_MODELS:
+            raise SystemExit(f"strong scaling splits 512 lines over 1, 2, 4 or 8 GPUs, not {world}")
+        model_name = STRONG_MODELS[world]
+    else:
+        model_name = args.model
     rec = pipeline.LineRecognizer(model_name, dev)
     LINES = rec.batch
     rng = np.random.default_rng(SEED + rank)
@@ -291,7 +338,8 @@ def b200_arm(args):
         torch.cuda.synchronize(dev)
     barrier()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = max_over_ranks(sum(step_ms))
+    rank_total_ms = sum(step_ms)
+    total_ms = max_over_ranks(rank_total_ms)
     value = world * LINES * args.steps / (total_ms / 1e3)
 
     # ---- end to end: pinned host in, tokens out, every step, through the
@@ -327,8 +375,10 @@ def b200_arm(args):
     x_chk = torch.from_numpy(np.random.default_rng(SEED).uniform(-1, 1, (LINES, H, W, 3))
                              .astype(np.float16)).to(dev)
     rec.enqueue(x_chk)
-    digest = tokens_digest(*rec.results(LINES))
+    chk_ids, chk_len, chk_sc = rec.results(LINES)
+    digest = tokens_digest(chk_ids, chk_len, chk_sc)
     identical = all_equal_over_ranks(digest)
+    distinct = len(np.unique(np.concatenate([chk_ids[k, :chk_len[k]] for k in range(LINES)])))
 
     # ---- the CTC head alone (vocabulary projection + merge + collapse)
     head_ms = _event_steps(stream, 10, lambda i: rec.enqueue_head(LINES), flush)
@@ -348,13 +398,36 @@ def b200_arm(args):
     tf = REPO / "profiles" / "traffic.json"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(op_names[dom] + f"#{dom}")
+    rec.close()
+    del flush
 
-    cpu = None
-    if rank == 0:
-        cpu_value, cpu_lines, cores = cpu_port_forward(8)
-        cpu = {"value": round(cpu_value, 3), "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"{cpu_lines} lines of the batch through the oracle's CPU restatement "
-                         f"(torch fp32, same graph and weights, vocabulary projection, argmax, collapse)"}
+    # ---- BASELINE metric, second half: page p50 latency (config 5) on every
+    # rank, 8 pages + 512 crops per rank (pages sharded across the GPUs)
+    page = None
+    if not args.no_pages:
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        barrier()
+        pg = measure_pages(dev, args.page_runs, max(args.warmup, 3), flush, seed_offset=rank)
+        barrier()
+        page_p50 = max_over_ranks(pg["p50_ms"])
+        page_e2e = max_over_ranks(pg["e2e_p50_ms"])
+        page = {"metric": "page p50 latency ms @960^2 (C5: 8 pages -> detector + binarize, 512 line crops "
+                          "-> recognizer + head + collapse per GPU)",
+                "p50_ms": round(page_p50, 4), "unit": "ms", "higher_is_better": False,
+                "pages_per_s": round(world * 8 / (page_p50 / 1e3), 1),
+                "p90_ms": pg["p90_ms"], "e2e_p50_ms": round(page_e2e, 4), "runs": pg["runs"],
+                "e2e": {"value": round(page_e2e, 4), "unit": "ms", "h2d_bytes_per_step": pg["h2d_bytes_per_run"],
+                        "d2h_bytes_per_step": pg["d2h_bytes_per_run"]},
+                "roofline": pg["roofline"], "binarize": pg["binarize"],
+                "detector_top_ops": pg["detector_top_ops"][:5], "clocks": pg["clocks"],
+                "gpu_launches": pg["launches_per_run"] * pg["runs"], "cpu_baseline": cpu_pages}
+        rank_page = pg["p50_ms"]
+        del flush
+    else:
+        rank_page = float("nan")
+
+    csum = clocks.summary()
+    per_rank = gather([rank_total_ms / args.steps, csum["sm_mhz"] or 0.0, rank_page])
     gpu_launches = launches_per_step * args.steps
     if world > 1:
         dist.barrier()
@@ -362,12 +435,13 @@ def b200_arm(args):
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+            "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "fp16",
             "data": "synthetic (seeded U(-1,1) FP16 NHWC line images, seeded random-init weights)",
             "config": {"workload": f"BASELINE config 4: full recognizer forward, {LINES} lines/GPU of 48x320, "
                                    "HGNet-style backbone 48-128-512-1024-2048 + SVTR neck dim 120 x2 + CTC "
                                    "projection V=18385 with fused argmax + device collapse",
-                       "model": model_name, "lines_per_gpu": LINES, "parallelism": f"replicas x{world} (no collective)",
+                       "model": model_name, "lines_per_gpu": LINES, "lines_total": LINES * world,
+                       "parallelism": f"replicas x{world} (no collective)",
                        "l2": "flushed between timed steps (256 MB write outside the timed events)"},
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
@@ -378,14 +452,19 @@ def b200_arm(args):
                          "traffic": traffic, "launch_ms": round(per_op[dom], 4), "flops": flops},
             "cpu_baseline": cpu,
             "gpu_launches": gpu_launches,
-            "clocks": clocks.summary(),
-            "replica_tokens": {"sha256": digest[:16], "identical_across_ranks": identical},
+            "clocks": csum,
+            "per_rank": [{"rank": k, "ms_per_step": round(v[0], 4), "sm_mhz": v[1],
+                          "page_p50_ms": None if v[2] != v[2] else round(v[2], 4)} for k, v in enumerate(per_rank)],
+            "replica_tokens": {"sha256": digest[:16], "identical_across_ranks": identical,
+                               "mean_length": round(float(np.mean(chk_len)), 2), "distinct_ids": distinct},
             "head_ms": round(head_ms, 4),
             "ops_ms": {f"{op_names[i]}#{i}": round(per_op[i], 4)
                        for i in sorted(range(len(per_op)), key=lambda i: -per_op[i])[:16]},
         }
+        if page is not None:
+            line["page_p50_ms"] = page["p50_ms"]
+            line["page"] = page
         print(json.dumps(line), flush=True)
-    rec.close()
     if world > 1:
         dist.destroy_process_group()
 
@@ -506,6 +585,92 @@ def _roofline_for(kind, ms, bytes_, flops, key, peak_tf, peak_hbm, peak_kind):
     return {"bound": "tensor", "kernel": key, "achieved": round(achieved, 1), "peak": peak_tf, "unit": "TFLOP/s",
             "frac": round(achieved / peak_tf, 4), "peak_source": f"bf16_tflops of {peak_kind} peaks",
             "traffic": traffic, "launch_ms": round(ms, 5), "flops": flops}
+
+
+def measure_pages(dev, runs, warm, flush, with_cpu=False, seed_offset=0):
+    """BASELINE config 5 on this GPU: 8 FP16 NHWC 960^2 pages (detector +
+    binarize) and 512 line crops (recognizer + head + collapse) per run,
+    `runs` timed runs after `warm` warm-up runs; CUDA events on the
+    pipeline's stream, L2 flushed outside the events, clocks sampled.
+    Returns step/e2e times, p50/p90, the detector's dominant-op roofline and
+    per-op figures, and (with_cpu) the CPU port's bounded-sample latency."""
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    from ppocr_b200 import capi, models, pipeline, workloads
+
+    lib = capi.load()
+    peak_tf, peak_hbm, peak_kind = peaks()
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    r = workloads.rng(SEED + seed_offset)
+    pp = pipeline.PagePipeline(device=dev)
+    pages_np, crops_np = workloads.c5_pages(r)
+    pages_h = torch.from_numpy(pages_np).pin_memory()
+    crops_h = torch.from_numpy(crops_np).pin_memory()
+    pages, crops = pages_h.to(dev), crops_h.to(dev)
+    stream = pp.stream
+    for _ in range(warm):
+        pp.enqueue(pages, crops)
+    stream.synchronize()
+    assert lib.ppocr_b200_device_error() == 0
+    with ClockSampler(dev.index or 0) as clocks:
+        step_ms = _event_steps(stream, runs, lambda i: pp.enqueue(pages, crops), flush)
+    bm_h = torch.empty_like(pp.bitmap, device="cpu").pin_memory()
+    ids_h = torch.empty_like(pp.rec.out_ids, device="cpu").pin_memory()
+    len_h = torch.empty_like(pp.rec.out_len, device="cpu").pin_memory()
+    sc_h = torch.empty_like(pp.rec.out_score, device="cpu").pin_memory()
+    st_p, st_c = torch.empty_like(pages), torch.empty_like(crops)
+
+    def e2e_body(i):
+        with torch.cuda.stream(stream):
+            st_p.copy_(pages_h, non_blocking=True)
+            st_c.copy_(crops_h, non_blocking=True)
+        pp.enqueue(st_p, st_c)
+        with torch.cuda.stream(stream):
+            bm_h.copy_(pp.bitmap, non_blocking=True)
+            ids_h.copy_(pp.rec.out_ids, non_blocking=True)
+            len_h.copy_(pp.rec.out_len, non_blocking=True)
+            sc_h.copy_(pp.rec.out_score, non_blocking=True)
+
+    e2e_ms = _event_steps(stream, runs, e2e_body, None)
+    out = {"step_ms": step_ms, "e2e_ms": e2e_ms}
+    out["h2d_bytes_per_run"] = (pages_h.numel() + crops_h.numel()) * 2
+    out["d2h_bytes_per_run"] = bm_h.numel() + ids_h.numel() * 4 + len_h.numel() * 4 + sc_h.numel() * 4
+    dom, dname, dms, dbytes, dflops, per, names = _dominant(pp.det, "det_b8")
+    out["roofline"] = _roofline_for("tensor", dms, dbytes, dflops, f"c5:det:{dname}#{dom}", peak_tf, peak_hbm,
+                                    peak_kind)
+    gdet, _ = models.graph("det_b8")
+    top = sorted(range(len(per)), key=lambda i: -per[i])[:10]
+    out["detector_top_ops"] = []
+    for i in top:
+        f = op_flops(gdet, i)
+        b = op_bytes(gdet, i)
+        out["detector_top_ops"].append({
+            "op": f"{names[i]}#{i}", "ms": round(per[i], 5),
+            "tflops": round(f / (per[i] / 1e3) / 1e12, 1) if f and per[i] > 0 else None,
+            "gbs": round(b / (per[i] / 1e3) / 1e9, 1) if per[i] > 0 else None})
+    # binarize alone: 5 B/pixel (f32 read + u8 write)
+    n = pp.prob.numel()
+    s = ctypes.c_void_p(stream.cuda_stream)
+    bin_ms = _event_steps(stream, 20, lambda i: capi.check(lib.ppocr_b200_binarize(
+        P(pp.prob), P(pp.bitmap), n, pp.thresh, s)), flush)
+    out["binarize"] = _roofline_for("hbm", statistics.mean(bin_ms), 5.0 * n, None, "c5:binarize",
+                                    peak_tf, peak_hbm, peak_kind)
+    out["detector_eager_ms"] = round(sum(_per_op(pp.det)), 4)
+    out["p50_ms"] = round(float(np.percentile(step_ms, 50)), 4)
+    out["p90_ms"] = round(float(np.percentile(step_ms, 90)), 4)
+    out["e2e_p50_ms"] = round(float(np.percentile(e2e_ms, 50)), 4)
+    out["runs"] = runs
+    # detector ops after the staged transpose, binarize, recognizer ops
+    # after its staged transpose, vocabulary projection (2), collapse (1)
+    out["launches_per_run"] = (len(names) - 1) + 1 + (len(pp.rec.model.lib.op_names(pp.rec.model.handle)) - 1) + 3
+    out["clocks_obj"] = clocks
+    out["clocks"] = clocks.summary()
+    out["cpu_baseline"] = _cpu_c5() if with_cpu else None
+    pp.close()
+    return out
 
 
 def config_arm(args):
@@ -801,67 +966,12 @@ def config_arm(args):
                     "text-line blobs per page over speckle) -> binarize 0.3 -> 8-connected components labelled "
                     "in OpenCV's order with (left, top, width, height, area) and fixed-point probability sums")
     else:  # c5
-        pp = pipeline.PagePipeline(device=dev)
-        pages_np, crops_np = workloads.c5_pages(r)
-        pages_h = torch.from_numpy(pages_np).pin_memory()
-        crops_h = torch.from_numpy(crops_np).pin_memory()
-        pages, crops = pages_h.to(dev), crops_h.to(dev)
-        stream = pp.stream
-        for _ in range(warm):
-            pp.enqueue(pages, crops)
-        stream.synchronize()
-        assert lib.ppocr_b200_device_error() == 0
-        runs = args.steps
-        with ClockSampler(local) as clocks:
-            step_ms = _event_steps(stream, runs, lambda i: pp.enqueue(pages, crops), flush)
-        bm_h = torch.empty_like(pp.bitmap, device="cpu").pin_memory()
-        ids_h = torch.empty_like(pp.rec.out_ids, device="cpu").pin_memory()
-        len_h = torch.empty_like(pp.rec.out_len, device="cpu").pin_memory()
-        sc_h = torch.empty_like(pp.rec.out_score, device="cpu").pin_memory()
-        st_p, st_c = torch.empty_like(pages), torch.empty_like(crops)
-
-        def e2e_body(i):
-            with torch.cuda.stream(stream):
-                st_p.copy_(pages_h, non_blocking=True)
-                st_c.copy_(crops_h, non_blocking=True)
-            pp.enqueue(st_p, st_c)
-            with torch.cuda.stream(stream):
-                bm_h.copy_(pp.bitmap, non_blocking=True)
-                ids_h.copy_(pp.rec.out_ids, non_blocking=True)
-                len_h.copy_(pp.rec.out_len, non_blocking=True)
-                sc_h.copy_(pp.rec.out_score, non_blocking=True)
-
-        e2e_ms = _event_steps(stream, runs, e2e_body, None)
-        h2d = (pages_h.numel() + crops_h.numel()) * 2
-        d2h = bm_h.numel() + ids_h.numel() * 4 + len_h.numel() * 4 + sc_h.numel() * 4
-        dom, dname, dms, dbytes, dflops, per, names = _dominant(pp.det, "det_b8")
-        roof = _roofline_for("tensor", dms, dbytes, dflops, f"c5:det:{dname}#{dom}", peak_tf, peak_hbm, peak_kind)
-        gdet, _ = models.graph("det_b8")
-        top = sorted(range(len(per)), key=lambda i: -per[i])[:10]
-        extra["detector_top_ops"] = []
-        for i in top:
-            f = op_flops(gdet, i)
-            b = op_bytes(gdet, i)
-            extra["detector_top_ops"].append({
-                "op": f"{names[i]}#{i}", "ms": round(per[i], 5),
-                "tflops": round(f / (per[i] / 1e3) / 1e12, 1) if f and per[i] > 0 else None,
-                "gbs": round(b / (per[i] / 1e3) / 1e9, 1) if per[i] > 0 else None})
-        # binarize alone: 5 B/pixel (f32 read + u8 write)
-        n = pp.prob.numel()
-        s = ctypes.c_void_p(stream.cuda_stream)
-        bin_ms = _event_steps(stream, 20, lambda i: capi.check(lib.ppocr_b200_binarize(
-            P(pp.prob), P(pp.bitmap), n, pp.thresh, s)), flush)
-        extra["binarize"] = _roofline_for("hbm", statistics.mean(bin_ms), 5.0 * n, None, "c5:binarize",
-                                          peak_tf, peak_hbm, peak_kind)
-        det_ms = sum(_per_op(pp.det))
-        extra["detector_eager_ms"] = round(det_ms, 4)
-        extra["p90_ms"] = round(float(np.percentile(step_ms, 90)), 4)
-        extra["runs"] = runs
-        # detector ops after the staged transpose, binarize, recognizer ops
-        # after its staged transpose, vocabulary projection (2), collapse (1)
-        launches = (len(names) - 1) + 1 + (len(pp.rec.model.lib.op_names(pp.rec.model.handle)) - 1) + 3
-        cpu = _cpu_c5()
-        pp.close()
+        pg = measure_pages(dev, args.steps, warm, flush, with_cpu=True)
+        step_ms, e2e_ms = pg.pop("step_ms"), pg.pop("e2e_ms")
+        roof, cpu, launches = pg.pop("roofline"), pg.pop("cpu_baseline"), pg.pop("launches_per_run")
+        h2d, d2h = pg.pop("h2d_bytes_per_run"), pg.pop("d2h_bytes_per_run")
+        clocks = pg.pop("clocks_obj")
+        extra.update(pg)
         units = None
         workload = ("BASELINE config 5: 8 FP16 NHWC pages 960x960 -> DB detector (backbone strides 2..32, FPN "
                     "256, head 3x3 -> deconv x2 -> sigmoid) -> binarize 0.3, plus 64 synthetic 48x320 crops per "

@@ -16,15 +16,25 @@ extern "C" {
 #endif
 
 const char *ppocr_b200_last_error(void);
-// Reads and clears the device error word that kernels set when one of their
-// bounded waits ran out (0 = no error). Synchronizes the device.
+// Reads and clears the current device's error words that kernels set when
+// one of their bounded waits ran out (0 = no error; the outputs of the work
+// enqueued since the last call are then invalid). Covers every kernel of the
+// library, the allocation-free head's own word included. Synchronizes the
+// device; a serving loop calls it after its stream sync and fails the batch
+// on a nonzero code.
 int ppocr_b200_device_error(void);
+// Test support, no counterpart in the reference: stores `code` in one of the
+// current device's error words, as a kernel whose bounded wait ran out would
+// (which = 0: the library-wide word; 1: the allocation-free head's word), so
+// tests can check how ppocr_b200_device_error() and the model shells report
+// it. The library-wide word is allocated on first use; nothing else is.
+int ppocr_b200_test_store_error_code(int which, int code);
 
 // Replaces tiled_classifier_workspace_shape
-// (native/include/ppocrv6_native/kernels/classifier.h:16-17): partial-buffer
-// size for ppocr_b200_linear_argmax_prob. The B200 kernel reduces vocabulary
-// tiles of 256 columns whatever vocab_tile_size asks for, so num_vocab_blocks
-// is ceil(vocab/256) and partial_count = round_up(rows,16) * num_vocab_blocks.
+// (native/include/ppocrv6_native/kernels/classifier.h:16-17,
+// classifier.cu:520-536), with the same results: num_row_blocks =
+// ceil(rows/row_block_size), num_vocab_blocks = ceil(vocab/vocab_tile_size),
+// partial_count = num_row_blocks * num_vocab_blocks * row_block_size.
 int ppocr_b200_classifier_workspace(int rows, int vocab_size,
                                     int row_block_size, int vocab_tile_size,
                                     int *num_row_blocks, int *num_vocab_blocks,
@@ -35,8 +45,15 @@ int ppocr_b200_classifier_workspace(int rows, int vocab_size,
 // [hidden_size][vocab_size] (row-major, as the reference loads it), bias FP16
 // [vocab_size]. Outputs per row: argmax id (ties -> lowest id), 1/sum
 // exp(l - max) (1.0 when calculate_probability is 0) and the max logit.
-// The weight is transposed per call into a library-owned buffer; callers
-// that keep the weight resident use ppocr_b200_classifier_pack/_run instead.
+// partial_* are sized as the reference sizes them for this vocab_tile_size
+// (ppocr_b200_classifier_workspace with row_block_size 16). The B200 kernel
+// reduces 256-column vocabulary tiles whatever vocab_tile_size says; when the
+// caller's partial buffers are too small for that, it uses a workspace of the
+// calling stream instead. The weight is transposed per call into that
+// per-(device, stream) workspace (allocated stream-ordered on first use and
+// grown the same way; callers on different streams never share it), so each
+// call depends only on its own arguments. Callers that keep the weight
+// resident use ppocr_b200_classifier_pack/_run_packed instead.
 int ppocr_b200_linear_argmax_prob(
     const void *hidden, const void *weight, const void *bias, int *out_indices,
     float *out_prob, float *out_max_logits, int rows, int hidden_size,
@@ -68,11 +85,15 @@ int ppocr_b200_classifier_run_packed(
 // a message. All calls on a device share the array, so calls whose kernels
 // may overlap on the GPU race; order them on one stream. The first call on
 // each device performs a one-time set-up (array lookup and a synchronous
-// clear), so make it before any stream capture on that device.
+// clear), so make it before any stream capture on that device; a failed
+// set-up is retried by the next call. A projection whose bounded wait ran out
+// writes its code into the array's own error word, which
+// ppocr_b200_device_error() reads and clears like the library's other word.
 int ppocr_b200_classifier_run_packed_noalloc(
     const void *hidden, const void *packed, const void *bias, int *out_indices,
     float *out_prob, float *out_max_logits, int rows, int hidden_size,
     int vocab_size, int calculate_probability, cudaStream_t stream);
+
 
 // Replaces cuda_selected_class_vs_max_probability (classifier.h:45-49,
 // classifier.cu:111-143): p(class) / (p(class) + p(max)) per row.

@@ -6,8 +6,10 @@
 #include "../../include/ppocr_b200_preprocess.h"
 #include "kernels.h"
 #include <algorithm>
+#include <map>
 #include <mutex>
 #include <string>
+#include <utility>
 
 using namespace pb2;
 
@@ -26,30 +28,41 @@ int status(cudaError_t e, const char *what) {
 const half *H(const void *p) { return static_cast<const half *>(p); }
 half *Hm(void *p) { return static_cast<half *>(p); }
 
-// Library-owned grow-only buffer per device for the transposed classifier
-// weight used by the reference-signature entry point.
-struct PackCache {
-  std::mutex m;
-  void *ptr[64] = {};
-  size_t bytes[64] = {};
-} g_pack;
+// Workspace of the reference-signature head, one per (device, stream): the
+// per-call transposed weight and, when the caller's partial buffers are sized
+// for the reference's vocabulary tiles (fewer than the 256-column tiles this
+// kernel reduces), the partials. Work on one stream is ordered, so a stream's
+// buffer is reused without synchronisation; growing it frees the old buffer
+// in stream order (cudaFreeAsync), after the work already queued on that
+// stream. Callers on different streams never share a buffer, and nothing
+// persists between calls but the allocation: each call repacks the weight
+// it is given, so results depend only on that call's arguments.
+struct StreamWorkspace {
+  void *ptr = nullptr;
+  size_t bytes = 0;
+};
+std::mutex g_ws_mutex;
+std::map<std::pair<int, cudaStream_t>, StreamWorkspace> g_ws;
 
-half *pack_buffer(size_t bytes) {
+void *stream_workspace(size_t bytes, cudaStream_t stream) {
   int d = 0;
-  cudaGetDevice(&d);
-  d &= 63;
-  std::lock_guard<std::mutex> lock(g_pack.m);
-  if (g_pack.bytes[d] < bytes) {
-    if (g_pack.ptr[d])
-      cudaFree(g_pack.ptr[d]);
-    g_pack.ptr[d] = nullptr;
-    g_pack.bytes[d] = 0;
-    if (cudaMalloc(&g_pack.ptr[d], bytes) != cudaSuccess)
+  if (cudaGetDevice(&d) != cudaSuccess)
+    return nullptr;
+  std::lock_guard<std::mutex> lock(g_ws_mutex);
+  StreamWorkspace &w = g_ws[{d, stream}];
+  if (w.bytes < bytes) {
+    if (w.ptr)
+      cudaFreeAsync(w.ptr, stream);
+    w.ptr = nullptr;
+    w.bytes = 0;
+    if (cudaMallocAsync(&w.ptr, bytes, stream) != cudaSuccess)
       return nullptr;
-    g_pack.bytes[d] = bytes;
+    w.bytes = bytes;
   }
-  return static_cast<half *>(g_pack.ptr[d]);
+  return w.ptr;
 }
+
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 } // namespace
 
 void pb2::set_last_error(const std::string &message) { g_error = message; }
@@ -60,7 +73,25 @@ const char *ppocr_b200_last_error(void) { return g_error.c_str(); }
 
 int ppocr_b200_device_error(void) {
   cudaDeviceSynchronize();
-  return take_device_error();
+  // Both words are read (and so cleared); the library-wide one is reported
+  // first when both hold a code.
+  const int shared = take_device_error();
+  const int noalloc = take_noalloc_error();
+  return shared ? shared : noalloc;
+}
+
+int ppocr_b200_test_store_error_code(int which, int code) {
+  g_error.clear();
+  if (which == 0) {
+    int *word = device_error_word();
+    if (!word)
+      return fail("cannot allocate the device error word");
+    return status(cudaMemcpy(word, &code, sizeof(int), cudaMemcpyHostToDevice),
+                  "store error code");
+  }
+  if (which == 1)
+    return status(store_noalloc_error(code), "store allocation-free error code");
+  return fail("which must be 0 (library word) or 1 (allocation-free head word)");
 }
 
 int ppocr_b200_classifier_workspace(int rows, int vocab, int row_block,
@@ -77,10 +108,13 @@ int ppocr_b200_classifier_workspace(int rows, int vocab, int row_block,
   }
   if (row_block <= 0 || row_block > 16 || vocab_tile <= 0)
     return fail("invalid tiled classifier workspace shape");
-  *num_row_blocks = (rows + 15) / 16;
-  *num_vocab_blocks = vocab_tiles(vocab);
-  *partial_count = static_cast<size_t>(*num_row_blocks) * 16 *
-                   static_cast<size_t>(*num_vocab_blocks);
+  // The reference's shape, unchanged (classifier.cu:520-536), so buffers
+  // sized by either library fit ppocr_b200_linear_argmax_prob.
+  *num_row_blocks = (rows + row_block - 1) / row_block;
+  *num_vocab_blocks = (vocab + vocab_tile - 1) / vocab_tile;
+  *partial_count = static_cast<size_t>(*num_row_blocks) *
+                   static_cast<size_t>(*num_vocab_blocks) *
+                   static_cast<size_t>(row_block);
   return 0;
 }
 
@@ -129,9 +163,24 @@ int ppocr_b200_linear_argmax_prob(
       vocab_tile <= 0 || vocab_tile % 16 != 0 || !part_id || !part_max ||
       !part_sum || !hidden || !weight || !bias)
     return fail("invalid WMMA classifier launch arguments");
-  half *packed = pack_buffer(static_cast<size_t>(hidden_size) * vocab * 2);
-  if (!packed)
-    return fail("cannot allocate classifier pack buffer");
+  // The caller sized the partials for the reference's WMMA path: 16-row
+  // blocks x ceil(vocab / vocab_tile) tiles (classifier.cu:624-625). This
+  // kernel needs rows x ceil(vocab / 256); when that does not fit, the
+  // partials go to the stream's workspace instead.
+  const size_t need = static_cast<size_t>(rows) * vocab_tiles(vocab);
+  const size_t have = round_up(static_cast<size_t>(rows), 16) *
+                      ((static_cast<size_t>(vocab) + vocab_tile - 1) / vocab_tile);
+  const size_t pack_bytes = round_up(static_cast<size_t>(hidden_size) * vocab * 2, 256);
+  const size_t part_bytes = have >= need ? 0 : round_up(need * 4, 256);
+  auto *ws = static_cast<unsigned char *>(stream_workspace(pack_bytes + 3 * part_bytes, stream));
+  if (!ws)
+    return fail("cannot allocate the classifier workspace");
+  half *packed = reinterpret_cast<half *>(ws);
+  if (part_bytes) {
+    part_max = reinterpret_cast<float *>(ws + pack_bytes);
+    part_id = reinterpret_cast<int *>(ws + pack_bytes + part_bytes);
+    part_sum = reinterpret_cast<float *>(ws + pack_bytes + 2 * part_bytes);
+  }
   cudaError_t e = pack_vocab_weight(H(weight), packed, hidden_size, vocab, stream);
   if (e != cudaSuccess)
     return status(e, "classifier pack");

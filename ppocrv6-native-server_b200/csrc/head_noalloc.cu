@@ -14,12 +14,16 @@
 // the last call, so calls whose kernels overlap on the GPU (different
 // streams, no ordering between them) race on it. Every partial the merge
 // reads is written earlier in the same call, so nothing needs clearing
-// between calls; the wait-timeout word at the start of the array is zeroed
-// once at set-up.
+// between calls. The first word of the array is this path's wait-timeout
+// word: the projection kernel writes a nonzero code there when one of its
+// bounded waits runs out (its outputs are then invalid). It is zeroed at
+// set-up, and ppocr_b200_device_error() reads and clears it together with
+// the library's other error word.
 //
 // Set-up happens inside the first call on each device (address lookup of
 // the array plus a synchronous clear of its first 256 bytes), so make that
-// first call before any stream capture on the device.
+// first call before any stream capture on the device. A set-up that failed
+// is retried by the next call.
 #include "../../include/ppocr_b200_head.h"
 #include "kernels.h"
 #include <mutex>
@@ -35,15 +39,13 @@ constexpr size_t kScratchBytes = kHeaderBytes + 3 * kArrayBytes;
 
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
-struct DeviceScratch {
-  std::once_flag once;
-  cudaError_t status = cudaErrorNotReady;
-  unsigned char *base = nullptr;
-};
-DeviceScratch g_devices[64];
+constexpr int kMaxDevices = 64;
+std::mutex g_setup;
+unsigned char *g_base[kMaxDevices] = {}; // set once a device's set-up succeeded
 
 // In host code `g_scratch` names a host-side shadow, not device memory: the
-// device address is looked up once per device, with that device current.
+// device address is looked up per device, with that device current. A
+// failed look-up or clear leaves the entry empty, so the next call retries.
 unsigned char *device_scratch(cudaError_t *status) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -51,21 +53,68 @@ unsigned char *device_scratch(cudaError_t *status) {
     *status = e;
     return nullptr;
   }
-  DeviceScratch &d = g_devices[dev & 63];
-  std::call_once(d.once, [&] {
+  if (dev < 0 || dev >= kMaxDevices) {
+    *status = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_setup);
+  if (!g_base[dev]) {
     void *p = nullptr;
-    d.status = cudaGetSymbolAddress(&p, g_scratch);
-    if (d.status == cudaSuccess) {
-      d.base = static_cast<unsigned char *>(p);
-      // Clear the timeout word (the partials need no clearing).
-      d.status = cudaMemset(d.base, 0, kHeaderBytes);
+    e = cudaGetSymbolAddress(&p, g_scratch);
+    // Clear the timeout word (the partials need no clearing).
+    if (e == cudaSuccess)
+      e = cudaMemset(p, 0, kHeaderBytes);
+    if (e != cudaSuccess) {
+      *status = e;
+      return nullptr;
     }
-  });
-  *status = d.status;
-  return d.status == cudaSuccess ? d.base : nullptr;
+    g_base[dev] = static_cast<unsigned char *>(p);
+  }
+  *status = cudaSuccess;
+  return g_base[dev];
+}
+
+// The current device's timeout word, or null when this path has not been
+// set up on it (then no kernel of this path can have written it).
+int *set_up_error_word() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return nullptr;
+  std::lock_guard<std::mutex> lock(g_setup);
+  return reinterpret_cast<int *>(g_base[dev]);
 }
 
 } // namespace
+
+namespace pb2 {
+// Reads and clears the allocation-free path's timeout word on the current
+// device (0 when clear or never set up; -1 when the read failed). Used by
+// ppocr_b200_device_error().
+int take_noalloc_error() {
+  int *word = set_up_error_word();
+  if (!word)
+    return 0;
+  int v = 0;
+  if (cudaMemcpy(&v, word, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return -1;
+  if (v && cudaMemset(word, 0, sizeof(int)) != cudaSuccess)
+    return -1;
+  return v;
+}
+} // namespace pb2
+
+namespace pb2 {
+// Test support for ppocr_b200_test_store_error_code: writes `code` into the
+// current device's timeout word of this path, as a kernel whose wait ran out
+// would. Sets the path up on the device if needed; allocates nothing.
+cudaError_t store_noalloc_error(int code) {
+  cudaError_t status;
+  unsigned char *base = device_scratch(&status);
+  if (!base)
+    return status;
+  return cudaMemcpy(base, &code, sizeof(int), cudaMemcpyHostToDevice);
+}
+} // namespace pb2
 
 extern "C" int ppocr_b200_classifier_run_packed_noalloc(
     const void *hidden, const void *packed, const void *bias, int *ids,

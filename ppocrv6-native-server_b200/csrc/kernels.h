@@ -15,6 +15,10 @@ namespace pb2 {
 int *device_error_word();
 // Reads and clears the error word of the current device (synchronizes).
 int take_device_error();
+// Reads and clears the allocation-free head's timeout word (head_noalloc.cu).
+int take_noalloc_error();
+// Test support: writes `code` into that word (head_noalloc.cu).
+cudaError_t store_noalloc_error(int code);
 int sm_count();
 // Sets the calling thread's message returned by ppocr_b200_last_error().
 void set_last_error(const std::string &message);

@@ -7,6 +7,14 @@
 // join with the caller stream, input staging with a zero tail, eager first
 // run then CUDA-graph capture and replay (67-96), error strings and the
 // stream sync on a failed enqueue (150-176).
+//
+// Bounded waits: a kernel whose wait ran out sets the library's per-device
+// error word and its outputs are invalid. The first (eager) run checks the
+// word synchronously; every later enqueue copies the word into pinned host
+// memory behind its graph launch, and the next enqueue of the handle fails
+// with the code if that copy (already complete) saw one. Serving loops that
+// must not wait for the next batch call ppocr_b200_device_error() after their
+// stream sync.
 #include "../../include/ppocr_b200_model_abi.h"
 #include "kernels.h"
 #include "runtime.h"
@@ -33,10 +41,14 @@ struct Instance {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   bool warmed = false;
+  int *error_seen = nullptr; // pinned: the error word after the last replay
+  bool error_pending = false;
 
   ~Instance() {
     if (r.stream)
       cudaStreamSynchronize(r.stream);
+    if (error_seen)
+      cudaFreeHost(error_seen);
     if (exec)
       cudaGraphExecDestroy(exec);
     if (graph)
@@ -66,6 +78,8 @@ struct Instance {
     // The per-device error word is allocated here, outside any capture.
     if (!pb2::device_error_word())
       throw std::runtime_error("Cannot allocate device error word");
+    CU(cudaMallocHost(&error_seen, sizeof(int)));
+    *error_seen = 0;
     CU(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
     CU(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
   }
@@ -79,6 +93,19 @@ struct Instance {
   // eagerly, captures it and then stages the input again: when staging
   // writes a tensor the arena reuses later in the graph (the channels-last
   // input of the fast path), the warm-up run has overwritten it.
+  // Fails when the previous replay, now complete, saw a timed-out wait.
+  void check_previous() {
+    if (!error_pending || cudaEventQuery(done) != cudaSuccess)
+      return;
+    error_pending = false;
+    if (const int code = *error_seen) {
+      *error_seen = 0;
+      pb2::take_device_error(); // clear the word for the next batch
+      throw std::runtime_error("kernel wait timed out in the previous batch (code " +
+                               std::to_string(code) + "); its output is invalid");
+    }
+  }
+
   template <class Stage>
   void execute(const Stage &stage, void *output, int batch,
                cudaStream_t caller) {
@@ -104,6 +131,9 @@ struct Instance {
     else
       CU(cudaMemcpyAsync(output, r.t[OUTPUT_ID], output_n * 2,
                          cudaMemcpyDeviceToDevice, r.stream));
+    CU(cudaMemcpyAsync(error_seen, pb2::device_error_word(), sizeof(int),
+                       cudaMemcpyDeviceToHost, r.stream));
+    error_pending = true;
     CU(cudaGetLastError());
     CU(cudaEventRecord(done, r.stream));
     CU(cudaStreamWaitEvent(caller, done));
@@ -112,6 +142,7 @@ struct Instance {
   void enqueue_f32(const float *input, void *output, int batch,
                    cudaStream_t caller) {
     check_batch(input, output, batch);
+    check_previous();
     CU(cudaEventRecord(ready, caller));
     CU(cudaStreamWaitEvent(r.stream, ready));
     auto stage = [&] {
@@ -132,6 +163,7 @@ struct Instance {
   void enqueue_nhwc(const void *input, void *output, int batch,
                     cudaStream_t caller) {
     check_batch(input, output, batch);
+    check_previous();
     CU(cudaEventRecord(ready, caller));
     CU(cudaStreamWaitEvent(r.stream, ready));
     auto stage = [&] {

@@ -32,11 +32,13 @@ PI, PF = POINTER(c_int), POINTER(c_float)
 SIGNATURES = {
     "ppocr_b200_last_error": (c_char_p, []),
     "ppocr_b200_device_error": (I, []),
+    "ppocr_b200_test_store_error_code": (I, [I, I]),
     "ppocr_b200_classifier_workspace": (I, [I, I, I, I, PI, PI, POINTER(c_size_t)]),
     "ppocr_b200_linear_argmax_prob": (I, [V, V, V, V, V, V, I, I, I, I, V, V, V, I, V]),
     "ppocr_b200_classifier_pack": (I, [V, V, I, I, V]),
     "ppocr_b200_classifier_run_packed": (I, [V, V, V, V, V, V, I, I, I, V, V, V, I, V]),
     "ppocr_b200_classifier_run_packed_noalloc": (I, [V, V, V, V, V, V, I, I, I, I, V]),
+
     "ppocr_b200_selected_class_vs_max_probability": (I, [V, V, V, V, V, I, I, I, I, V]),
     "ppocr_b200_logits_argmax_prob": (I, [V, I, I, V, V, V, I, V]),
     "ppocr_b200_ctc_collapse": (I, [V, V, I, I, I, V, V, V, V]),

@@ -66,9 +66,7 @@ class Classifier:
     """CTC head weights resident on the device in the packed layout."""
 
     def __init__(self, hidden: int, vocab: int, device: torch.device, seed: int = models.SEED):
-        init = modelgen.Init(seed + 1)
-        w = init.xavier((hidden, vocab), hidden, vocab)
-        b = init.normal((vocab,), 0.0, 0.01)
+        w, b = models.head_weights(hidden, vocab, seed)
         self.hidden, self.vocab = hidden, vocab
         self.weight_host = w
         self.bias_host = b

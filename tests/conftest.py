@@ -55,6 +55,21 @@ def cuda():
     return torch.device("cuda:0")
 
 
+@pytest.fixture(scope="session")
+def parity_report():
+    """Measured parity figures (max-abs, relative L2) collected by the tests;
+    written as JSON to $PPOCR_PARITY_REPORT at the end of the session when
+    that variable is set."""
+    import json
+
+    report = {}
+    yield report
+    path = os.environ.get("PPOCR_PARITY_REPORT")
+    if path and report:
+        Path(path).parent.mkdir(parents=True, exist_ok=True)
+        Path(path).write_text(json.dumps(report, indent=1, sort_keys=True) + "\n")
+
+
 def ptr(t):
     return ctypes.c_void_p(t.data_ptr())
 

@@ -42,3 +42,57 @@ def assert_close(got, want, max_abs=2e-2, rel=1e-3, what=""):
     assert ma <= max_abs and r <= rel, (
         f"{what}: max_abs={ma:.4g} (at {where}: got {got[where].item() if diff.numel() else 0:.5g} "
         f"want {want[where].item() if diff.numel() else 0:.5g}) rel_l2={r:.3g}")
+
+
+def check_decode(rec, n, oracle_c, oracle_hidden=None, margin=0.25):
+    """Decoded-text parity of a LineRecognizer after rec.enqueue() of n lines.
+
+    1. The fused vocabulary projection + argmax on the device's own hidden
+       states against float64 logits from the same FP16 hidden and head
+       weights: ids exact on every frame whose top-2 gap exceeds 1e-3 (at
+       least 90 % of frames must be that clear), max-prob within 1e-5.
+    2. The device collapse against the oracle's C collapse of the device's
+       frame ids and probabilities (ctc_decode.cpp:7-51 semantics): ids,
+       lengths and scores bit-exact; mean decoded length at least 8.
+    3. With oracle_hidden (the CPU oracle's hidden states of the same
+       lines): frames whose oracle top-2 gap exceeds `margin` (far above the
+       logit error the FP16 hidden-state difference can cause) decode to the
+       same id, and at least half of all frames are that clear.
+    Returns (ids, lens, scores) of the device."""
+    import ctypes
+
+    ids, lens, scores = rec.results(n)
+    T, H = rec.T, rec.H
+    w = torch.from_numpy(rec.head.weight_host).half().double()
+    b = torch.from_numpy(rec.head.bias_host).half().double()
+    hidden = rec.hidden[:n].float().cpu().reshape(-1, H).double()
+    logits = hidden @ w + b
+    top2 = torch.topk(logits, 2, 1).values
+    clear = ((top2[:, 0] - top2[:, 1]) > 1e-3).numpy()
+    assert clear.mean() >= 0.9, f"only {clear.mean():.3f} of frames have a top-2 gap > 1e-3"
+    want_ids = logits.argmax(1).numpy().astype(np.int32)
+    want_prob = (1.0 / torch.exp(logits - top2[:, :1]).sum(1)).numpy()
+    frame_ids = rec.ids[: n * T].cpu().numpy()
+    frame_prob = rec.prob[: n * T].cpu().numpy()
+    assert np.array_equal(frame_ids[clear], want_ids[clear])
+    assert np.abs(frame_prob - want_prob).max() <= 1e-5
+    o_ids = np.empty((n, T), np.int32)
+    o_len = np.empty(n, np.int32)
+    o_sc = np.empty(n, np.float32)
+    fi = np.ascontiguousarray(frame_ids, np.int32)
+    fp = np.ascontiguousarray(frame_prob, np.float32)
+    oracle_c.oracle_ctc_collapse(fi.ctypes.data, fp.ctypes.data, n, T, rec.blank, o_ids.ctypes.data,
+                                 o_len.ctypes.data, o_sc.ctypes.data)
+    assert np.array_equal(lens, o_len)
+    for k in range(n):
+        assert np.array_equal(ids[k, : lens[k]], o_ids[k, : o_len[k]])
+    assert np.array_equal(scores, o_sc)
+    assert lens.mean() >= 8, f"degenerate decode: mean length {lens.mean()}"
+    if oracle_hidden is not None:
+        lo = oracle_hidden.reshape(-1, H).double() @ w + b
+        t2 = torch.topk(lo, 2, 1).values
+        sure = ((t2[:, 0] - t2[:, 1]) > margin).numpy()
+        assert sure.mean() >= 0.5, f"only {sure.mean():.2f} of frames clear the {margin} margin"
+        assert np.array_equal(frame_ids[sure], lo.argmax(1).numpy().astype(np.int32)[sure])
+    del ctypes
+    return ids, lens, scores

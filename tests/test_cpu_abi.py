@@ -109,4 +109,8 @@ def test_op_entry_points_reject_bad_arguments():
     nrb, nvb, cnt = ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
     assert lib.ppocr_b200_classifier_workspace(1280, 18385, 16, 512, ctypes.byref(nrb), ctypes.byref(nvb),
                                                ctypes.byref(cnt)) == 0
-    assert (nrb.value, nvb.value, cnt.value) == (80, 72, 80 * 16 * 72)
+    # The reference's shape (classifier.cu:520-536), not the B200 kernel's.
+    assert (nrb.value, nvb.value, cnt.value) == (80, 36, 80 * 16 * 36)
+    assert lib.ppocr_b200_classifier_workspace(1281, 18385, 8, 128, ctypes.byref(nrb), ctypes.byref(nvb),
+                                               ctypes.byref(cnt)) == 0
+    assert (nrb.value, nvb.value, cnt.value) == (161, 144, 161 * 144 * 8)

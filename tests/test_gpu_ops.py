@@ -548,22 +548,26 @@ def _check_classifier(hid, w, b, ids, prob, mx):
     assert (mx.cpu().double() - logits.max(1).values).abs().max().item() <= 1e-3
 
 
-@pytest.mark.parametrize("rows,H,V", [(300, 128, 5000), (1280, 128, 18385)])
-def test_classifier_reference_signature(native, cuda, rows, H, V):
-    """Reference-signature entry (weight [H][V] as the worker holds it)."""
+@pytest.mark.parametrize("rows,H,V,tile", [(300, 128, 5000, 512), (1280, 128, 18385, 512),
+                                           (1280, 128, 18385, 128), (77, 64, 2200, 64)])
+def test_classifier_reference_signature(native, cuda, rows, H, V, tile):
+    """Reference-signature entry (weight [H][V] as the worker holds it), with
+    partial buffers sized by the reference's workspace shape: smaller than the
+    B200 kernel's 256-column tiles need at tile 512 (the stream workspace is
+    used), large enough at tiles 128 and 64 (the caller's buffers are)."""
     hid, w, b = _classifier_case(rows, H, V)
     dh, dw, db = dev(hid), dev(w), dev(b)
     ids = torch.empty(rows, dtype=torch.int32, device=cuda)
     prob = torch.empty(rows, dtype=torch.float32, device=cuda)
     mx = torch.empty(rows, dtype=torch.float32, device=cuda)
     nrb, nvb, cnt = ctypes.c_int(), ctypes.c_int(), ctypes.c_size_t()
-    assert native.ppocr_b200_classifier_workspace(rows, V, 16, 512, ctypes.byref(nrb), ctypes.byref(nvb),
+    assert native.ppocr_b200_classifier_workspace(rows, V, 16, tile, ctypes.byref(nrb), ctypes.byref(nvb),
                                                   ctypes.byref(cnt)) == 0
     pid = torch.empty(cnt.value, dtype=torch.int32, device=cuda)
     pmax = torch.empty(cnt.value, dtype=torch.float32, device=cuda)
     psum = torch.empty(cnt.value, dtype=torch.float32, device=cuda)
     rc = native.ppocr_b200_linear_argmax_prob(ptr(dh), ptr(dw), ptr(db), ptr(ids), ptr(prob), ptr(mx), rows, H, V,
-                                              512, ptr(pid), ptr(pmax), ptr(psum), 1, stream_handle())
+                                              tile, ptr(pid), ptr(pmax), ptr(psum), 1, stream_handle())
     assert rc == 0, native.ppocr_b200_last_error()
     sync()
     check_device_error(native)
@@ -573,7 +577,10 @@ def test_classifier_reference_signature(native, cuda, rows, H, V):
                                                 V, 512, ptr(pid), ptr(pmax), ptr(psum), 1, stream_handle()) == -1
 
 
-@pytest.mark.parametrize("rows,H,V", [(20480, 120, 18385), (16, 120, 300), (129, 64, 257)])
+@pytest.mark.parametrize("rows,H,V", [(20480, 120, 18385), (16, 120, 300), (129, 64, 257),
+                                      # vocabulary tile counts 8, 9, 11 (the four-threads-per-row merge,
+                                      # uneven tile strides) with row counts off the 64-row block
+                                      (1, 64, 2048), (65, 120, 2200), (130, 64, 2816)])
 def test_classifier_packed(native, cuda, rows, H, V):
     """Packed-weight entry used by the pipeline (hidden 120, BASELINE)."""
     hid, w, b = _classifier_case(rows, H, V)

@@ -58,7 +58,18 @@ def test_noalloc_matches_packed_twice(native, cuda, rows, H, V):
         assert torch.equal(ids2, ids)
         assert torch.equal(mx2, mx)
         assert (prob2 - prob).abs().max().item() <= 1e-6
+        # Reads (and clears) the allocation-free path's own timeout word too.
         assert native.ppocr_b200_device_error() == 0
+
+
+def test_noalloc_timeout_word_is_reported_once(native, cuda):
+    """A code in the allocation-free head's timeout word (stored the way a
+    projection whose bounded wait ran out stores it) is reported once by
+    ppocr_b200_device_error() and then cleared."""
+    assert native.ppocr_b200_device_error() == 0
+    assert native.ppocr_b200_test_store_error_code(1, 77) == 0, native.ppocr_b200_last_error()
+    assert native.ppocr_b200_device_error() == 77
+    assert native.ppocr_b200_device_error() == 0
 
 
 def test_noalloc_rejects_oversize(native, cuda):
