@@ -220,6 +220,14 @@ cudaError_t matmul_batched(const half *a, const half *b, half *y, int batches,
 // qkv [lines][seq][3*heads*dh] (q | k | v), out [lines][seq][heads*dh].
 // Reference rounding points: S = round(q.k^T), S = round(S*scale),
 // P = round(softmax(S)), O = round(P.v).
+// Tensor-core attention (attention_tc.cu) for the shapes
+// attention_tc_supported() accepts; attention() dispatches to it.
+bool attention_tc_supported(int seq, int dh);
+cudaError_t attention_tc(const half *qkv, half *out, int lines, int seq, int heads, int dh, float scale,
+                         cudaStream_t s);
+// SIMT attention kernels (seq.cu), used for every other shape.
+cudaError_t attention_simt(const half *qkv, half *out, int lines, int seq, int heads, int dh, float scale,
+                           cudaStream_t s);
 cudaError_t attention(const half *qkv, half *out, int lines, int seq, int heads,
                       int dh, float scale, cudaStream_t stream);
 

@@ -675,6 +675,16 @@ cudaError_t attention(const half *qkv, half *out, int lines, int seq, int heads,
                       int dh, float scale, cudaStream_t s) {
   if (lines <= 0)
     return cudaSuccess;
+  if (attention_tc_supported(seq, dh) && (reinterpret_cast<uintptr_t>(qkv) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(out) & 3) == 0)
+    return attention_tc(qkv, out, lines, seq, heads, dh, scale, s);
+  return attention_simt(qkv, out, lines, seq, heads, dh, scale, s);
+}
+
+cudaError_t attention_simt(const half *qkv, half *out, int lines, int seq, int heads,
+                           int dh, float scale, cudaStream_t s) {
+  if (lines <= 0)
+    return cudaSuccess;
   if (dh <= 16 && seq == 40 && heads * 40 <= 512) {
     const int threads = (heads * 40 + 31) / 32 * 32;
     const size_t smem = sizeof(float) * 3ull * heads * 40 * 16;
