@@ -101,13 +101,15 @@ __device__ __forceinline__ void fetch_windows(const AttArgs &g, int seq, int u, 
   const int ell = m / seq, t = m - ell * seq;
   const int line = group * g.G + ell;
   const bool valid = m < g.G * seq && line < g.lines;
-  const int hd = g.heads * g.dh, width = 3 * hd;
-  const long long total = static_cast<long long>(g.lines) * seq * width;
+  // Element indices fit 32 bits (the launcher checks the tensor size).
+  const uint32_t hd = static_cast<uint32_t>(g.heads * g.dh), width = 3 * hd;
+  const uint32_t total = static_cast<uint32_t>(g.lines) * seq * width;
+  const uint32_t row_e = (static_cast<uint32_t>(line) * seq + t) * width + h * g.dh;
 #pragma unroll
   for (int sec = 0; sec < 3; ++sec) {
-    const long long e0 = (static_cast<long long>(line) * seq + t) * width + sec * hd + h * g.dh;
-    const long long a0 = e0 & ~7ll; // 16-byte aligned element index
-    shift[sec] = static_cast<uint32_t>(e0 - a0) * 2;
+    const uint32_t e0 = row_e + sec * hd;
+    const uint32_t a0 = e0 & ~7u; // 16-byte aligned element index
+    shift[sec] = (e0 - a0) * 2;
 #pragma unroll
     for (int c = 0; c < 3; ++c) {
       // Stay inside the tensor (the element count is a multiple of 8, so a
@@ -166,6 +168,11 @@ __global__ void __launch_bounds__(kAttThreads, kAttCtasPerSm) attention_tc_kerne
   const int w_hi = min(SEQ * ((warp * 32 + 31) / SEQ + 1), rows);
   const int own = SEQ * ell - w_lo;         // 0 or SEQ
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  // Words of a head slice past head_dim are zero.
+  uint32_t dmask[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    dmask[i] = (2 * i < g.dh ? 0xFFFFu : 0u) | (2 * i + 1 < g.dh ? 0xFFFF0000u : 0u);
   const uint32_t idesc_s = idesc_f16_f32(128, 128);
   const uint32_t idesc_o = idesc_f16_f32(128, 16);
   bool ok = true;
@@ -195,14 +202,8 @@ __global__ void __launch_bounds__(kAttThreads, kAttCtasPerSm) attention_tc_kerne
           x[i] = lds_u32(a + 4 * i);
         const uint32_t bits = (sh & 2u) * 8u;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          uint32_t word = __funnelshift_r(x[i], x[i + 1], bits);
-          if (!valid || 2 * i >= g.dh)
-            word = 0;
-          else if (2 * i + 1 >= g.dh)
-            word &= 0xFFFFu;
-          w[i] = word;
-        }
+        for (int i = 0; i < 8; ++i)
+          w[i] = __funnelshift_r(x[i], x[i + 1], bits) & (valid ? dmask[i] : 0u);
       };
       take(raw, sh0, q);
       take(raw + 48, sh1, k);
@@ -240,7 +241,11 @@ __global__ void __launch_bounds__(kAttThreads, kAttCtasPerSm) attention_tc_kerne
                0);
       umma_commit(bar_s);
     }
-    ok = __syncthreads_and(ok && mbar_wait(bar_s, it & 1, abort));
+    // One thread watches the barrier; the rest wait in the block barrier
+    // (no issue slots spent spinning).
+    if (tid == 0)
+      ok = mbar_wait(bar_s, it & 1, abort);
+    ok = __syncthreads_and(ok);
     if (!ok)
       break;
     tc_fence_after();
@@ -259,21 +264,32 @@ __global__ void __launch_bounds__(kAttThreads, kAttCtasPerSm) attention_tc_kerne
         s[j] = round_half(__uint_as_float(own == 0 ? r[j] : r[SEQ + j]));
         mx = fmaxf(mx, s[j]);
       }
+      // exp(s - max) = 2^(s*log2e - max*log2e), pairs of lanes per packed
+      // fp32 FMA (each rounded once, as fmaf).
       const float mL = mx * kLog2e;
-      float sum = 0.f;
+      float2 sum2 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int j = 0; j < SEQ; ++j) {
-        s[j] = ex2_ftz(fmaf(s[j], kLog2e, -mL));
-        sum += s[j];
+      for (int j = 0; j < SEQ; j += 2) {
+        float2 a = make_float2(-mL, -mL);
+        ffma2(a, make_float2(s[j], s[j + 1]), make_float2(kLog2e, kLog2e));
+        s[j] = ex2_ftz(a.x);
+        s[j + 1] = ex2_ftz(a.y);
+        sum2.x += s[j];
+        sum2.y += s[j + 1];
       }
-      const float inv = 1.f / sum;
+      const float inv = 1.f / (sum2.x + sum2.y);
       const uint32_t pb = sbase + kOffP + static_cast<uint32_t>(SEQ * ell / 8) * kAPlane + row_off;
 #pragma unroll
-      for (int c = 0; c < SEQ / 8; ++c)
-        sts_v4(pb + c * kAPlane,
-               make_uint4(pack2(s[8 * c] * inv, s[8 * c + 1] * inv), pack2(s[8 * c + 2] * inv, s[8 * c + 3] * inv),
-                          pack2(s[8 * c + 4] * inv, s[8 * c + 5] * inv),
-                          pack2(s[8 * c + 6] * inv, s[8 * c + 7] * inv)));
+      for (int c = 0; c < SEQ / 8; ++c) {
+        uint32_t pw[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float2 pp = make_float2(0.f, 0.f);
+          ffma2(pp, make_float2(s[8 * c + 2 * e], s[8 * c + 2 * e + 1]), make_float2(inv, inv));
+          pw[e] = pack2(pp.x, pp.y);
+        }
+        sts_v4(pb + c * kAPlane, make_uint4(pw[0], pw[1], pw[2], pw[3]));
+      }
     }
     fence_async_smem();
     tc_fence_before();
@@ -287,7 +303,9 @@ __global__ void __launch_bounds__(kAttThreads, kAttCtasPerSm) attention_tc_kerne
                  sdesc_plain(sbase + kOffV + ks * 2 * kVPlane, kVPlane, 128), idesc_o, ks != 0);
       umma_commit(bar_o);
     }
-    ok = __syncthreads_and(ok && mbar_wait(bar_o, it & 1, abort));
+    if (tid == 0)
+      ok = mbar_wait(bar_o, it & 1, abort);
+    ok = __syncthreads_and(ok);
     if (!ok)
       break;
     tc_fence_after();
@@ -311,27 +329,41 @@ __global__ void __launch_bounds__(kAttThreads, kAttCtasPerSm) attention_tc_kerne
       // Output block of the unit: rows group*G*seq .. + rows, columns
       // [h*dh, h*dh + dh) of rows of heads*dh halves. Eight threads per row
       // write it as 32-bit words (a half at an unaligned start or end).
-      const int hdw = g.heads * g.dh;
-      const long long row0 = static_cast<long long>(group) * g.G * SEQ;
-      const long long nrows = min(static_cast<long long>(rows), static_cast<long long>(g.lines) * SEQ - row0);
+      const uint32_t hdw = static_cast<uint32_t>(g.heads * g.dh);
+      const int row0 = group * g.G * SEQ;
+      const int nrows = min(rows, g.lines * SEQ - row0);
       const int slot = tid & 7;
-#pragma unroll 1
-      for (int rr = tid >> 3; rr < nrows; rr += kAttThreads / 8) {
-        const long long e0 = (row0 + rr) * hdw + h * g.dh; // first element
+      // The 16 row passes are independent: all shared loads first, then
+      // all stores.
+      uint32_t wv[kAttThreads / 16];
+      uint32_t *dstw[kAttThreads / 16];
+#pragma unroll
+      for (int i = 0; i < kAttThreads / 16; ++i) {
+        const int rr = (tid >> 3) + i * (kAttThreads / 8);
+        const uint32_t e0 = static_cast<uint32_t>(row0 + rr) * hdw + h * g.dh; // first element
+        const int ld = static_cast<int>(e0 & 1u);            // a half before the first word
+        const int j = ld + 2 * slot;
         const uint32_t ob = sbase + kOffOut + static_cast<uint32_t>(rr) * 32;
+        wv[i] = (j & 1) ? (static_cast<uint32_t>(lds_u16(ob + 2 * j)) |
+                           (static_cast<uint32_t>(lds_u16(ob + 2 * j + 2)) << 16))
+                        : lds_u32(ob + 2 * j);
+        dstw[i] = reinterpret_cast<uint32_t *>(reinterpret_cast<uint16_t *>(g.out) + e0 + j);
+      }
+#pragma unroll
+      for (int i = 0; i < kAttThreads / 16; ++i) {
+        const int rr = (tid >> 3) + i * (kAttThreads / 8);
+        if (rr >= nrows)
+          break;
+        const uint32_t e0 = static_cast<uint32_t>(row0 + rr) * hdw + h * g.dh;
+        const int ld = static_cast<int>(e0 & 1u);
+        const int j = ld + 2 * slot;
         uint16_t *dst = reinterpret_cast<uint16_t *>(g.out) + e0;
-        const int lead = static_cast<int>(e0 & 1);          // a half before the first word
-        // halves [lead + 2*slot, lead + 2*slot + 2) as one word when inside
-        const int j = lead + 2 * slot;
-        if (j + 1 < g.dh) {
-          const uint32_t w = (j & 1) ? ((static_cast<uint32_t>(lds_u16(ob + 2 * j)) |
-                                         (static_cast<uint32_t>(lds_u16(ob + 2 * j + 2)) << 16)))
-                                     : lds_u32(ob + 2 * j);
-          *reinterpret_cast<uint32_t *>(dst + j) = w;
-        } else if (j < g.dh) {
+        const uint32_t ob = sbase + kOffOut + static_cast<uint32_t>(rr) * 32;
+        if (j + 1 < g.dh)
+          *dstw[i] = wv[i];
+        else if (j < g.dh)
           dst[j] = lds_u16(ob + 2 * j);
-        }
-        if (slot == 0 && lead)
+        if (slot == 0 && ld)
           dst[0] = lds_u16(ob);
       }
     }
@@ -370,6 +402,9 @@ cudaError_t attention_tc(const half *qkv, half *out, int lines, int seq, int hea
   // words need a 4-byte aligned output.
   if (!attention_tc_supported(seq, dh) || heads <= 0 || (reinterpret_cast<uintptr_t>(qkv) & 15) ||
       (reinterpret_cast<uintptr_t>(out) & 3))
+    return cudaErrorInvalidValue;
+  // 32-bit element indices inside the kernel.
+  if (static_cast<long long>(lines) * seq * 3 * heads * dh >= (1ll << 31))
     return cudaErrorInvalidValue;
   AttArgs a{};
   a.qkv = qkv;

@@ -676,7 +676,8 @@ cudaError_t attention(const half *qkv, half *out, int lines, int seq, int heads,
   if (lines <= 0)
     return cudaSuccess;
   if (attention_tc_supported(seq, dh) && (reinterpret_cast<uintptr_t>(qkv) & 15) == 0 &&
-      (reinterpret_cast<uintptr_t>(out) & 3) == 0)
+      (reinterpret_cast<uintptr_t>(out) & 3) == 0 &&
+      static_cast<long long>(lines) * seq * 3 * heads * dh < (1ll << 31))
     return attention_tc(qkv, out, lines, seq, heads, dh, scale, s);
   return attention_simt(qkv, out, lines, seq, heads, dh, scale, s);
 }
