@@ -114,3 +114,45 @@ def test_op_entry_points_reject_bad_arguments():
     assert lib.ppocr_b200_classifier_workspace(1281, 18385, 8, 128, ctypes.byref(nrb), ctypes.byref(nvb),
                                                ctypes.byref(cnt)) == 0
     assert (nrb.value, nvb.value, cnt.value) == (161, 144, 161 * 144 * 8)
+
+
+def test_reference_engine_loads_and_validates_catalog(tmp_path):
+    """The reference's own catalog engine (native/src/engine/
+    model_engine_compiled.cpp, unmodified, oracle/_ref/libref_engine.so) loads
+    a catalog of this repository's libraries written by write_catalog (dlopen,
+    dlsym of the seven symbols, PpocrModelInfo checks, profiles sorted by
+    batch) and rejects a weights file of the wrong size with its own message.
+    No CUDA call is made. Skipped where the reference tree was never present
+    to build the engine."""
+    engine = REPO / "oracle" / "_ref" / "libref_engine.so"
+    if not engine.exists():
+        pytest.skip("oracle/_ref/libref_engine.so not built (reference tree absent)")
+    from ppocr_b200 import models
+
+    lib = ctypes.CDLL(str(engine))
+    lib.ref_engine_error.restype = ctypes.c_char_p
+    lib.ref_engine_load.restype = ctypes.c_void_p
+    lib.ref_engine_load.argtypes = [ctypes.c_char_p]
+    lib.ref_engine_profiles.argtypes = [ctypes.c_void_p]
+    lib.ref_engine_profile_shape.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_longlong)]
+    lib.ref_engine_destroy.argtypes = [ctypes.c_void_p]
+    for n in ("rec_b64", "rec_b2"):
+        models.ensure_weights(n)
+    catalog = models.write_catalog("recognizer", ["rec_b64", "rec_b2"], tmp_path / "ok")
+    h = lib.ref_engine_load(str(catalog).encode())
+    assert h, lib.ref_engine_error().decode()
+    try:
+        assert lib.ref_engine_profiles(h) == 2
+        shapes = []
+        for p in range(2):
+            s = (ctypes.c_longlong * 4)()
+            lib.ref_engine_profile_shape(h, p, s)
+            shapes.append(tuple(s))
+        assert shapes == [(2, 3, 48, 320), (64, 3, 48, 320)]
+    finally:
+        lib.ref_engine_destroy(h)
+    bad = tmp_path / "w.f32"
+    bad.write_bytes(b"\0" * 64)
+    (tmp_path / "models.tsv").write_text(f"{models.library_path('rec_b2')}\t{bad}\n")
+    assert not lib.ref_engine_load(str(tmp_path / "models.tsv").encode())
+    assert b"Compiled weight size mismatch" in lib.ref_engine_error()
