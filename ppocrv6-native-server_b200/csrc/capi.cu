@@ -306,7 +306,8 @@ int ppocr_b200_gemm_epilogue(const void *x, const void *w, const void *bias,
 int ppocr_b200_matmul(const void *a, const void *b, void *y, int batches,
                       int m, int n, int k, cudaStream_t stream) {
   g_error.clear();
-  if (!a || !b || !y || batches < 0 || m < 0 || n < 0 || k < 0)
+  // Empty operands (k = 0) may be null: the product is zeros.
+  if ((k > 0 && (!a || !b)) || !y || batches < 0 || m < 0 || n < 0 || k < 0)
     return fail("invalid matmul arguments");
   return status(matmul_batched(H(a), H(b), Hm(y), batches, m, n, k,
                                static_cast<long long>(m) * k,

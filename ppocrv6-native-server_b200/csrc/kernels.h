@@ -213,6 +213,10 @@ cudaError_t mean_rows(const half *x, half *y, int rows, int cols,
 cudaError_t mean_nhwc(const half *x, half *y, int batch, int C, int spatial,
                       cudaStream_t stream);
 // Batched row-major matmul y[b] = a[b] (m x k) . b[b] (k x n), fp32 accumulate.
+// Batched matmul on the tensor cores with SIMT-staged operands
+// (matmul_tc.cu); matmul_batched dispatches to it.
+cudaError_t matmul_tc(const half *a, const half *b, half *y, int batches, int m, int n, int k, long long sa,
+                      long long sb, long long sy, cudaStream_t s);
 cudaError_t matmul_batched(const half *a, const half *b, half *y, int batches,
                            int m, int n, int k, long long sa, long long sb,
                            long long sy, cudaStream_t stream);

@@ -666,6 +666,10 @@ cudaError_t matmul_batched(const half *a, const half *b, half *y, int batches,
                            long long sy, cudaStream_t s) {
   if (batches <= 0 || m <= 0 || n <= 0)
     return cudaSuccess;
+  // Tensor cores (matmul_tc.cu) whenever the grid fits; the SIMT tile
+  // kernel remains for batch counts past the grid's z limit.
+  if (batches <= 65535 && k >= 0)
+    return matmul_tc(a, b, y, batches, m, n, k, sa, sb, sy, s);
   dim3 grid((n + 15) / 16, (m + 15) / 16, batches);
   matmul_kernel<<<grid, dim3(16, 16), 0, s>>>(a, b, y, m, n, k, sa, sb, sy);
   return cudaGetLastError();

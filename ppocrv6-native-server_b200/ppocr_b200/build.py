@@ -31,7 +31,7 @@ COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
 
 LIB_SOURCES = ["common.cu", "tc_gemm.cu", "halo_conv.cu", "dwpw.cu", "stem_tc.cu", "spatial.cu", "seq.cu", "head.cu",
                "detect.cu", "components.cu", "preprocess.cu", "lines.cu", "runtime.cu", "capi.cu",
-               "head_noalloc.cu", "attention_tc.cu"]
+               "head_noalloc.cu", "attention_tc.cu", "matmul_tc.cu"]
 
 
 def _run(cmd: list[str]) -> None:

@@ -281,6 +281,22 @@ def test_softmax(native, cuda):
     assert_close(host(y), L.softmax(x), what="softmax")
 
 
+@pytest.mark.parametrize("batches,m,n,k", [(16, 40, 40, 15), (16, 40, 15, 40), (3, 200, 300, 130), (1, 5, 7, 3),
+                                           (2, 129, 17, 64), (4, 33, 64, 65), (2, 16, 128, 0)])
+def test_matmul_batched(native, cuda, batches, m, n, k):
+    """Runtime::matmul with a computed right-hand side (the exporter's
+    attention products; tensor cores with SIMT-staged operands): fp32
+    accumulation, one fp16 rounding, against the oracle; k = 0 gives zeros."""
+    r = rng(30 + m + n + k)
+    a = f16(r.standard_normal((batches, m, k)))
+    b = f16(r.standard_normal((batches, k, n)))
+    y = torch.full((batches, m, n), 7.0, dtype=torch.float16, device=cuda)
+    assert native.ppocr_b200_matmul(ptr(dev(a)), ptr(dev(b)), ptr(y), batches, m, n, k, stream_handle()) == 0
+    sync()
+    check_device_error(native)
+    assert_close(host(y), L.matmul(a, b), what="matmul")
+
+
 @pytest.mark.parametrize("lines,seq,heads,dh", [(4, 40, 8, 15), (3, 25, 4, 16), (2, 20, 2, 24), (2, 70, 2, 8),
                                                (1, 10, 2, 40), (3, 17, 3, 5), (2, 64, 8, 16),
                                                (5, 40, 3, 7), (2, 40, 12, 16), (600, 40, 8, 15)])
