@@ -71,7 +71,8 @@ __global__ void __launch_bounds__(kDwpwThreads, 1)
   uint8_t *wpw = abuf + 2 * A_BYTES;              // [CO][128 B]
   half *wdw = reinterpret_cast<half *>(wpw + ((W_BYTES + 1023) & ~1023u)); // [K*K][64]
   half *bdw = wdw + K * K * 64;                   // [64]
-  uint64_t *bars = reinterpret_cast<uint64_t *>(bdw + 64);
+  half *bpw = bdw + 64;                           // [CO] pointwise bias (staged)
+  uint64_t *bars = reinterpret_cast<uint64_t *>(bpw + CO);
   uint64_t *hfull = bars, *hempty = bars + 2, *afull = bars + 4, *aempty = bars + 6;
   uint64_t *tfull = bars + 8, *tempty = bars + 10, *wbar = bars + 12, *drain = bars + 13;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
@@ -99,6 +100,8 @@ __global__ void __launch_bounds__(kDwpwThreads, 1)
   }
   if (threadIdx.x < 64)
     bdw[threadIdx.x] = g.bdw ? g.bdw[threadIdx.x] : __float2half(0.f);
+  for (int c = threadIdx.x; c < CO; c += blockDim.x)
+    bpw[c] = g.bpw ? g.bpw[c] : __float2half(0.f);
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
@@ -279,7 +282,7 @@ __global__ void __launch_bounds__(kDwpwThreads, 1)
             for (int e = 0; e < 8; ++e)
               v[e] = round_half(__uint_as_float(rr[8 * h + e]));
             if (g.bpw) {
-              const uint4 bb = __ldg(reinterpret_cast<const uint4 *>(g.bpw + cc));
+              const uint4 bb = lds_v4(smem_u32(bpw + cc));
               const half2 *bh = reinterpret_cast<const half2 *>(&bb);
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
@@ -313,7 +316,7 @@ template <int K, int CO, int ACT1, int ACT2>
 cudaError_t launch_dwpw(const CUtensorMap &mx, const CUtensorMap &mw, const DwpwArgs &g, cudaStream_t s) {
   auto kernel = dwpw_kernel<K, CO, ACT1, ACT2>;
   const size_t smem = 1024 + 2 * size_t(g.halo_stride) + 2 * 16384 + ((CO * 128 + 1023) & ~1023) + K * K * 128 +
-                      128 + 256;
+                      128 + CO * 2 + 256;
   static std::once_flag once[64];
   int dev = 0;
   cudaGetDevice(&dev);
