@@ -780,6 +780,11 @@ def config_arm(args):
         h2d = x_h.numel() * 2
         d2h = out_h.numel() * 2
         dom, dname, dms, dbytes, dflops, per, names = _dominant(model, name)
+        if dname == "dwpw_block":
+            # The fused block reads the depthwise input and writes the
+            # pointwise output (the graph's layer table describes the two
+            # layers separately): the fused minimum, weights included.
+            dbytes = (16 * 48 * 320 * 64 + 16 * 48 * 320 * 128 + 64 * 25 + 128 * 64 + 64 + 128) * 2.0
         roof = _roofline_for("hbm", dms, dbytes, dflops, f"{args.config}:{dname}#{dom}", peak_tf, peak_hbm,
                              peak_kind)
         g, _ = models.graph(name)

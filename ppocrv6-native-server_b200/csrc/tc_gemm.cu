@@ -869,9 +869,12 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   }
   int bn = pick_bn(s.Co);
   const int taps = s.KH * s.KW;
-  // Segment length: 32 pixels when it divides the output width (fewer TMA
-  // boxes per stage), else 16.
-  const int seg_log2 = OW % 32 == 0 ? 5 : 4;
+  // Segment length: 32 pixels when that pads the output row no more than
+  // 16-pixel segments do (half the TMA boxes per stage: OW = 30, 60, 120 of
+  // the detector, multiples of 32), else 16. Pixels past OW are zero-filled
+  // on load and not stored.
+  const int pad16 = (OW + 15) / 16 * 16, pad32 = (OW + 31) / 32 * 32;
+  const int seg_log2 = pad32 <= pad16 ? 5 : 4;
   const cuuint32_t seg = 1u << seg_log2;
   const int kb_tap = (s.Ci + kBK - 1) / kBK;
   const int num_kb = kb_tap * taps;
