@@ -979,9 +979,19 @@ cudaError_t tc_deconv(const half *x, const half *wpacked, const half *bias_rep,
     return cudaErrorInvalidValue;
   // N is a multiple of 64, so the tile (256, 128 or 64 columns) and each
   // 64-column store chunk cover whole taps' channel blocks.
-  const int bn = pick_bn(N);
+  int bn = pick_bn(N);
   const int seg_log2 = W % 32 == 0 ? 5 : 4;
   const cuuint32_t seg = 1u << seg_log2;
+  // One k-block per tile (Ci <= 64 in the DB head): the epilogue, not the
+  // tensor core, sets the pace. With enough tiles, 256-row x 128-column
+  // tiles put 8 epilogue warps on a double-buffered accumulator instead of
+  // 4 warps on 128-row x 256-column tiles.
+  const long long m_rows = static_cast<long long>(batch) * H *
+                           ((W + static_cast<int>(seg) - 1) / static_cast<int>(seg)) * seg;
+  const bool two = N % 128 == 0 && (Ci + kBK - 1) / kBK <= 2 &&
+                   (m_rows + 2 * kBM - 1) / (2 * kBM) * (N / 128) >= 2LL * sm_count();
+  if (two)
+    bn = 128;
   CUtensorMap ma, mb, mc;
   cuuint64_t da[4] = {static_cast<cuuint64_t>(Ci), static_cast<cuuint64_t>(W),
                       static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(batch)};
@@ -1014,7 +1024,7 @@ cudaError_t tc_deconv(const half *x, const half *wpacked, const half *bias_rep,
   g.kb_per_tap = (Ci + kBK - 1) / kBK;
   g.num_kb = g.kb_per_tap;
   g.KW = 1;
-  g.mt = (g.M + kBM - 1) / kBM;
+  g.mt = (g.M + (two ? 2 * kBM : kBM) - 1) / (two ? 2 * kBM : kBM);
   g.nt = (N + bn - 1) / bn;
   g.epi.bias = bias_rep;
   g.epi.out = y;
@@ -1023,6 +1033,9 @@ cudaError_t tc_deconv(const half *x, const half *wpacked, const half *bias_rep,
   g.dec_co = Co;
   g.dec_kw = KW;
   g.err = device_error_word();
+  if (two)
+    return act == kActRelu ? launch<128, true, kEpiDeconv, kActRelu, 2>(ma, mb, mc, g, stream)
+                           : launch<128, true, kEpiDeconv, -1, 2>(ma, mb, mc, g, stream);
   switch (bn) {
   case 64:
     return act == kActRelu ? launch<64, true, kEpiDeconv, kActRelu>(ma, mb, mc, g, stream)
