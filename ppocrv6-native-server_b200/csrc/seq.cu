@@ -185,36 +185,6 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// Generic batched matmul, 16x16 output tile per block, fp32 accumulation.
-__global__ void __launch_bounds__(256)
-    matmul_kernel(const half *__restrict__ a, const half *__restrict__ b,
-                  half *__restrict__ y, int m, int n, int k, long long sa,
-                  long long sb, long long sy) {
-  __shared__ float as[16][17], bs[16][17];
-  const int bz = blockIdx.z;
-  const half *A = a + bz * sa;
-  const half *B = b + bz * sb;
-  const int row = blockIdx.y * 16 + threadIdx.y;
-  const int col = blockIdx.x * 16 + threadIdx.x;
-  float acc = 0.f;
-  for (int k0 = 0; k0 < k; k0 += 16) {
-    const int ka = k0 + threadIdx.x, kb = k0 + threadIdx.y;
-    as[threadIdx.y][threadIdx.x] =
-        row < m && ka < k ? __half2float(A[static_cast<long long>(row) * k + ka])
-                          : 0.f;
-    bs[threadIdx.y][threadIdx.x] =
-        kb < k && col < n ? __half2float(B[static_cast<long long>(kb) * n + col])
-                          : 0.f;
-    __syncthreads();
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      acc = fmaf(as[threadIdx.y][j], bs[j][threadIdx.x], acc);
-    __syncthreads();
-  }
-  if (row < m && col < n)
-    y[bz * sy + static_cast<long long>(row) * n + col] = __float2half_rn(acc);
-}
-
 // One block per text line; warp h handles head h (looping if heads > warps).
 // Shared memory: the line's qkv rows as fp32 plus one seq x seq score tile
 // per warp.
@@ -666,13 +636,18 @@ cudaError_t matmul_batched(const half *a, const half *b, half *y, int batches,
                            long long sy, cudaStream_t s) {
   if (batches <= 0 || m <= 0 || n <= 0)
     return cudaSuccess;
-  // Tensor cores (matmul_tc.cu) whenever the grid fits; the SIMT tile
-  // kernel remains for batch counts past the grid's z limit.
-  if (batches <= 65535 && k >= 0)
-    return matmul_tc(a, b, y, batches, m, n, k, sa, sb, sy, s);
-  dim3 grid((n + 15) / 16, (m + 15) / 16, batches);
-  matmul_kernel<<<grid, dim3(16, 16), 0, s>>>(a, b, y, m, n, k, sa, sb, sy);
-  return cudaGetLastError();
+  if (k < 0)
+    return cudaErrorInvalidValue;
+  // Tensor cores (matmul_tc.cu), one launch per 65535 batches (the grid's z
+  // limit). With k = 0 the operands may be null and are not offset.
+  for (long long b0 = 0; b0 < batches; b0 += 65535) {
+    const int nb = static_cast<int>(batches - b0 < 65535 ? batches - b0 : 65535);
+    const cudaError_t e = matmul_tc(k > 0 ? a + b0 * sa : a, k > 0 ? b + b0 * sb : b, y + b0 * sy, nb, m, n, k,
+                                    sa, sb, sy, s);
+    if (e != cudaSuccess)
+      return e;
+  }
+  return cudaSuccess;
 }
 
 cudaError_t attention(const half *qkv, half *out, int lines, int seq, int heads,

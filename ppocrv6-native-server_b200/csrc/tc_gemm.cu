@@ -810,7 +810,22 @@ cudaError_t tc_gemm(const half *A, int M, int K, int lda, const half *W, int N,
       (epi.bias && !aligned16(epi.bias)) ||
       (epi.residual && (!aligned16(epi.residual) || epi.ldr % 8)))
     return cudaErrorInvalidValue;
-  const int bn = pick_bn(N);
+  int bn = pick_bn(N);
+  const int num_kb = (K + kBK - 1) / kBK;
+  // 256-row tiles: long K at N = 256 (see use_two_halves), or a short K
+  // loop at N <= 128, where the epilogue dominates and 8 epilogue warps with
+  // a double-buffered accumulator drain twice the rows per tile. Very short K
+  // (<= 8 k-blocks) at N >= 256 takes 256 x 128 tiles for the same reason
+  // (measured: 1x1 512 -> 512 over 245,760 rows 0.141 -> 0.129 ms; at 16
+  // k-blocks the extra A re-reads cost more than the epilogue gains).
+  bool two = use_two_halves(bn, num_kb, M, (N + bn - 1) / bn) ||
+             ((bn == 64 || bn == 128) && num_kb <= 4 &&
+              (M + 2 * kBM - 1) / (2 * kBM) * ((N + bn - 1) / bn) >= 2LL * sm_count());
+  if (!two && bn == 256 && num_kb <= 8 && N % 128 == 0 &&
+      (M + 2 * kBM - 1) / (2 * kBM) * (N / 128) >= 2LL * sm_count()) {
+    bn = 128;
+    two = true;
+  }
   CUtensorMap ma, mb;
   cuuint64_t da[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
   cuuint64_t sa[1] = {static_cast<cuuint64_t>(lda) * 2};
@@ -829,16 +844,9 @@ cudaError_t tc_gemm(const half *A, int M, int K, int lda, const half *W, int N,
   Args g{};
   g.M = M;
   g.N = N;
-  g.num_kb = (K + kBK - 1) / kBK;
+  g.num_kb = num_kb;
   g.kb_per_tap = g.num_kb;
   g.KW = 1;
-  // 256-row tiles: long K at N = 256 (see use_two_halves), or a short K
-  // loop at N <= 128, where the epilogue dominates and 8 epilogue warps with
-  // a double-buffered accumulator drain twice the rows per tile.
-  const int nt = (N + bn - 1) / bn;
-  const bool two = use_two_halves(bn, g.num_kb, M, nt) ||
-                   ((bn == 64 || bn == 128) && g.num_kb <= 4 &&
-                    (M + 2 * kBM - 1) / (2 * kBM) * nt >= 2LL * sm_count());
   const int bm = two ? 2 * kBM : kBM;
   g.mt = (M + bm - 1) / bm;
   g.nt = (N + bn - 1) / bn;

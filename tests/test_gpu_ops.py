@@ -282,7 +282,9 @@ def test_softmax(native, cuda):
 
 
 @pytest.mark.parametrize("batches,m,n,k", [(16, 40, 40, 15), (16, 40, 15, 40), (3, 200, 300, 130), (1, 5, 7, 3),
-                                           (2, 129, 17, 64), (4, 33, 64, 65), (2, 16, 128, 0)])
+                                           (2, 129, 17, 64), (4, 33, 64, 65), (2, 16, 128, 0),
+                                           # more batches than one grid's z extent: two launches
+                                           (70000, 2, 3, 5)])
 def test_matmul_batched(native, cuda, batches, m, n, k):
     """Runtime::matmul with a computed right-hand side (the exporter's
     attention products; tensor cores with SIMT-staged operands): fp32
@@ -299,7 +301,10 @@ def test_matmul_batched(native, cuda, batches, m, n, k):
 
 @pytest.mark.parametrize("lines,seq,heads,dh", [(4, 40, 8, 15), (3, 25, 4, 16), (2, 20, 2, 24), (2, 70, 2, 8),
                                                (1, 10, 2, 40), (3, 17, 3, 5), (2, 64, 8, 16),
-                                               (5, 40, 3, 7), (2, 40, 12, 16), (600, 40, 8, 15)])
+                                               (5, 40, 3, 7), (2, 40, 12, 16), (600, 40, 8, 15),
+                                               # tensor-core path edges: one line (a group of three with
+                                               # two empty), one head, head_dim 1, odd head widths
+                                               (1, 40, 1, 1), (7, 40, 16, 4), (3, 40, 5, 9)])
 def test_attention(native, cuda, lines, seq, heads, dh):
     r = rng(13 + seq)
     qkv = f16(r.standard_normal((lines, seq, 3 * heads * dh)))
