@@ -45,11 +45,13 @@ constexpr int kBK = 64;
 // pixels through a 5-D tensor map).
 enum Epi : int { kEpiStore = 0, kEpiVocab = 1, kEpiDeconv = 2 };
 
-// Epilogue warps: 4 (one per TMEM lane quarter) for stores, 8 with 256-row
-// tiles (one per quarter and M half); 16 for the exp-heavy vocabulary
+// Epilogue warps: 8 for stores, two per TMEM lane quarter: with 256-row
+// tiles each drains one M half, with 128-row tiles of 128 or 256 columns
+// each drains one column half (a lone tile's epilogue is a latency chain per
+// warp, so two warps per quarter halve it); 16 for the exp-heavy vocabulary
 // reduction (four warps per quarter, 64 columns each).
 template <int EPI, int MH> struct EpiWarps {
-  static constexpr int value = EPI == kEpiVocab ? 16 : 4 * MH;
+  static constexpr int value = EPI == kEpiVocab ? 16 : 8;
 };
 static_assert(kEpiDeconv != kEpiVocab, "deconv uses the store warps");
 template <int EPI, int MH> constexpr int threads_for() {
@@ -91,12 +93,10 @@ template <int BN, int MH = 1> struct Cfg {
   // of the next) while both fit the 512 TMEM columns, else one.
   static constexpr int NACC = MH * ACC_COLS <= 256 ? 2 : 1;
   static constexpr uint32_t TMEM_COLS = NACC * MH * ACC_COLS;
-  // TMA-store epilogue: each epilogue warp stages 32 rows x 64 columns
-  // (4 KB, 128-byte swizzled), double buffered with 4 epilogue warps and
-  // single buffered with 8, then one lane stores it.
+  // TMA-store epilogue: each of the 8 epilogue warps stages 32 rows x 64
+  // columns (4 KB, 128-byte swizzled), then one lane stores it.
   static constexpr bool TMA_EPI = BN % 64 == 0;
-  static constexpr int EPI_BUFS = MH == 1 ? 2 : 1;
-  static constexpr uint32_t EPI_BYTES = TMA_EPI ? 4 * MH * EPI_BUFS * 4096 : 0;
+  static constexpr uint32_t EPI_BYTES = TMA_EPI ? 8 * 4096 : 0;
   // As many operand stages (up to 8) as the rest of the 227 KB leaves.
   static constexpr int STAGES_FIT = (232448 - 1024 - 256 - EPI_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
@@ -110,22 +110,34 @@ template <int BN, int MH = 1> struct Cfg {
   static_assert(SMEM <= 232448, "dynamic shared memory above 227 KB");
 };
 
-// Fused epilogue for 8 consecutive columns [n0, n0+8) of one accumulator
-// row: v = round(acc) + bias; v = round(v) + residual; y = round(act(v)).
-// Columns at or past N and rows without an output row (orow < 0) skip their
-// bias/residual loads; their values are never stored.
+// Bias and residual of 8 consecutive columns [n0, n0+8) of one output row,
+// fetched ahead of the accumulator they are added to. Columns at or past N
+// and rows without an output row (orow < 0) fetch nothing; their values are
+// never stored.
+struct Extra8 {
+  uint4 bias, res;
+};
+
+__device__ __forceinline__ Extra8 fetch_extra8(const GemmEpilogue &e, int n0, int N, long long orow) {
+  Extra8 x{make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+  const bool col_ok = n0 + 8 <= N;
+  if (e.bias && col_ok)
+    x.bias = __ldg(reinterpret_cast<const uint4 *>(e.bias + n0));
+  if (e.residual && col_ok && orow >= 0)
+    x.res = __ldg(reinterpret_cast<const uint4 *>(e.residual + orow * e.ldr + n0));
+  return x;
+}
+
+// Fused epilogue for 8 consecutive columns of one accumulator row:
+// v = round(acc) + bias; v = round(v) + residual; y = round(act(v)).
 template <int ACT>
-__device__ __forceinline__ uint4 epilogue8(const uint32_t *acc,
-                                           const GemmEpilogue &e, int n0,
-                                           int N, long long orow) {
+__device__ __forceinline__ uint4 epilogue8(const uint32_t *acc, const GemmEpilogue &e, const Extra8 &x) {
   float v[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j)
     v[j] = round_half(__uint_as_float(acc[j]));
-  const bool col_ok = n0 + 8 <= N;
-  if (e.bias && col_ok) {
-    uint4 bb = __ldg(reinterpret_cast<const uint4 *>(e.bias + n0));
-    const half2 *bh = reinterpret_cast<const half2 *>(&bb);
+  if (e.bias) {
+    const half2 *bh = reinterpret_cast<const half2 *>(&x.bias);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       float2 f = __half22float2(bh[j]);
@@ -133,10 +145,8 @@ __device__ __forceinline__ uint4 epilogue8(const uint32_t *acc,
       v[2 * j + 1] += f.y;
     }
   }
-  if (e.residual && col_ok && orow >= 0) {
-    uint4 rr = __ldg(
-        reinterpret_cast<const uint4 *>(e.residual + orow * e.ldr + n0));
-    const half2 *rh = reinterpret_cast<const half2 *>(&rr);
+  if (e.residual) {
+    const half2 *rh = reinterpret_cast<const half2 *>(&x.res);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       float2 f = __half22float2(rh[j]);
@@ -356,23 +366,23 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
   } else {
     // Epilogue warps: TMEM lane quarter is fixed by warp id modulo 4.
     const int q = warp & 3;          // TMEM lane quarter
-    const int hf = (warp - 2) >> 2;  // vocab: column quarter; MH = 2: M half
+    const int hf = (warp - 2) >> 2;  // vocab: column quarter; stores: M or column half
     const int mh = MH == 2 ? hf : 0; // M half drained by this warp
     const int row_in_tile = mh * kBM + q * 32 + lane;
     const int ew = warp - 2;         // epilogue warp index (staging buffer)
+    // Stores with 128-row tiles of 128 or 256 columns: the two warps of a
+    // lane quarter drain one column half each. Narrower 128-row tiles are
+    // drained by the first four warps; the other four only release the
+    // accumulator.
+    constexpr bool kColSplit = EPI != kEpiVocab && MH == 1 && BN >= 128;
+    const bool drains = EPI == kEpiVocab || MH == 2 || kColSplit || hf == 0;
+    const int c_lo = kColSplit ? hf * (BN / 2) : 0;
+    const int c_hi = kColSplit ? c_lo + BN / 2 : BN;
     int it = 0;
-    int epi_buf = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
       const int mb = tile / g.nt, nb = tile - mb * g.nt;
       const int acc = it % NACC;
       const uint32_t acc_phase = (it / NACC) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort)) {
-        fail(g, abort, 4);
-        break;
-      }
-      tc_fence_after();
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                             (acc * MH + mh) * C::ACC_COLS;
       // Map this thread's accumulator row to an output row.
       long long orow = -1;
       if (CONV && g.row_segs) {
@@ -399,13 +409,32 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
           orow = m;
       }
       const int n_base = nb * BN;
+      // Bias and residual of this warp's first 64-column chunk are fetched
+      // before the accumulator wait, each later chunk's while the previous
+      // one is stored: their load latency overlaps the tile's main loop and
+      // the stores instead of sitting in the epilogue's critical path.
+      Extra8 nx[8];
+      if constexpr ((EPI == kEpiStore || EPI == kEpiDeconv) && C::TMA_EPI) {
+        if (drains) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            nx[j] = fetch_extra8(g.epi, n_base + c_lo + 8 * j, g.N, orow);
+        }
+      }
+      if (!mbar_wait(&tfull[acc], acc_phase, abort)) {
+        fail(g, abort, 4);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                             (acc * MH + mh) * C::ACC_COLS;
       if constexpr ((EPI == kEpiStore || EPI == kEpiDeconv) && C::TMA_EPI) {
         // 64-column chunks: TMEM -> registers -> fused epilogue -> swizzled
         // smem row (this thread's row) -> one TMA store per warp. TMA drops
         // rows past M / past the image width and columns past N.
         const GemmEpilogue &e = g.epi;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 64) {
+        for (int c = drains ? c_lo : c_hi; c < c_hi; c += 64) {
           uint32_t r[64];
           tmem_ld16(taddr + c, *reinterpret_cast<uint32_t(*)[16]>(r));
           tmem_ld16(taddr + c + 16, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
@@ -415,13 +444,18 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
           uint4 packed[8];
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            packed[j] = epilogue8<ACT>(r + 8 * j, e, n_base + c + 8 * j, g.N, orow);
-          // The store issued from this buffer EPI_BUFS chunks ago must have
-          // read its source before the buffer is overwritten.
+            packed[j] = epilogue8<ACT>(r + 8 * j, e, nx[j]);
+          if (c + 64 < c_hi) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              nx[j] = fetch_extra8(e, n_base + c + 64 + 8 * j, g.N, orow);
+          }
+          // The store issued from this warp's buffer for the previous chunk
+          // must have read its source before the buffer is overwritten.
           if (lane == 0)
-            bulk_wait_read<C::EPI_BUFS - 1>();
+            bulk_wait_read<0>();
           __syncwarp();
-          uint8_t *buf = epi_smem + (ew * C::EPI_BUFS + (C::EPI_BUFS == 2 ? epi_buf : 0)) * 4096;
+          uint8_t *buf = epi_smem + ew * 4096;
           uint8_t *row = buf + lane * 128;
 #pragma unroll
           for (int j = 0; j < 8; ++j)
@@ -470,12 +504,11 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
             }
             bulk_commit();
           }
-          epi_buf ^= 1;
         }
       } else if constexpr (EPI == kEpiStore) {
         const GemmEpilogue &e = g.epi;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
+        for (int c = drains ? 0 : BN; c < BN; c += 16) {
           uint32_t r[16];
           tmem_ld16(taddr + c, r);
           tmem_ld_wait();
@@ -486,7 +519,7 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
               if (n0 + 8 > g.N)
                 continue;
               *reinterpret_cast<uint4 *>(e.out + orow * e.ldo + n0) =
-                  epilogue8<ACT>(r + 8 * h, e, n0, g.N, orow);
+                  epilogue8<ACT>(r + 8 * h, e, fetch_extra8(e, n0, g.N, orow));
             }
           }
         }

@@ -41,6 +41,15 @@ GEMM_CASES = [
     # 256-row tiles for short K at N <= 128 (double-buffered accumulator)
     (76000, 64, 128, True, False, 3),
     (80000, 120, 64, True, True, 0),
+    # 128-row tiles drained by two warps per lane quarter, one column half
+    # each (N tiles of 128 and 256), bias / residual fetched ahead
+    (20480, 120, 120, True, True, 0),
+    (10240, 120, 240, True, True, 5),
+    (3000, 240, 256, False, True, 1),
+    # N tile 64 at 128 rows: four of the eight epilogue warps drain it
+    (1000, 64, 64, True, True, 1),
+    # 256 x 128 tiles for short K (<= 8 k-blocks) at N >= 256
+    (80000, 512, 512, True, False, 1),
 ]
 
 
