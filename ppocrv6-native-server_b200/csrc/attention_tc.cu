@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(kAttThreads, kAttCtasPerSm) attention_tc_kerne
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5;
+  pdl_launch_dependents();
   if (tid == 0) {
     mbar_init(bar_s, 1);
     mbar_init(bar_o, 1);
@@ -159,6 +160,8 @@ __global__ void __launch_bounds__(kAttThreads, kAttCtasPerSm) attention_tc_kerne
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Nothing above touches global memory (programmatic dependent launch).
+  pdl_wait();
 
   const int m = tid;                        // tile row (query) = key column
   const int rows = g.G * SEQ;
@@ -423,7 +426,7 @@ cudaError_t attention_tc(const half *qkv, half *out, int lines, int seq, int hea
   if (e != cudaSuccess)
     return e;
   const int grid = std::min(a.units, kAttCtasPerSm * sm_count());
-  attention_tc_kernel<40><<<grid, kAttThreads, smem, s>>>(a);
+  launch_pdl(attention_tc_kernel<40>, grid, kAttThreads, smem, s, a);
   return cudaGetLastError();
 }
 

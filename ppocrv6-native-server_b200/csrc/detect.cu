@@ -21,6 +21,7 @@ __global__ void __launch_bounds__(256)
                   const half *__restrict__ bias, half *__restrict__ y,
                   long long total, int H, int W, int Ci, int Co, int KH,
                   int KW, int act, bool vec) {
+  pdl_begin();
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= total)
     return;
@@ -84,6 +85,7 @@ __global__ void __launch_bounds__(256)
                         const half *__restrict__ bias, half *__restrict__ y,
                         uint32_t pixels, FastDiv by_w, FastDiv by_h, int Ci,
                         int Co, int KH, int KW, int act) {
+  pdl_begin();
   extern __shared__ float dsm[];
   const int nout = KH * KW * Co;
   for (int j = threadIdx.x; j < Ci * nout; j += blockDim.x)
@@ -158,6 +160,7 @@ __global__ void __launch_bounds__(256)
                         const half *__restrict__ bias, half *__restrict__ y,
                         uint32_t pixels, FastDiv by_w, FastDiv by_h, int Co,
                         int KH, int KW, int act) {
+  pdl_begin();
   constexpr int NOUT = 4;
   constexpr uint32_t PPW = 32 / G; // pixels per warp per load
   const int nout = KH * KW * Co;
@@ -234,6 +237,7 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     binarize_kernel(const float *__restrict__ prob, uint8_t *__restrict__ map,
                     size_t n, float thresh) {
+  pdl_begin();
   const size_t nv = n / 4; // whole float4 vectors
   const size_t v0 = static_cast<size_t>(blockIdx.x) * blockDim.x * 4 + threadIdx.x;
   float4 v[4];
@@ -272,8 +276,7 @@ cudaError_t binarize(const float *prob, uint8_t *map, size_t n, float thresh,
     return cudaErrorInvalidValue;
   const size_t vectors = n / 4;
   const size_t blocks = vectors ? (vectors + 1023) / 1024 : 1;
-  binarize_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(prob, map, n,
-                                                                 thresh);
+  launch_pdl(binarize_kernel, static_cast<unsigned>(blocks), 256, 0, s, prob, map, n, thresh);
   return cudaGetLastError();
 }
 
@@ -311,31 +314,27 @@ cudaError_t deconv_kxk(const half *x, const half *w, const half *bias, half *y,
       blocks = cap;
     auto k = G == 8 ? deconv_group_kernel<8, U> : G == 16 ? deconv_group_kernel<16, U>
                                                           : deconv_group_kernel<32, U>;
-    k<<<static_cast<unsigned>(blocks), 256, 0, s>>>(x, w, bias, y,
-                                                    static_cast<uint32_t>(pixels),
-                                                    FastDiv(W), FastDiv(H), Co, KH,
-                                                    KW, act);
+    launch_pdl(k, static_cast<unsigned>(blocks), 256, 0, s, x, w, bias, y,
+        static_cast<uint32_t>(pixels), FastDiv(W), FastDiv(H), Co, KH, KW, act);
     return cudaGetLastError();
   }
   const size_t smem = sizeof(float) * static_cast<size_t>(Ci) * nout;
   if (nout <= 16 && pixels < (1LL << 31) && smem <= 48 * 1024) {
     const unsigned blocks = static_cast<unsigned>((pixels + 255) / 256);
     if (nout <= 4)
-      deconv_small_kernel<4><<<blocks, 256, smem, s>>>(
-          x, w, bias, y, static_cast<uint32_t>(pixels), FastDiv(W), FastDiv(H),
-          Ci, Co, KH, KW, act);
+      launch_pdl(deconv_small_kernel<4>, blocks, 256, smem, s, x, w, bias, y,
+          static_cast<uint32_t>(pixels), FastDiv(W), FastDiv(H), Ci, Co, KH, KW, act);
     else
-      deconv_small_kernel<16><<<blocks, 256, smem, s>>>(
-          x, w, bias, y, static_cast<uint32_t>(pixels), FastDiv(W), FastDiv(H),
-          Ci, Co, KH, KW, act);
+      launch_pdl(deconv_small_kernel<16>, blocks, 256, smem, s, x, w, bias, y,
+          static_cast<uint32_t>(pixels), FastDiv(W), FastDiv(H), Ci, Co, KH, KW, act);
     return cudaGetLastError();
   }
   const bool vec = Co % 8 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(y) & 15) == 0;
   const long long total = static_cast<long long>(batch) * H * KH * W * KW *
                           (vec ? Co / 8 : Co);
-  deconv_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(
-      x, w, bias, y, total, H, W, Ci, Co, KH, KW, act, vec);
+  launch_pdl(deconv_kernel, static_cast<unsigned>((total + 255) / 256), 256, 0, s, x, w, bias, y,
+      total, H, W, Ci, Co, KH, KW, act, vec);
   return cudaGetLastError();
 }
 

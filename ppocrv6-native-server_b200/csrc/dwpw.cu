@@ -79,6 +79,7 @@ __global__ void __launch_bounds__(kDwpwThreads, 1)
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_launch_dependents();
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&hfull[i], 1);
@@ -93,6 +94,8 @@ __global__ void __launch_bounds__(kDwpwThreads, 1)
     *abort = 0;
     fence_barrier_init();
   }
+  // First global-memory access below (programmatic dependent launch).
+  pdl_wait();
   // Depthwise filter tap-major ([tap][channel]) and bias, staged once.
   for (int i = threadIdx.x; i < K * K * 64; i += blockDim.x) {
     const int tap = i >> 6, c = i & 63;
@@ -329,7 +332,7 @@ cudaError_t launch_dwpw(const CUtensorMap &mx, const CUtensorMap &mw, const Dwpw
   if (smem > 232448)
     return cudaErrorNotSupported;
   const int grid = g.tiles < sm_count() ? g.tiles : sm_count();
-  kernel<<<grid, kDwpwThreads, smem, s>>>(mx, mw, g);
+  launch_pdl(kernel, grid, kDwpwThreads, smem, s, mx, mw, g);
   return cudaGetLastError();
 }
 

@@ -103,6 +103,7 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntile = blockIdx.x % g.ntiles;
   const int first = blockIdx.x / g.ntiles, step = gridDim.x / g.ntiles;
+  pdl_launch_dependents();
   if (threadIdx.x == 0) {
     for (int b = 0; b < kMaxBufs; ++b) {
       mbar_init(&full[b], 1);
@@ -125,6 +126,8 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Nothing above touches global memory (programmatic dependent launch).
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -324,7 +327,7 @@ cudaError_t launch_halo(const CUtensorMap &mx, const CUtensorMap &mw, const Halo
   int grid = sm_count() / g.ntiles * g.ntiles;
   if (work < grid)
     grid = static_cast<int>(work);
-  kernel<<<grid, kHaloThreads, smem, s>>>(mx, mw, g);
+  launch_pdl(kernel, grid, kHaloThreads, smem, s, mx, mw, g);
   return cudaGetLastError();
 }
 

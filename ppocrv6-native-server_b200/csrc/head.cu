@@ -159,6 +159,7 @@ __global__ void __launch_bounds__(kArgmaxThreads)
     logits_argmax_kernel(const half *__restrict__ logits, int V,
                          int *__restrict__ ids, float *__restrict__ prob,
                          float *__restrict__ max_logit, int calc_prob) {
+  pdl_begin();
   const long long row = blockIdx.x;
   const half *lr = logits + row * V;
   const int head =
@@ -173,6 +174,7 @@ __global__ void __launch_bounds__(256)
                        const float *__restrict__ ps, int rows, int tiles,
                        int *__restrict__ ids, float *__restrict__ prob,
                        float *__restrict__ max_logit, int calc_prob) {
+  pdl_begin();
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= rows)
     return;
@@ -205,6 +207,7 @@ __global__ void __launch_bounds__(256)
                         int blank, int *__restrict__ out_ids,
                         int *__restrict__ out_len,
                         float *__restrict__ out_score) {
+  pdl_begin();
   const int line = blockIdx.x * blockDim.x + threadIdx.x;
   if (line >= lines)
     return;
@@ -236,6 +239,7 @@ __global__ void __launch_bounds__(256)
                           const float *__restrict__ max_logits,
                           float *__restrict__ out, int rows, int H, int V,
                           int cls) {
+  pdl_begin();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows)
@@ -402,6 +406,7 @@ __global__ void __launch_bounds__(THREADS)
     logits_argmax_row_kernel(const half *__restrict__ logits, int V,
                              int *__restrict__ ids, float *__restrict__ prob,
                              float *__restrict__ max_logit, int calc_prob) {
+  pdl_begin();
   __shared__ WarpPart slot[THREADS / 32];
   const long long row = blockIdx.x;
   SpanRegs<VPT> r;
@@ -430,7 +435,7 @@ cudaError_t logits_argmax_prob(const half *logits, int rows, int V, int *ids,
   // over a thread-block cluster 32.8 us, and computing a quarter of the
   // exponentials on the FMA pipe 17.9 us).
   auto row_form = [&](auto kernel, int threads) {
-    kernel<<<rows, threads, 0, s>>>(logits, V, ids, prob, max_logit, calc_prob);
+    launch_pdl(kernel, rows, threads, 0, s, logits, V, ids, prob, max_logit, calc_prob);
     return cudaGetLastError();
   };
   if (V <= 4088)
@@ -444,8 +449,8 @@ cudaError_t logits_argmax_prob(const half *logits, int rows, int V, int *ids,
   if (V <= 32760)
     return row_form(logits_argmax_row_kernel<512, 8>, 512);
   // Longer rows: 16-byte loads in a loop over the row (two passes).
-  logits_argmax_kernel<<<rows, kArgmaxThreads, 0, s>>>(logits, V, ids, prob,
-                                                       max_logit, calc_prob);
+  launch_pdl(logits_argmax_kernel, rows, kArgmaxThreads, 0, s, logits, V, ids, prob, max_logit,
+      calc_prob);
   return cudaGetLastError();
 }
 
@@ -461,6 +466,7 @@ __global__ void __launch_bounds__(256)
                         const float *__restrict__ ps, int rows, int tiles,
                         int *__restrict__ ids, float *__restrict__ prob,
                         float *__restrict__ max_logit, int calc_prob) {
+  pdl_begin();
   __shared__ float sm[4][64];
   __shared__ int si[4][64];
   const int r = threadIdx.x & 63, q = threadIdx.x >> 6;
@@ -512,13 +518,12 @@ cudaError_t vocab_merge(const float *part_max, const int *part_id,
   if (rows <= 0)
     return cudaSuccess;
   if (tiles >= 8) {
-    vocab_merge4_kernel<<<(rows + 63) / 64, 256, 0, s>>>(part_max, part_id, part_sum, rows, tiles,
-                                                       ids, prob, max_logit, calc_prob);
+    launch_pdl(vocab_merge4_kernel, (rows + 63) / 64, 256, 0, s, part_max, part_id, part_sum, rows,
+        tiles, ids, prob, max_logit, calc_prob);
     return cudaGetLastError();
   }
-  vocab_merge_kernel<<<(rows + 255) / 256, 256, 0, s>>>(
-      part_max, part_id, part_sum, rows, tiles, ids, prob, max_logit,
-      calc_prob);
+  launch_pdl(vocab_merge_kernel, (rows + 255) / 256, 256, 0, s, part_max, part_id, part_sum, rows,
+      tiles, ids, prob, max_logit, calc_prob);
   return cudaGetLastError();
 }
 
@@ -529,8 +534,8 @@ cudaError_t ctc_collapse(const int *ids, const float *probs, int lines, int T,
     return cudaSuccess;
   if (T < 0 || !ids || !out_ids || !out_len || !out_score)
     return cudaErrorInvalidValue;
-  ctc_collapse_kernel<<<(lines + 255) / 256, 256, 0, s>>>(
-      ids, probs, lines, T, blank, out_ids, out_len, out_score);
+  launch_pdl(ctc_collapse_kernel, (lines + 255) / 256, 256, 0, s, ids, probs, lines, T, blank,
+      out_ids, out_len, out_score);
   return cudaGetLastError();
 }
 
@@ -548,8 +553,8 @@ cudaError_t selected_class_vs_max(const half *hidden, const half *w,
   if (!hidden || !w || !bias || !max_logits || !out || H <= 0 || V <= 0 ||
       class_id < 0 || class_id >= V)
     return cudaErrorInvalidValue;
-  selected_class_kernel<<<(rows + 7) / 8, 256, 0, s>>>(
-      hidden, w, bias, max_logits, out, rows, H, V, class_id);
+  launch_pdl(selected_class_kernel, (rows + 7) / 8, 256, 0, s, hidden, w, bias, max_logits, out,
+      rows, H, V, class_id);
   return cudaGetLastError();
 }
 

@@ -196,6 +196,16 @@ cudaError_t copy_input_nhwc_f16(const half *x, half *y, int valid, int batch,
                                 int C, int H, int W, cudaStream_t stream);
 cudaError_t half_to_float(const half *x, float *y, size_t n,
                           cudaStream_t stream);
+// ABI input staging of a layout the graph reads as is: the first `valid`
+// bytes of x, zeros up to `total` bytes (16-byte vectors when aligned).
+cudaError_t stage_bytes(const void *x, void *y, size_t valid, size_t total,
+                        cudaStream_t stream);
+// ABI output: n fp16 values copied (to_f32: widened to f32) into y, and the
+// device error word `err` mirrored into host-mapped memory `err_host`
+// (device pointer) by the same kernel, so that one launch replaces the output
+// copy and the error-word read back.
+cudaError_t output_copy(const half *x, void *y, size_t n, bool to_f32,
+                        const int *err, int *err_host, cudaStream_t stream);
 // NCHW f32 (valid images) -> NHWC fp16 with zero images past `valid`: the
 // ABI input copy fused with the exporter's channels-last transpose.
 cudaError_t nchw_f32_to_nhwc_f16(const float *x, half *y, int valid,

@@ -62,6 +62,7 @@ __global__ void __launch_bounds__(kMmThreads) matmul_tc_kernel(const __grid_cons
   const int batch = blockIdx.z, row0 = blockIdx.y * 128, col0 = blockIdx.x * NT;
   const half *A = g.a + batch * g.sa;
   const half *B = g.b + batch * g.sb;
+  pdl_launch_dependents();
   if (tid == 0) {
     mbar_init(bar, 1);
     fence_barrier_init();
@@ -74,6 +75,8 @@ __global__ void __launch_bounds__(kMmThreads) matmul_tc_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Nothing above touches global memory (programmatic dependent launch).
+  pdl_wait();
   const uint32_t idesc = idesc_f16_f32(128, NT);
   const int row = row0 + tid;
   const int col = col0 + tid;
@@ -184,7 +187,7 @@ cudaError_t launch_mm(const MmArgs &a, int batches, cudaStream_t s) {
   if (e != cudaSuccess)
     return e;
   dim3 grid((a.n + NT - 1) / NT, (a.m + 127) / 128, batches);
-  matmul_tc_kernel<NT><<<grid, kMmThreads, smem, s>>>(a);
+  launch_pdl(matmul_tc_kernel<NT>, grid, kMmThreads, smem, s, a);
   return cudaGetLastError();
 }
 

@@ -41,7 +41,8 @@ struct Instance {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   bool warmed = false;
-  int *error_seen = nullptr; // pinned: the error word after the last replay
+  int *error_seen = nullptr;     // host-mapped: the error word after the last replay
+  int *error_seen_dev = nullptr; // its device address
   bool error_pending = false;
 
   ~Instance() {
@@ -78,8 +79,9 @@ struct Instance {
     // The per-device error word is allocated here, outside any capture.
     if (!pb2::device_error_word())
       throw std::runtime_error("Cannot allocate device error word");
-    CU(cudaMallocHost(&error_seen, sizeof(int)));
+    CU(cudaHostAlloc(&error_seen, sizeof(int), cudaHostAllocMapped));
     *error_seen = 0;
+    CU(cudaHostGetDevicePointer(reinterpret_cast<void **>(&error_seen_dev), error_seen, 0));
     CU(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
     CU(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
   }
@@ -98,7 +100,7 @@ struct Instance {
     if (!error_pending || cudaEventQuery(done) != cudaSuccess)
       return;
     error_pending = false;
-    if (const int code = *error_seen) {
+    if (const int code = *reinterpret_cast<volatile int *>(error_seen)) {
       *error_seen = 0;
       pb2::take_device_error(); // clear the word for the next batch
       throw std::runtime_error("kernel wait timed out in the previous batch (code " +
@@ -124,15 +126,11 @@ struct Instance {
       stage();
     }
     CU(cudaGraphLaunch(exec, r.stream));
+    // One kernel copies the output (widened to f32 for the detector) and
+    // mirrors the error word into host-mapped memory for check_previous().
     const size_t output_n = OUTPUT_ELEMENTS / MODEL_INPUT_SHAPE[0] * batch;
-    if (PPOCR_MODEL_DETECTOR)
-      CU(pb2::half_to_float(r.t[OUTPUT_ID], static_cast<float *>(output),
-                            output_n, r.stream));
-    else
-      CU(cudaMemcpyAsync(output, r.t[OUTPUT_ID], output_n * 2,
-                         cudaMemcpyDeviceToDevice, r.stream));
-    CU(cudaMemcpyAsync(error_seen, pb2::device_error_word(), sizeof(int),
-                       cudaMemcpyDeviceToHost, r.stream));
+    CU(pb2::output_copy(r.t[OUTPUT_ID], output, output_n, PPOCR_MODEL_DETECTOR != 0,
+                        pb2::device_error_word(), error_seen_dev, r.stream));
     error_pending = true;
     CU(cudaGetLastError());
     CU(cudaEventRecord(done, r.stream));
@@ -170,13 +168,8 @@ struct Instance {
       if (r.first_op == 1) {
         // Already channels-last: copy the valid images, zero the rest.
         const size_t per_image = INPUT_ELEMENTS / MODEL_INPUT_SHAPE[0] * 2;
-        CU(cudaMemcpyAsync(r.t[r.input_nhwc_id], input, per_image * batch,
-                           cudaMemcpyDeviceToDevice, r.stream));
-        if (batch < MODEL_INPUT_SHAPE[0])
-          CU(cudaMemsetAsync(reinterpret_cast<char *>(r.t[r.input_nhwc_id]) +
-                                 per_image * batch,
-                             0, per_image * (MODEL_INPUT_SHAPE[0] - batch),
-                             r.stream));
+        CU(pb2::stage_bytes(input, r.t[r.input_nhwc_id], per_image * batch,
+                            per_image * MODEL_INPUT_SHAPE[0], r.stream));
       } else {
         CU(pb2::copy_input_nhwc_f16(static_cast<const half *>(input), r.t[0],
                                     batch, MODEL_INPUT_SHAPE[0],

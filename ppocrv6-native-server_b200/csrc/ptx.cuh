@@ -7,7 +7,9 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
+#include <cuda_runtime.h>
 #include <stdint.h>
+#include <utility>
 
 namespace pb2 {
 
@@ -90,6 +92,46 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
       return false;
   }
   return true;
+}
+
+// ------------------------------------------------ programmatic dependent launch
+// Kernels of the layer path are launched with programmatic stream
+// serialization (launch_pdl below, kept when a stream is captured into a
+// CUDA graph): the next kernel's CTAs may be scheduled while this kernel's
+// last CTAs run, so its launch and its global-memory-free prologue (barrier
+// set-up, TMEM allocation, tensor-map prefetch) overlap them.
+//  * pdl_wait(): blocks until every prerequisite grid has completed and its
+//    memory operations are visible. Every kernel launched by launch_pdl calls
+//    it in every CTA before its first global-memory access (read or write),
+//    so completion of a kernel implies completion of all earlier ones.
+//  * pdl_launch_dependents(): lets the dependent grid be scheduled once every
+//    CTA of this grid has issued it (or exited). Safe at any point: the
+//    dependent still waits for this grid's completion in pdl_wait().
+// Both are no-ops for a grid launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// The two together, for kernels without a prologue to overlap.
+__device__ __forceinline__ void pdl_begin() {
+  pdl_launch_dependents();
+  pdl_wait();
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args &&...args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------- TMA loads

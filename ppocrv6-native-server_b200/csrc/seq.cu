@@ -33,6 +33,7 @@ __global__ void __launch_bounds__(256)
     layernorm_kernel(const half *__restrict__ x, const half *__restrict__ scale,
                      const half *__restrict__ bias, half *__restrict__ y,
                      int rows, int cols, float eps) {
+  pdl_begin();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows)
@@ -66,6 +67,7 @@ __global__ void __launch_bounds__(256)
     layernorm_vec_kernel(const half *__restrict__ x, const half *__restrict__ scale,
                          const half *__restrict__ bias, half *__restrict__ y,
                          int rows, int cols, float eps) {
+  pdl_begin();
   constexpr int GPW = 32 / LPR; // row groups per warp
   const int lane = threadIdx.x & 31;
   const int sub = lane / LPR, l = lane % LPR;
@@ -129,6 +131,7 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     softmax_kernel(const half *__restrict__ x, half *__restrict__ y, int rows,
                    int cols) {
+  pdl_begin();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows)
@@ -150,6 +153,7 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     mean_rows_kernel(const half *__restrict__ x, half *__restrict__ y, int rows,
                      int cols) {
+  pdl_begin();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows)
@@ -167,6 +171,7 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     mean_nhwc_kernel(const half *__restrict__ x, half *__restrict__ y, int C,
                      int spatial) {
+  pdl_begin();
   __shared__ float part[8][33];
   const int c = blockIdx.x * 32 + (threadIdx.x & 31);
   const int w = threadIdx.x >> 5;
@@ -191,6 +196,7 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     attention_kernel(const half *__restrict__ qkv, half *__restrict__ out,
                      int seq, int heads, int dh, float scale) {
+  pdl_begin();
   extern __shared__ float sm[];
   const int width = 3 * heads * dh;
   float *xs = sm;                      // [seq][width]
@@ -256,6 +262,7 @@ __global__ void __launch_bounds__(256)
     attention_staged_kernel(const half *__restrict__ qkv,
                             half *__restrict__ out, int seq, int heads, int dh,
                             float scale) {
+  pdl_begin();
   constexpr int RS = DP + 8;
   extern __shared__ uint4 att_smem[];
   half *qs = reinterpret_cast<half *>(att_smem); // [heads][seq][RS]
@@ -349,6 +356,7 @@ template <int SEQ>
 __global__ void __launch_bounds__(512)
     attention_f32_kernel(const half *__restrict__ qkv, half *__restrict__ out,
                          int heads, int dh, float scale, FastDiv by_dh, int vec) {
+  pdl_begin();
   constexpr int DP = 16;
   extern __shared__ float4 att32_smem[];
   float *qs = reinterpret_cast<float *>(att32_smem); // [heads][SEQ][DP]
@@ -469,6 +477,7 @@ __global__ void __launch_bounds__(512)
     attention_rows_kernel(const half *__restrict__ qkv, half *__restrict__ out,
                           int seq, int heads, int dh, float scale,
                           FastDiv by_hd, FastDiv by_dh, FastDiv by_seq, int vec) {
+  pdl_begin();
   constexpr int DP = 16;
   extern __shared__ uint4 att_smem[];
   half *qs = reinterpret_cast<half *>(att_smem); // [heads][seq][DP]
@@ -591,8 +600,8 @@ cudaError_t layernorm(const half *x, const half *scale, const half *bias,
     constexpr int RPW = 4;
     auto launch = [&](auto kernel, int lpr) {
       const long long per_block = 8LL * (32 / lpr) * RPW;
-      kernel<<<static_cast<unsigned>((rows + per_block - 1) / per_block), 256, 0, s>>>(
-          x, scale, bias, y, rows, cols, eps);
+      launch_pdl(kernel, static_cast<unsigned>((rows + per_block - 1) / per_block), 256, 0, s, x,
+          scale, bias, y, rows, cols, eps);
       return cudaGetLastError();
     };
     if (cols <= 64)
@@ -601,8 +610,7 @@ cudaError_t layernorm(const half *x, const half *scale, const half *bias,
       return launch(layernorm_vec_kernel<16, RPW>, 16);
     return launch(layernorm_vec_kernel<32, RPW>, 32);
   }
-  layernorm_kernel<<<rows_blocks(rows), 256, 0, s>>>(x, scale, bias, y, rows,
-                                                     cols, eps);
+  launch_pdl(layernorm_kernel, rows_blocks(rows), 256, 0, s, x, scale, bias, y, rows, cols, eps);
   return cudaGetLastError();
 }
 
@@ -610,7 +618,7 @@ cudaError_t softmax_rows(const half *x, half *y, int rows, int cols,
                          cudaStream_t s) {
   if (rows <= 0)
     return cudaSuccess;
-  softmax_kernel<<<rows_blocks(rows), 256, 0, s>>>(x, y, rows, cols);
+  launch_pdl(softmax_kernel, rows_blocks(rows), 256, 0, s, x, y, rows, cols);
   return cudaGetLastError();
 }
 
@@ -618,7 +626,7 @@ cudaError_t mean_rows(const half *x, half *y, int rows, int cols,
                       cudaStream_t s) {
   if (rows <= 0)
     return cudaSuccess;
-  mean_rows_kernel<<<rows_blocks(rows), 256, 0, s>>>(x, y, rows, cols);
+  launch_pdl(mean_rows_kernel, rows_blocks(rows), 256, 0, s, x, y, rows, cols);
   return cudaGetLastError();
 }
 
@@ -626,8 +634,7 @@ cudaError_t mean_nhwc(const half *x, half *y, int batch, int C, int spatial,
                       cudaStream_t s) {
   if (batch <= 0)
     return cudaSuccess;
-  mean_nhwc_kernel<<<dim3((C + 31) / 32, batch), 256, 0, s>>>(x, y, C,
-                                                               spatial);
+  launch_pdl(mean_nhwc_kernel, dim3((C + 31) / 32, batch), 256, 0, s, x, y, C, spatial);
   return cudaGetLastError();
 }
 
@@ -675,8 +682,8 @@ cudaError_t attention_simt(const half *qkv, half *out, int lines, int seq, int h
                                            static_cast<int>(smem));
       if (e != cudaSuccess)
         return e;
-      attention_f32_kernel<40><<<lines, threads, smem, s>>>(qkv, out, heads, dh, scale,
-                                                            FastDiv(dh), vec);
+      launch_pdl(attention_f32_kernel<40>, lines, threads, smem, s, qkv, out, heads, dh, scale,
+          FastDiv(dh), vec);
       return cudaGetLastError();
     }
   }
@@ -686,9 +693,8 @@ cudaError_t attention_simt(const half *qkv, half *out, int lines, int seq, int h
     const size_t smem = sizeof(half) * 3ull * heads * seq * 16;
     const int vec = (heads * dh) % 8 == 0 && (reinterpret_cast<uintptr_t>(qkv) & 15) == 0;
     if (smem <= 48 * 1024) {
-      attention_rows_kernel<64><<<lines, threads, smem, s>>>(
-          qkv, out, seq, heads, dh, scale, FastDiv(heads * dh), FastDiv(dh),
-          FastDiv(seq), vec);
+      launch_pdl(attention_rows_kernel<64>, lines, threads, smem, s, qkv, out, seq, heads, dh,
+          scale, FastDiv(heads * dh), FastDiv(dh), FastDiv(seq), vec);
       return cudaGetLastError();
     }
   }
@@ -704,7 +710,7 @@ cudaError_t attention_simt(const half *qkv, half *out, int lines, int seq, int h
           static_cast<int>(staged));
       if (e != cudaSuccess)
         return e;
-      kernel<<<lines, 256, staged, s>>>(qkv, out, seq, heads, dh, scale);
+      launch_pdl(kernel, lines, 256, staged, s, qkv, out, seq, heads, dh, scale);
       return cudaGetLastError();
     }
   }
@@ -719,7 +725,7 @@ cudaError_t attention_simt(const half *qkv, half *out, int lines, int seq, int h
       static_cast<int>(smem));
   if (e != cudaSuccess)
     return e;
-  attention_kernel<<<lines, 256, smem, s>>>(qkv, out, seq, heads, dh, scale);
+  launch_pdl(attention_kernel, lines, 256, smem, s, qkv, out, seq, heads, dh, scale);
   return cudaGetLastError();
 }
 

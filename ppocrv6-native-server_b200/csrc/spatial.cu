@@ -48,6 +48,7 @@ __global__ void __launch_bounds__(kBlock, 4)
                      int batch, int C, int H, int W, int OH, int OW, int PH,
                      int PW, int act, uint32_t total, FastDiv by_groups,
                      FastDiv by_tiles, FastDiv by_oh) {
+  pdl_begin();
   extern __shared__ uint4 dw_smem[];
   half *ws = reinterpret_cast<half *>(dw_smem);
   constexpr int TAPS = KH * KW;
@@ -143,6 +144,7 @@ __global__ void __launch_bounds__(kBlock)
                              half *__restrict__ y, int batch, int C, int H,
                              int W, int OH, int OW, int KH, int KW, int SH,
                              int SW, int PH, int PW, int act) {
+  pdl_begin();
   const int groups = C >> 3;
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(batch) * OH * OW * groups;
@@ -210,6 +212,7 @@ __global__ void __launch_bounds__(256)
                          const half *__restrict__ bias, half *__restrict__ y,
                          int C, int H, int OH, int OW, int PH, int PW, int CB,
                          int TW, int tiles_w, int chunks, int act, int *err) {
+  pdl_begin();
   constexpr int TAPS = KH * KW;
   constexpr int NCOL = (PIX - 1) * SW + KW;
   extern __shared__ __align__(128) uint8_t dwt_smem[];
@@ -358,9 +361,8 @@ cudaError_t launch_dw_tma(const half *x, const half *w, const half *bias,
   if (e != cudaSuccess)
     return e;
   *handled = true;
-  kernel<<<static_cast<unsigned>(blocks), 256, smem, s>>>(
-      map, w, bias, y, C, H, OH, OW, PH, PW, CB, TW, tiles_w, chunks, act,
-      device_error_word());
+  launch_pdl(kernel, static_cast<unsigned>(blocks), 256, smem, s, map, w, bias, y, C, H, OH, OW, PH,
+      PW, CB, TW, tiles_w, chunks, act, device_error_word());
   return cudaGetLastError();
 }
 
@@ -383,6 +385,7 @@ __global__ void __launch_bounds__(256)
                           int C, int H, int OH, int OW, int PH, int PW, int CB,
                           int TH, int TW, int tiles_h, int tiles_w, int chunks,
                           int act, int *err) {
+  pdl_begin();
   constexpr int TAPS = KH * KW;
   constexpr int NCOL = (PIX - 1) * SW + KW;
   extern __shared__ __align__(128) uint8_t dwt_smem[];
@@ -576,9 +579,8 @@ cudaError_t launch_dw_tile(const half *x, const half *w, const half *bias,
   if (e != cudaSuccess)
     return e;
   *handled = true;
-  kernel<<<static_cast<unsigned>(blocks), t.threads, t.smem, s>>>(
-      map, w, bias, y, C, H, OH, OW, PH, PW, t.CB, t.TH, t.TW, t.tiles_h,
-      t.tiles_w, chunks, act, device_error_word());
+  launch_pdl(kernel, static_cast<unsigned>(blocks), t.threads, t.smem, s, map, w, bias, y, C, H, OH,
+      OW, PH, PW, t.CB, t.TH, t.TW, t.tiles_h, t.tiles_w, chunks, act, device_error_word());
   return cudaGetLastError();
 }
 
@@ -610,9 +612,9 @@ cudaError_t launch_dw(const half *x, const half *w, const half *bias, half *y,
     if (e != cudaSuccess)
       return e;
   }
-  kernel<<<static_cast<unsigned>(blocks), kBlock, smem, s>>>(
-      x, w, bias, y, batch, C, H, W, OH, OW, PH, PW, act,
-      static_cast<uint32_t>(total), FastDiv(C / 8), FastDiv(tiles), FastDiv(OH));
+  launch_pdl(kernel, static_cast<unsigned>(blocks), kBlock, smem, s, x, w, bias, y, batch, C, H, W,
+      OH, OW, PH, PW, act, static_cast<uint32_t>(total), FastDiv(C / 8), FastDiv(tiles),
+      FastDiv(OH));
   return cudaGetLastError();
 }
 
@@ -625,6 +627,7 @@ __global__ void __launch_bounds__(kBlock)
                        int batch, int Ci, int H, int W, int Co, int OH, int OW,
                        int KH, int KW, int SH, int SW, int PH, int PW,
                        int act) {
+  pdl_begin();
   extern __shared__ float wsm[];
   const int wn = Co * KH * KW * Ci;
   for (int j = threadIdx.x; j < wn; j += blockDim.x)
@@ -687,6 +690,7 @@ __global__ void __launch_bounds__(kBlock)
                      int batch, int Ci, int H, int W, int OH, int OW, int KH,
                      int KW, int SH, int SW, int PH, int PW, int act,
                      uint32_t total, FastDiv by_ow, FastDiv by_oh) {
+  pdl_begin();
   extern __shared__ float wsm[];
   const int taps = KH * KW * Ci;
   for (int j = threadIdx.x; j < taps * CO; j += blockDim.x) {
@@ -759,6 +763,7 @@ __global__ void __launch_bounds__(kBlock)
                       int Ci, int H, int W, int OH, int OW, int KH, int KW,
                       int SH, int SW, int PH, int PW, int act, uint32_t items,
                       FastDiv by_pairs, FastDiv by_oh) {
+  pdl_begin();
   extern __shared__ float wsm[];
   const int taps = KH * KW * Ci;
   for (int j = threadIdx.x; j < taps * CO; j += blockDim.x) {
@@ -840,6 +845,7 @@ __global__ void __launch_bounds__(kBlock)
                          int batch, int C, int H, int W, int OH, int OW,
                          int KH, int KW, int SH, int SW, int PH, int PW,
                          bool maximum) {
+  pdl_begin();
   const int groups = C >> 3;
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(batch) * OH * OW * groups;
@@ -891,6 +897,7 @@ __global__ void __launch_bounds__(kBlock)
     pool_fixed_kernel(const half *__restrict__ x, half *__restrict__ y,
                       int batch, int C, int H, int W, int OH, int OW,
                       FastDiv by_groups, FastDiv by_ow, FastDiv by_oh) {
+  pdl_begin();
   const int groups = C >> 3;
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(batch) * OH * OW * groups;
@@ -949,6 +956,7 @@ __global__ void __launch_bounds__(kBlock)
                        long long total, int C, int H, int W, int OH, int OW,
                        int KH, int KW, int SH, int SW, int PH, int PW,
                        bool maximum, bool nhwc) {
+  pdl_begin();
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= total)
     return;
@@ -987,6 +995,7 @@ __global__ void __launch_bounds__(kBlock)
     pad_kernel(const half *__restrict__ x, half *__restrict__ y,
                long long total, int C, int H, int W, int OH, int OW, int PH,
                int PW, bool vec) {
+  pdl_begin();
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= total)
     return;
@@ -1016,6 +1025,7 @@ __global__ void __launch_bounds__(kBlock)
                        const half *__restrict__ addend, half *__restrict__ y,
                        long long total, int C, int H, int W, int OH, int OW,
                        float sh, float sw, bool vec) {
+  pdl_begin();
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= total)
     return;
@@ -1059,6 +1069,7 @@ __global__ void __launch_bounds__(kBlock)
 __global__ void __launch_bounds__(kBlock)
     upsample_concat_kernel(const __grid_constant__ UpcatArgs a, half *__restrict__ y,
                            uint32_t total, FastDiv by_groups, FastDiv by_ow, FastDiv by_oh) {
+  pdl_begin();
   // The source table goes to shared memory once per block: lanes of a warp
   // pick different sources, and lane-dependent indices into the parameter
   // block (or selecting through all of it per thread) stall on its loads.
@@ -1103,6 +1114,7 @@ __global__ void __launch_bounds__(kBlock)
     resize_nhwc_vec_kernel(const half *__restrict__ x, const half *__restrict__ addend,
                            half *__restrict__ y, uint32_t total, int C, int H, int W,
                            FastDiv by_groups, FastDiv by_ow, FastDiv by_oh, float sh, float sw) {
+  pdl_begin();
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total)
     return;
@@ -1133,6 +1145,7 @@ __global__ void __launch_bounds__(kBlock)
     resize_nchw_kernel(const half *__restrict__ x, half *__restrict__ y,
                        long long total, int H, int W, int OH, int OW, float sh,
                        float sw) {
+  pdl_begin();
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= total)
     return;
@@ -1149,6 +1162,7 @@ __global__ void __launch_bounds__(kBlock)
     concat_kernel(const half *__restrict__ a, const half *__restrict__ b,
                   half *__restrict__ y, long long total, int na, int nb,
                   bool vec) {
+  pdl_begin();
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= total)
     return;
@@ -1167,6 +1181,7 @@ __global__ void __launch_bounds__(kBlock)
 // ------------------------------------------------------------ transpose
 __global__ void transpose_kernel(const half *__restrict__ x,
                                  half *__restrict__ y, int rows, int cols) {
+  pdl_begin();
   __shared__ half tile[32][34];
   const long long base = static_cast<long long>(blockIdx.z) * rows * cols;
   int c = blockIdx.x * 32 + threadIdx.x;
@@ -1196,6 +1211,7 @@ __device__ __forceinline__ long long locate(long long i, const Gather &g) {
 __global__ void __launch_bounds__(kBlock)
     gather_kernel(const half *__restrict__ x, half *__restrict__ y,
                   long long n, Gather g) {
+  pdl_begin();
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < n)
     y[i] = x[locate(i, g)];
@@ -1213,6 +1229,7 @@ __global__ void __launch_bounds__(kBlock)
     binary_kernel(const half *__restrict__ a, const half *__restrict__ b,
                   half *__restrict__ y, long long n, Gather ga, Gather gb,
                   int op) {
+  pdl_begin();
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < n)
     y[i] = __float2half_rn(binop(__half2float(a[locate(i, ga)]),
@@ -1233,6 +1250,7 @@ __global__ void __launch_bounds__(kBlock)
     binary_flat_kernel(const half *__restrict__ a, const half *__restrict__ b,
                        half *__restrict__ y, long long n, int ad, int am,
                        int bd, int bm, int op) {
+  pdl_begin();
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < n)
     y[i] = __float2half_rn(binop(__half2float(a[flat(i, ad, am)]),
@@ -1242,6 +1260,7 @@ __global__ void __launch_bounds__(kBlock)
 __global__ void __launch_bounds__(kBlock)
     unary_kernel(const half *__restrict__ x, half *__restrict__ y, long long n,
                  int op, float alpha, float beta) {
+  pdl_begin();
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n)
     return;
@@ -1272,6 +1291,7 @@ __global__ void __launch_bounds__(kBlock)
 __global__ void __launch_bounds__(kBlock)
     copy_input_f32_kernel(const float *__restrict__ x, half *__restrict__ y,
                           size_t valid, size_t total) {
+  pdl_begin();
   size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < total)
     y[i] = i < valid ? __float2half_rn(x[i]) : __float2half_rn(0.f);
@@ -1281,6 +1301,7 @@ __global__ void __launch_bounds__(kBlock)
 __global__ void __launch_bounds__(kBlock)
     copy_input_nhwc_kernel(const half *__restrict__ x, half *__restrict__ y,
                            int valid, long long total, int C, int H, int W) {
+  pdl_begin();
   long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= total)
     return;
@@ -1294,6 +1315,7 @@ __global__ void __launch_bounds__(kBlock)
 __global__ void __launch_bounds__(kBlock)
     half_to_float_kernel(const half *__restrict__ x, float *__restrict__ y,
                          size_t n) {
+  pdl_begin();
   size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < n)
     y[i] = __half2float(x[i]);
@@ -1304,6 +1326,7 @@ __global__ void __launch_bounds__(kBlock)
 __global__ void __launch_bounds__(kBlock)
     nchw_to_nhwc_kernel(const float *__restrict__ x, half *__restrict__ y,
                         int valid, long long pixels, int C, int HW) {
+  pdl_begin();
   long long p = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (p >= pixels)
     return;
@@ -1329,8 +1352,7 @@ cudaError_t nchw_f32_to_nhwc_f16(const float *x, half *y, int valid, int batch,
   const long long pixels = static_cast<long long>(batch) * H * W;
   if (pixels <= 0)
     return cudaSuccess;
-  nchw_to_nhwc_kernel<<<blocks_for(pixels), kBlock, 0, s>>>(x, y, valid, pixels,
-                                                             C, H * W);
+  launch_pdl(nchw_to_nhwc_kernel, blocks_for(pixels), kBlock, 0, s, x, y, valid, pixels, C, H * W);
   return cudaGetLastError();
 }
 
@@ -1366,8 +1388,8 @@ cudaError_t depthwise(const half *x, const half *w, const half *bias, half *y,
   PB2_DW(9, 9, 1, 1)
 #undef PB2_DW
   const long long total = static_cast<long long>(batch) * OH * OW * (C / 8);
-  depthwise_generic_kernel<<<blocks_for(total), kBlock, 0, s>>>(
-      x, w, bias, y, batch, C, H, W, OH, OW, KH, KW, SH, SW, PH, PW, act);
+  launch_pdl(depthwise_generic_kernel, blocks_for(total), kBlock, 0, s, x, w, bias, y, batch, C, H,
+      W, OH, OW, KH, KW, SH, SW, PH, PW, act);
   return cudaGetLastError();
 }
 
@@ -1383,6 +1405,7 @@ __global__ void __launch_bounds__(kBlock)
     space_to_depth2_kernel(const half *__restrict__ x, uint4 *__restrict__ y,
                            int Ci, int H, int W, int H2, int W2, uint32_t total,
                            FastDiv by_w2, FastDiv by_h2) {
+  pdl_begin();
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total)
     return;
@@ -1408,6 +1431,7 @@ __global__ void __launch_bounds__(kBlock)
 __global__ void __launch_bounds__(kBlock)
     stem_s2d_pack_kernel(const half *__restrict__ w, half *__restrict__ wp,
                          int Co, int Ci) {
+  pdl_begin();
   // wp [Co][2][2][16] from w [Co][3][3][Ci] (OHWI)
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= Co * 64)
@@ -1428,8 +1452,8 @@ cudaError_t stem_s2d_pack(const half *w, half *wp, int Co, int Ci,
                           cudaStream_t s) {
   if (Co <= 0 || Ci <= 0 || Ci > 4)
     return cudaErrorInvalidValue;
-  stem_s2d_pack_kernel<<<blocks_for(static_cast<long long>(Co) * 64), kBlock, 0, s>>>(
-      w, wp, Co, Ci);
+  launch_pdl(stem_s2d_pack_kernel, blocks_for(static_cast<long long>(Co) * 64), kBlock, 0, s, w, wp,
+      Co, Ci);
   return cudaGetLastError();
 }
 
@@ -1448,9 +1472,9 @@ cudaError_t stem_conv_s2d(const half *x, const half *wp, const half *bias,
   const long long total = static_cast<long long>(batch) * H2 * W2;
   if (total >= (1LL << 31))
     return cudaErrorInvalidValue;
-  space_to_depth2_kernel<<<blocks_for(total), kBlock, 0, s>>>(
-      x, reinterpret_cast<uint4 *>(scratch), Ci, H, W, H2, W2,
-      static_cast<uint32_t>(total), FastDiv(W2), FastDiv(H2));
+  launch_pdl(space_to_depth2_kernel, blocks_for(total), kBlock, 0, s, x,
+      reinterpret_cast<uint4 *>(scratch), Ci, H, W, H2, W2, static_cast<uint32_t>(total),
+      FastDiv(W2), FastDiv(H2));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
     return e;
@@ -1487,9 +1511,9 @@ cudaError_t direct_conv(const half *x, const half *w, const half *bias,
     const int per_row = (OW + 1) / 2;
 #define PB2_STEM2(co)                                                          \
   if (Co == co) {                                                              \
-    (act == kActRelu ? stem_conv2_kernel<co, kActRelu>                         \
-                     : stem_conv2_kernel<co, -1>)<<<blocks_for(pairs), kBlock, \
-                                                    smem, s>>>(                \
+    launch_pdl(act == kActRelu ? stem_conv2_kernel<co, kActRelu>               \
+                               : stem_conv2_kernel<co, -1>,                    \
+               blocks_for(pairs), kBlock, smem, s,                             \
         x, w, bias, y, Ci, H, W, OH, OW, KH, KW, SH, SW, PH, PW, act,          \
         static_cast<uint32_t>(pairs), FastDiv(per_row), FastDiv(OH));          \
     return cudaGetLastError();                                                 \
@@ -1503,9 +1527,9 @@ cudaError_t direct_conv(const half *x, const half *w, const half *bias,
       pixels < (1LL << 31)) {
 #define PB2_STEM(co)                                                           \
   if (Co == co) {                                                              \
-    (act == kActRelu ? stem_conv_kernel<co, kActRelu>                          \
-                     : stem_conv_kernel<co, -1>)<<<blocks_for(pixels), kBlock, \
-                                                   smem, s>>>(                 \
+    launch_pdl(act == kActRelu ? stem_conv_kernel<co, kActRelu>                \
+                               : stem_conv_kernel<co, -1>,                     \
+               blocks_for(pixels), kBlock, smem, s,                            \
         x, w, bias, y, batch, Ci, H, W, OH, OW, KH, KW, SH, SW, PH, PW, act,   \
         static_cast<uint32_t>(pixels), FastDiv(OW), FastDiv(OH));              \
     return cudaGetLastError();                                                 \
@@ -1517,8 +1541,8 @@ cudaError_t direct_conv(const half *x, const half *w, const half *bias,
 #undef PB2_STEM
   }
   const long long total = static_cast<long long>(batch) * OH * OW * (Co / 8);
-  direct_conv_kernel<<<blocks_for(total), kBlock, smem, s>>>(
-      x, w, bias, y, batch, Ci, H, W, Co, OH, OW, KH, KW, SH, SW, PH, PW, act);
+  launch_pdl(direct_conv_kernel, blocks_for(total), kBlock, smem, s, x, w, bias, y, batch, Ci, H, W,
+      Co, OH, OW, KH, KW, SH, SW, PH, PW, act);
   return cudaGetLastError();
 }
 
@@ -1529,26 +1553,26 @@ cudaError_t pool_nhwc(const half *x, half *y, int batch, int C, int H, int W,
       (OH - 1) * SH + KH <= H && (OW - 1) * SW + KW <= W) {
     const long long total = static_cast<long long>(batch) * OH * OW * (C / 8);
     if (!maximum && KH == 3 && KW == 2 && SH == 3 && SW == 2) {
-      pool_fixed_kernel<3, 2, 3, 2, false><<<blocks_for(total), kBlock, 0, s>>>(
-          x, y, batch, C, H, W, OH, OW, FastDiv(static_cast<uint32_t>(C / 8)),
+      launch_pdl(pool_fixed_kernel<3, 2, 3, 2, false>, blocks_for(total), kBlock, 0, s, x, y, batch,
+          C, H, W, OH, OW, FastDiv(static_cast<uint32_t>(C / 8)),
           FastDiv(static_cast<uint32_t>(OW)), FastDiv(static_cast<uint32_t>(OH)));
       return cudaGetLastError();
     }
     if (maximum && KH == 2 && KW == 2 && SH == 1 && SW == 1) {
-      pool_fixed_kernel<2, 2, 1, 1, true><<<blocks_for(total), kBlock, 0, s>>>(
-          x, y, batch, C, H, W, OH, OW, FastDiv(static_cast<uint32_t>(C / 8)),
+      launch_pdl(pool_fixed_kernel<2, 2, 1, 1, true>, blocks_for(total), kBlock, 0, s, x, y, batch,
+          C, H, W, OH, OW, FastDiv(static_cast<uint32_t>(C / 8)),
           FastDiv(static_cast<uint32_t>(OW)), FastDiv(static_cast<uint32_t>(OH)));
       return cudaGetLastError();
     }
   }
   if (C % 8 == 0 && al16(x) && al16(y)) {
     const long long total = static_cast<long long>(batch) * OH * OW * (C / 8);
-    pool_nhwc_vec_kernel<<<blocks_for(total), kBlock, 0, s>>>(
-        x, y, batch, C, H, W, OH, OW, KH, KW, SH, SW, PH, PW, maximum);
+    launch_pdl(pool_nhwc_vec_kernel, blocks_for(total), kBlock, 0, s, x, y, batch, C, H, W, OH, OW,
+        KH, KW, SH, SW, PH, PW, maximum);
   } else {
     const long long total = static_cast<long long>(batch) * OH * OW * C;
-    pool_scalar_kernel<<<blocks_for(total), kBlock, 0, s>>>(
-        x, y, total, C, H, W, OH, OW, KH, KW, SH, SW, PH, PW, maximum, true);
+    launch_pdl(pool_scalar_kernel, blocks_for(total), kBlock, 0, s, x, y, total, C, H, W, OH, OW,
+        KH, KW, SH, SW, PH, PW, maximum, true);
   }
   return cudaGetLastError();
 }
@@ -1557,8 +1581,8 @@ cudaError_t pool_nchw(const half *x, half *y, int planes, int H, int W, int OH,
                       int OW, int KH, int KW, int SH, int SW, int PH, int PW,
                       bool maximum, cudaStream_t s) {
   const long long total = static_cast<long long>(planes) * OH * OW;
-  pool_scalar_kernel<<<blocks_for(total), kBlock, 0, s>>>(
-      x, y, total, 1, H, W, OH, OW, KH, KW, SH, SW, PH, PW, maximum, false);
+  launch_pdl(pool_scalar_kernel, blocks_for(total), kBlock, 0, s, x, y, total, 1, H, W, OH, OW, KH,
+      KW, SH, SW, PH, PW, maximum, false);
   return cudaGetLastError();
 }
 
@@ -1567,16 +1591,15 @@ cudaError_t pad_nhwc(const half *x, half *y, int batch, int C, int H, int W,
   const bool vec = C % 8 == 0 && al16(x) && al16(y);
   const long long total =
       static_cast<long long>(batch) * OH * OW * (vec ? C / 8 : C);
-  pad_kernel<<<blocks_for(total), kBlock, 0, s>>>(x, y, total, C, H, W, OH, OW,
-                                                   PH, PW, vec);
+  launch_pdl(pad_kernel, blocks_for(total), kBlock, 0, s, x, y, total, C, H, W, OH, OW, PH, PW, vec);
   return cudaGetLastError();
 }
 
 cudaError_t pad_nchw(const half *x, half *y, int planes, int H, int W, int OH,
                      int OW, int PH, int PW, cudaStream_t s) {
   const long long total = static_cast<long long>(planes) * OH * OW;
-  pad_kernel<<<blocks_for(total), kBlock, 0, s>>>(x, y, total, 1, H, W, OH, OW,
-                                                   PH, PW, false);
+  launch_pdl(pad_kernel, blocks_for(total), kBlock, 0, s, x, y, total, 1, H, W, OH, OW, PH, PW,
+      false);
   return cudaGetLastError();
 }
 
@@ -1588,14 +1611,13 @@ cudaError_t resize_nearest_nhwc(const half *x, const half *addend, half *y,
   const long long total =
       static_cast<long long>(batch) * OH * OW * (vec ? C / 8 : C);
   if (vec && total < (1LL << 31)) {
-    resize_nhwc_vec_kernel<<<blocks_for(total), kBlock, 0, s>>>(
-        x, addend, y, static_cast<uint32_t>(total), C, H, W,
-        FastDiv(static_cast<uint32_t>(C / 8)), FastDiv(static_cast<uint32_t>(OW)),
-        FastDiv(static_cast<uint32_t>(OH)), sh, sw);
+    launch_pdl(resize_nhwc_vec_kernel, blocks_for(total), kBlock, 0, s, x, addend, y,
+        static_cast<uint32_t>(total), C, H, W, FastDiv(static_cast<uint32_t>(C / 8)),
+        FastDiv(static_cast<uint32_t>(OW)), FastDiv(static_cast<uint32_t>(OH)), sh, sw);
     return cudaGetLastError();
   }
-  resize_nhwc_kernel<<<blocks_for(total), kBlock, 0, s>>>(
-      x, addend, y, total, C, H, W, OH, OW, sh, sw, vec);
+  launch_pdl(resize_nhwc_kernel, blocks_for(total), kBlock, 0, s, x, addend, y, total, C, H, W, OH,
+      OW, sh, sw, vec);
   return cudaGetLastError();
 }
 
@@ -1615,8 +1637,8 @@ cudaError_t upsample_concat_nhwc(const UpcatArgs &a, half *y, int batch, int OH,
   const long long total = static_cast<long long>(batch) * OH * OW * (ctot / 8);
   if (total >= (1LL << 31))
     return cudaErrorInvalidValue;
-  upsample_concat_kernel<<<blocks_for(total), kBlock, 0, s>>>(
-      a, y, static_cast<uint32_t>(total), FastDiv(static_cast<uint32_t>(ctot / 8)),
+  launch_pdl(upsample_concat_kernel, blocks_for(total), kBlock, 0, s, a, y,
+      static_cast<uint32_t>(total), FastDiv(static_cast<uint32_t>(ctot / 8)),
       FastDiv(static_cast<uint32_t>(OW)), FastDiv(static_cast<uint32_t>(OH)));
   return cudaGetLastError();
 }
@@ -1625,8 +1647,7 @@ cudaError_t resize_nearest_nchw(const half *x, half *y, int planes, int H,
                                 int W, int OH, int OW, float sh, float sw,
                                 cudaStream_t s) {
   const long long total = static_cast<long long>(planes) * OH * OW;
-  resize_nchw_kernel<<<blocks_for(total), kBlock, 0, s>>>(x, y, total, H, W,
-                                                           OH, OW, sh, sw);
+  launch_pdl(resize_nchw_kernel, blocks_for(total), kBlock, 0, s, x, y, total, H, W, OH, OW, sh, sw);
   return cudaGetLastError();
 }
 
@@ -1635,8 +1656,7 @@ cudaError_t concat_rows(const half *a, const half *b, half *y, long long rows,
   const bool vec = na % 8 == 0 && nb % 8 == 0 && al16(a) && al16(b) && al16(y);
   const int wa = vec ? na / 8 : na, wb = vec ? nb / 8 : nb;
   const long long total = rows * (wa + wb);
-  concat_kernel<<<blocks_for(total), kBlock, 0, s>>>(a, b, y, total, wa, wb,
-                                                      vec);
+  launch_pdl(concat_kernel, blocks_for(total), kBlock, 0, s, a, b, y, total, wa, wb, vec);
   return cudaGetLastError();
 }
 
@@ -1645,7 +1665,7 @@ cudaError_t transpose2d(const half *x, half *y, int batch, int rows, int cols,
   if (batch <= 0 || rows <= 0 || cols <= 0)
     return cudaSuccess;
   dim3 grid((cols + 31) / 32, (rows + 31) / 32, batch);
-  transpose_kernel<<<grid, dim3(32, 8), 0, s>>>(x, y, rows, cols);
+  launch_pdl(transpose_kernel, grid, dim3(32, 8), 0, s, x, y, rows, cols);
   return cudaGetLastError();
 }
 
@@ -1653,7 +1673,7 @@ cudaError_t gather(const half *x, half *y, long long n, const Gather &g,
                    cudaStream_t s) {
   if (n <= 0)
     return cudaSuccess;
-  gather_kernel<<<blocks_for(n), kBlock, 0, s>>>(x, y, n, g);
+  launch_pdl(gather_kernel, blocks_for(n), kBlock, 0, s, x, y, n, g);
   return cudaGetLastError();
 }
 
@@ -1662,7 +1682,7 @@ cudaError_t binary(const half *a, const half *b, half *y, long long n,
                    cudaStream_t s) {
   if (n <= 0)
     return cudaSuccess;
-  binary_kernel<<<blocks_for(n), kBlock, 0, s>>>(a, b, y, n, ga, gb, op);
+  launch_pdl(binary_kernel, blocks_for(n), kBlock, 0, s, a, b, y, n, ga, gb, op);
   return cudaGetLastError();
 }
 
@@ -1671,8 +1691,7 @@ cudaError_t binary_flat(const half *a, const half *b, half *y, long long n,
                         cudaStream_t s) {
   if (n <= 0)
     return cudaSuccess;
-  binary_flat_kernel<<<blocks_for(n), kBlock, 0, s>>>(a, b, y, n, ad, am, bd,
-                                                       bm, op);
+  launch_pdl(binary_flat_kernel, blocks_for(n), kBlock, 0, s, a, b, y, n, ad, am, bd, bm, op);
   return cudaGetLastError();
 }
 
@@ -1680,7 +1699,7 @@ cudaError_t unary(const half *x, half *y, long long n, int op, float alpha,
                   float beta, cudaStream_t s) {
   if (n <= 0)
     return cudaSuccess;
-  unary_kernel<<<blocks_for(n), kBlock, 0, s>>>(x, y, n, op, alpha, beta);
+  launch_pdl(unary_kernel, blocks_for(n), kBlock, 0, s, x, y, n, op, alpha, beta);
   return cudaGetLastError();
 }
 
@@ -1688,8 +1707,8 @@ cudaError_t copy_input_f32(const float *x, half *y, size_t valid, size_t total,
                            cudaStream_t s) {
   if (!total)
     return cudaSuccess;
-  copy_input_f32_kernel<<<blocks_for(static_cast<long long>(total)), kBlock, 0,
-                          s>>>(x, y, valid, total);
+  launch_pdl(copy_input_f32_kernel, blocks_for(static_cast<long long>(total)), kBlock, 0, s, x, y,
+      valid, total);
   return cudaGetLastError();
 }
 
@@ -1698,16 +1717,99 @@ cudaError_t copy_input_nhwc_f16(const half *x, half *y, int valid, int batch,
   const long long total = static_cast<long long>(batch) * C * H * W;
   if (total <= 0)
     return cudaSuccess;
-  copy_input_nhwc_kernel<<<blocks_for(total), kBlock, 0, s>>>(x, y, valid,
-                                                              total, C, H, W);
+  if (C == 1 || static_cast<long long>(H) * W == 1) {
+    // One channel (or one pixel): NHWC and NCHW are the same layout, so the
+    // valid images are one contiguous copy and the rest is zero.
+    const size_t image = static_cast<size_t>(C) * H * W * sizeof(half);
+    return stage_bytes(x, y, image * valid, image * batch, s);
+  }
+  launch_pdl(copy_input_nhwc_kernel, blocks_for(total), kBlock, 0, s, x, y, valid, total, C, H, W);
   return cudaGetLastError();
+}
+
+namespace {
+
+__global__ void __launch_bounds__(kBlock)
+    stage_bytes_kernel(const uint4 *__restrict__ x, uint4 *__restrict__ y, size_t valid16,
+                       size_t total16) {
+  pdl_begin();
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total16;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    y[i] = i < valid16 ? __ldg(x + i) : make_uint4(0, 0, 0, 0);
+}
+
+// Thread = 8 consecutive values (n % 8 == 0, 16-byte aligned) or one value.
+template <bool VEC, bool F32>
+__global__ void __launch_bounds__(kBlock)
+    output_copy_kernel(const half *__restrict__ x, void *__restrict__ y, size_t n,
+                       const int *__restrict__ err, int *__restrict__ err_host) {
+  pdl_begin();
+  if (blockIdx.x == 0 && threadIdx.x == 0 && err_host)
+    *reinterpret_cast<volatile int *>(err_host) = *reinterpret_cast<const volatile int *>(err);
+  const size_t step = static_cast<size_t>(gridDim.x) * blockDim.x;
+  if constexpr (VEC) {
+    const uint4 *xv = reinterpret_cast<const uint4 *>(x);
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n / 8; i += step) {
+      Pack8 p;
+      p.u = __ldg(xv + i);
+      if constexpr (F32) {
+        float4 *yv = reinterpret_cast<float4 *>(y) + 2 * i;
+        const float2 a = __half22float2(p.h[0]), b = __half22float2(p.h[1]);
+        const float2 c = __half22float2(p.h[2]), d = __half22float2(p.h[3]);
+        yv[0] = make_float4(a.x, a.y, b.x, b.y);
+        yv[1] = make_float4(c.x, c.y, d.x, d.y);
+      } else {
+        reinterpret_cast<uint4 *>(y)[i] = p.u;
+      }
+    }
+  } else {
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += step) {
+      if constexpr (F32)
+        reinterpret_cast<float *>(y)[i] = __half2float(x[i]);
+      else
+        reinterpret_cast<half *>(y)[i] = x[i];
+    }
+  }
+}
+
+// Grid-stride launches: a few CTAs per SM cover any size.
+unsigned stride_blocks(size_t items) {
+  const size_t cap = static_cast<size_t>(sm_count()) * 8;
+  const size_t b = (items + kBlock - 1) / kBlock;
+  return static_cast<unsigned>(b < 1 ? 1 : b > cap ? cap : b);
+}
+
+} // namespace
+
+cudaError_t stage_bytes(const void *x, void *y, size_t valid, size_t total, cudaStream_t s) {
+  if (!total)
+    return cudaSuccess;
+  if (valid > total)
+    return cudaErrorInvalidValue;
+  if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | valid | total) & 15) == 0)
+    return launch_pdl(stage_bytes_kernel, stride_blocks(total / 16), kBlock, 0, s,
+                      static_cast<const uint4 *>(x), static_cast<uint4 *>(y), valid / 16, total / 16);
+  cudaError_t e = valid ? cudaMemcpyAsync(y, x, valid, cudaMemcpyDeviceToDevice, s) : cudaSuccess;
+  if (e == cudaSuccess && valid < total)
+    e = cudaMemsetAsync(static_cast<char *>(y) + valid, 0, total - valid, s);
+  return e;
+}
+
+cudaError_t output_copy(const half *x, void *y, size_t n, bool to_f32, const int *err, int *err_host,
+                        cudaStream_t s) {
+  const bool vec = n % 8 == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  const unsigned blocks = stride_blocks(vec ? n / 8 : n);
+  if (vec)
+    return to_f32 ? launch_pdl(output_copy_kernel<true, true>, blocks, kBlock, 0, s, x, y, n, err, err_host)
+                  : launch_pdl(output_copy_kernel<true, false>, blocks, kBlock, 0, s, x, y, n, err, err_host);
+  return to_f32 ? launch_pdl(output_copy_kernel<false, true>, blocks, kBlock, 0, s, x, y, n, err, err_host)
+                : launch_pdl(output_copy_kernel<false, false>, blocks, kBlock, 0, s, x, y, n, err, err_host);
 }
 
 cudaError_t half_to_float(const half *x, float *y, size_t n, cudaStream_t s) {
   if (!n)
     return cudaSuccess;
-  half_to_float_kernel<<<blocks_for(static_cast<long long>(n)), kBlock, 0, s>>>(
-      x, y, n);
+  launch_pdl(half_to_float_kernel, blocks_for(static_cast<long long>(n)), kBlock, 0, s, x, y, n);
   return cudaGetLastError();
 }
 

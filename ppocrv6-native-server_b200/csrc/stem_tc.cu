@@ -111,6 +111,7 @@ __global__ void __launch_bounds__(kStemThreads, 1) stem_tc_kernel(const __grid_c
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_launch_dependents();
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&ifull[i], 1);
@@ -126,6 +127,8 @@ __global__ void __launch_bounds__(kStemThreads, 1) stem_tc_kernel(const __grid_c
     *abort = 0;
     fence_barrier_init();
   }
+  // First global-memory access below (programmatic dependent launch).
+  pdl_wait();
   // Filter [CO][27] -> 4 planes of [CO][8] halves (columns 27..31 zero).
   for (int i = threadIdx.x; i < CO * kStemK; i += blockDim.x) {
     const int n = i / kStemK, k = i - n * kStemK;
@@ -383,7 +386,7 @@ cudaError_t launch_stem(const StemArgs &g, size_t smem, cudaStream_t s) {
   if (attr != cudaSuccess)
     return attr;
   const int grid = g.units < sm_count() ? g.units : sm_count();
-  kernel<<<grid, kStemThreads, smem, s>>>(g);
+  launch_pdl(kernel, grid, kStemThreads, smem, s, g);
   return cudaGetLastError();
 }
 

@@ -199,6 +199,7 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int total = g.mt * g.nt;
+  pdl_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -223,6 +224,8 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Nothing above touches global memory (programmatic dependent launch).
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -722,8 +725,7 @@ cudaError_t launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap
     return attr;
   const int total = g.mt * g.nt;
   const int grid = total < sm_count() ? total : sm_count();
-  kernel<<<grid, threads_for<EPI, MH>(), C::SMEM, stream>>>(a, b, c, g);
-  return cudaGetLastError();
+  return launch_pdl(kernel, grid, threads_for<EPI, MH>(), C::SMEM, stream, a, b, c, g);
 }
 
 // Picks the UMMA N tile that pads the column count least (ties: larger).

@@ -193,6 +193,87 @@ class LineStream:
                 scores[:n].copy_(rec.out_score[:n], non_blocking=True)
 
 
+class ModelStream:
+    """Host batches in, host outputs out, for any compiled model, with both
+    copies off the model's critical path: the host->device copy of batch k+1
+    runs on one copy stream and the device->host copy of batch k-1 on
+    another while the model works on batch k.
+
+    Two device input buffers and two device output buffers alternate. A copy
+    into an input buffer waits for the forward that last read it; a forward
+    into an output buffer waits for the device->host copy that last read it.
+    The reference's workers copy, enqueue and read back on one stream
+    (recognition_worker.cpp:700-746), so the three take turns; LineStream
+    overlaps only the input copy (the recognizer's outputs are small).
+    """
+
+    def __init__(self, model: CompiledModel, stream: torch.cuda.Stream | None = None):
+        self.model = model
+        dev = model.device
+        with torch.cuda.device(dev):
+            self.stream = stream if stream is not None else torch.cuda.Stream(dev)
+            self.h2d = torch.cuda.Stream(dev)
+            self.d2h = torch.cuda.Stream(dev)
+            self.out = [model.output_tensor() for _ in range(2)]
+            self.copied, self.consumed, self.produced, self.drained = (
+                [torch.cuda.Event() for _ in range(2)] for _ in range(4))
+        self.stage: list[torch.Tensor | None] = [None, None]
+        self._in_used = [False, False]
+        self._out_used = [False, False]
+
+    def _stage(self, s: int, host: torch.Tensor) -> torch.Tensor:
+        buf = self.stage[s]
+        if buf is None or buf.shape[1:] != host.shape[1:] or buf.dtype != host.dtype or buf.shape[0] < host.shape[0]:
+            if self._in_used[s]:
+                self.consumed[s].synchronize()
+            buf = torch.empty((self.model.input_shape[0],) + tuple(host.shape[1:]), dtype=host.dtype,
+                              device=self.model.device)
+            self.stage[s] = buf
+        return buf
+
+    def enqueue(self, batches, outputs) -> None:
+        """Asynchronous. batches[k]: pinned FP16 NHWC host tensor of n_k <=
+        the compiled batch images; outputs[k]: pinned host tensor receiving
+        the first n_k output rows. Work starts after everything already
+        queued on `self.stream`; join() orders a stream after the last
+        device->host copy."""
+        if len(batches) != len(outputs):
+            raise ValueError("one output per batch")
+        self.h2d.wait_stream(self.stream)
+
+        def copy_in(k: int) -> None:
+            s = k % 2
+            buf = self._stage(s, batches[k])
+            if self._in_used[s]:
+                self.h2d.wait_event(self.consumed[s])
+            with torch.cuda.stream(self.h2d):
+                buf[: batches[k].shape[0]].copy_(batches[k], non_blocking=True)
+                self.copied[s].record(self.h2d)
+
+        if batches:
+            copy_in(0)
+        for k, host in enumerate(batches):
+            s = k % 2
+            if k + 1 < len(batches):
+                copy_in(k + 1)
+            n = host.shape[0]
+            self.stream.wait_event(self.copied[s])
+            if self._out_used[s]:
+                self.stream.wait_event(self.drained[s])
+            self.model.enqueue_nhwc(self.stage[s][:n], self.out[s], self.stream)
+            self.consumed[s].record(self.stream)
+            self.produced[s].record(self.stream)
+            self._in_used[s] = self._out_used[s] = True
+            self.d2h.wait_event(self.produced[s])
+            with torch.cuda.stream(self.d2h):
+                outputs[k][:n].copy_(self.out[s][:n], non_blocking=True)
+                self.drained[s].record(self.d2h)
+
+    def join(self, stream: torch.cuda.Stream) -> None:
+        """Orders `stream` after every copy enqueued so far."""
+        stream.wait_stream(self.d2h)
+
+
 class PagePipeline:
     """Full-page path on one GPU: detector graph -> DB binarize -> recognizer
     over the page's line crops -> fused head -> device collapse, all on one

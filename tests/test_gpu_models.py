@@ -194,3 +194,33 @@ def test_line_stream_matches_serial(cuda):
             assert np.all(lens[n:].numpy() == -1)
     finally:
         rec.close()
+
+
+def test_model_stream_matches_serial(cuda):
+    """ModelStream (input copy of batch k+1 and output copy of batch k-1 on
+    their own streams while batch k runs) returns every batch's output, short
+    batches included, exactly as a serial copy + enqueue + read back."""
+    from ppocr_b200 import pipeline
+
+    model = pipeline.CompiledModel("neck_b256", cuda)
+    try:
+        sizes = [256, 100, 256, 7, 256]
+        batches = [torch.from_numpy(rng(80 + k).standard_normal((n, 1, 40, 120)).astype(np.float16)).pin_memory()
+                   for k, n in enumerate(sizes)]
+        stream = torch.cuda.Stream(cuda)
+        want = []
+        out = model.output_tensor()
+        for b in batches:
+            model.enqueue_nhwc(b.to(cuda), out, stream)
+            stream.synchronize()
+            want.append(out[: b.shape[0]].cpu().clone())
+        outs = [torch.full(tuple(out.shape), -1.0, dtype=out.dtype).pin_memory() for _ in sizes]
+        ms = pipeline.ModelStream(model, stream)
+        ms.enqueue(batches, outs)
+        ms.join(stream)
+        stream.synchronize()
+        for got, w, n in zip(outs, want, sizes):
+            assert torch.equal(got[:n], w)
+            assert torch.all(got[n:] == -1)
+    finally:
+        model.close()
