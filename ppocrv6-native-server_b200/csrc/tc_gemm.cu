@@ -111,56 +111,86 @@ template <int BN, int MH = 1> struct Cfg {
 };
 
 // Bias and residual of 8 consecutive columns [n0, n0+8) of one output row,
-// fetched ahead of the accumulator they are added to. Columns at or past N
-// and rows without an output row (orow < 0) fetch nothing; their values are
-// never stored.
+// fetched ahead of the accumulator they are added to, without branches: an
+// absent bias or residual (and a row without an output row) reads eight
+// fp16 -0, the exact identity of fp16 and fp32 addition (x + -0 = x for
+// every x, +0 included); columns at or past N read an in-range column
+// instead (their values are never stored).
 struct Extra8 {
   uint4 bias, res;
 };
 
+__device__ const uint4 kNegZeroHalves = {0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u};
+
 __device__ __forceinline__ Extra8 fetch_extra8(const GemmEpilogue &e, int n0, int N, long long orow) {
-  Extra8 x{make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-  const bool col_ok = n0 + 8 <= N;
-  if (e.bias && col_ok)
-    x.bias = __ldg(reinterpret_cast<const uint4 *>(e.bias + n0));
-  if (e.residual && col_ok && orow >= 0)
-    x.res = __ldg(reinterpret_cast<const uint4 *>(e.residual + orow * e.ldr + n0));
-  return x;
+  const int nc = n0 + 8 <= N ? n0 : N - 8;
+  const uint4 *bp = e.bias ? reinterpret_cast<const uint4 *>(e.bias + nc) : &kNegZeroHalves;
+  const uint4 *rp = e.residual && orow >= 0
+                        ? reinterpret_cast<const uint4 *>(e.residual + orow * e.ldr + nc)
+                        : &kNegZeroHalves;
+  return Extra8{__ldg(bp), __ldg(rp)};
 }
 
 // Fused epilogue for 8 consecutive columns of one accumulator row:
 // v = round(acc) + bias; v = round(v) + residual; y = round(act(v)).
+//
+// With no activation or ReLU the chain runs in packed fp16 (one conversion,
+// then HADD2 / HMAX2 per pair) and gives the same bits as the fp32 formula,
+// because rounding the fp32 sum of two fp16 values to fp16 equals rounding
+// their exact sum: when their exponents differ by at most 13 the fp32 sum is
+// exact, except for a carry out of a 13-apart pair, whose fp32 rounding
+// cannot land on an fp16 midpoint; further apart, the smaller operand is
+// below an eighth of the larger one's fp16 ulp and both roundings return the
+// larger operand (checked exhaustively over all pairs of finite fp16
+// values). ReLU commutes with the final rounding. The other activations act
+// on the unrounded fp32 sum and keep the fp32 formula.
 template <int ACT>
 __device__ __forceinline__ uint4 epilogue8(const uint32_t *acc, const GemmEpilogue &e, const Extra8 &x) {
-  float v[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j)
-    v[j] = round_half(__uint_as_float(acc[j]));
-  if (e.bias) {
+  if constexpr (ACT == kActNone || ACT == kActRelu) {
+    uint4 o;
+    half2 *h = reinterpret_cast<half2 *>(&o);
     const half2 *bh = reinterpret_cast<const half2 *>(&x.bias);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float2 f = __half22float2(bh[j]);
-      v[2 * j] += f.x;
-      v[2 * j + 1] += f.y;
-    }
-  }
-  if (e.residual) {
     const half2 *rh = reinterpret_cast<const half2 *>(&x.res);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float2 f = __half22float2(rh[j]);
-      v[2 * j] = round_half(v[2 * j]) + f.x;
-      v[2 * j + 1] = round_half(v[2 * j + 1]) + f.y;
+      // Absent operands are -0 (fetch_extra8): both additions always run.
+      h[j] = __float22half2_rn(make_float2(__uint_as_float(acc[2 * j]), __uint_as_float(acc[2 * j + 1])));
+      h[j] = __hadd2(__hadd2(h[j], bh[j]), rh[j]);
+      if constexpr (ACT == kActRelu)
+        h[j] = __hmax2(h[j], __float2half2_rn(0.f));
     }
-  }
-  uint4 o;
-  half2 *oh2 = reinterpret_cast<half2 *>(&o);
+    return o;
+  } else {
+    float v[8];
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
-    oh2[j] = __floats2half2_rn(act_t<ACT>(v[2 * j], e.act),
-                               act_t<ACT>(v[2 * j + 1], e.act));
-  return o;
+    for (int j = 0; j < 8; ++j)
+      v[j] = round_half(__uint_as_float(acc[j]));
+    {
+      const half2 *bh = reinterpret_cast<const half2 *>(&x.bias); // -0 when absent
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __half22float2(bh[j]);
+        v[2 * j] += f.x;
+        v[2 * j + 1] += f.y;
+      }
+    }
+    if (e.residual) {
+      const half2 *rh = reinterpret_cast<const half2 *>(&x.res);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __half22float2(rh[j]);
+        v[2 * j] = round_half(v[2 * j]) + f.x;
+        v[2 * j + 1] = round_half(v[2 * j + 1]) + f.y;
+      }
+    }
+    uint4 o;
+    half2 *oh2 = reinterpret_cast<half2 *>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      oh2[j] = __floats2half2_rn(act_t<ACT>(v[2 * j], e.act),
+                                 act_t<ACT>(v[2 * j + 1], e.act));
+    return o;
+  }
 }
 
 __device__ __forceinline__ void fail(const Args &g, volatile int *abort,
@@ -436,6 +466,49 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
         // smem row (this thread's row) -> one TMA store per warp. TMA drops
         // rows past M / past the image width and columns past N.
         const GemmEpilogue &e = g.epi;
+        // TMA store coordinates of this warp's 32 rows, fixed for the tile
+        // (the column coordinate moves per chunk): one piece for plain
+        // GEMMs, two 16-row pieces of long segments (seg_len is a multiple
+        // of 16, so a piece lies inside one segment), or 32 >> seg_log2
+        // pixel segments; piece h is staged at h << piece_shift.
+        int npieces = 1, piece_shift = 0;
+        int sx[2] = {0, 0}, sy[2] = {0, 0}, sz[2] = {0, 0};
+        bool sok[2] = {true, false};
+        if (CONV && g.row_segs) {
+          npieces = 2;
+          piece_shift = 11;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int row0 = mh * kBM + q * 32 + h * 16;
+            const int sidx = row0 / g.seg_len;
+            const int sg = mb * g.row_segs + sidx;
+            const int rr = sg / g.seg_parts;
+            const int n = rr / g.OH;
+            sok[h] = sidx < g.row_segs && n < g.batch;
+            sx[h] = (sg - rr * g.seg_parts) * g.seg_len + row0 - sidx * g.seg_len;
+            sy[h] = rr - n * g.OH;
+            sz[h] = n;
+          }
+        } else if (CONV) {
+          npieces = 32 >> g.seg_log2;
+          piece_shift = g.seg_log2 + 7;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int seg = mb * (BM >> g.seg_log2) + ((mh * kBM + q * 32) >> g.seg_log2) + h;
+            const int rr = seg / g.Wseg;
+            sok[h] = h < npieces;
+            sx[h] = (seg - rr * g.Wseg) << g.seg_log2;
+            if constexpr (EPI == kEpiDeconv) {
+              sy[h] = rr; // the input row n * H + h
+            } else {
+              const int n = rr / g.OH;
+              sy[h] = rr - n * g.OH;
+              sz[h] = n;
+            }
+          }
+        } else {
+          sx[0] = mb * BM + mh * kBM + q * 32;
+        }
 #pragma unroll 1
         for (int c = drains ? c_lo : c_hi; c < c_hi; c += 64) {
           uint32_t r[64];
@@ -467,43 +540,22 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
-            if (CONV && g.row_segs) {
-              // Two 16-row pieces; seg_len is a multiple of 16, so a piece
-              // lies inside one segment.
-              for (int h = 0; h < 2; ++h) {
-                const int row0 = mh * kBM + q * 32 + h * 16;
-                const int sidx = row0 / g.seg_len;
-                const int sg = mb * g.row_segs + sidx;
-                const int r = sg / g.seg_parts;
-                const int n = r / g.OH;
-                if (sidx < g.row_segs && n < g.batch)
-                  tma_store_4d(&mapC, buf + h * 2048, n_base + c,
-                               (sg - r * g.seg_parts) * g.seg_len + row0 - sidx * g.seg_len,
-                               r - n * g.OH, n);
-              }
+            if constexpr (EPI == kEpiDeconv) {
+              // Columns [n_base + c, +64) are channels co0.. of tap (a, b).
+              const int tap = (n_base + c) / g.dec_co;
+              const int co0 = n_base + c - tap * g.dec_co;
+              const int a = tap / g.dec_kw;
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+                if (h < npieces)
+                  tma_store_5d(&mapC, buf + (h << piece_shift), co0, tap - a * g.dec_kw, sx[h], a, sy[h]);
             } else if (CONV) {
-              // This warp's 32 rows are 32 >> seg_log2 whole segments.
-              for (int h = 0; h < (32 >> g.seg_log2); ++h) {
-                const int seg = mb * (BM >> g.seg_log2) +
-                                ((mh * kBM + q * 32) >> g.seg_log2) + h;
-                const int rr = seg / g.Wseg;
-                const int w0 = (seg - rr * g.Wseg) << g.seg_log2;
-                if constexpr (EPI == kEpiDeconv) {
-                  // Columns [n_base + c, +64) are channels co0.. of tap
-                  // (a, b); rr is the input row n * H + h.
-                  const int tap = (n_base + c) / g.dec_co;
-                  const int co0 = n_base + c - tap * g.dec_co;
-                  const int a = tap / g.dec_kw;
-                  tma_store_5d(&mapC, buf + (h << (g.seg_log2 + 7)), co0,
-                               tap - a * g.dec_kw, w0, a, rr);
-                } else {
-                  const int n = rr / g.OH;
-                  tma_store_4d(&mapC, buf + (h << (g.seg_log2 + 7)), n_base + c,
-                               w0, rr - n * g.OH, n);
-                }
-              }
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+                if (h < npieces && sok[h])
+                  tma_store_4d(&mapC, buf + (h << piece_shift), n_base + c, sx[h], sy[h], sz[h]);
             } else {
-              tma_store_2d(&mapC, buf, n_base + c, mb * BM + mh * kBM + q * 32);
+              tma_store_2d(&mapC, buf, n_base + c, sx[0]);
             }
             bulk_commit();
           }
