@@ -25,6 +25,14 @@ cores) is timed on rank 0 before the ranks join the process group.
 implementation of its layer path; the oracle port in oracle/ is the CPU
 baseline) on rank 0 only. `--config c1|c2|c3|c5|pre|post` measures the other
 configurations on one GPU.
+
+Side by side on the same B200: the default line's `abi_forward` times this
+repository's recognizer (B=512) and detector (8 pages of 960^2) libraries
+through ppocr_model_enqueue, the reference-facing Model ABI call, and the
+reference arm's `reference_gpu` times the reference's own compiled runtime
+(model_library.cu + runtime.cuh on cuDNN / cuBLAS / CUTLASS, built unmodified
+under oracle/_ref around the exporter-vocabulary twin of the same graph)
+through the same call.
 """
 
 from __future__ import annotations
@@ -247,6 +255,20 @@ def reference_arm(args):
                          "sample": f"{lines_per_step} lines per step (a bounded sample of the 512-line batch)"},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    # The reference's own GPU layer path on this box, for the side-by-side
+    # with this repository's libraries (the b200 arm's `abi_forward`).
+    try:
+        import torch
+
+        if torch.cuda.is_available():
+            _, _, local = dist_env()
+            dev = torch.device("cuda", local)
+            torch.cuda.set_device(dev)
+            line["reference_gpu"] = abi_comparison("reference", dev)
+        else:
+            line["reference_gpu"] = {"unavailable": "no CUDA device"}
+    except Exception as exc:  # reported, never fatal to the CPU arm
+        line["reference_gpu"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
     print(json.dumps(line), flush=True)
 
 
@@ -426,6 +448,10 @@ def b200_arm(args):
     else:
         rank_page = float("nan")
 
+    # ---- the same forwards through the reference-facing Model ABI call, for
+    # the side-by-side with the reference's own runtime (--impl reference)
+    abi = abi_comparison("b200", dev) if not args.no_pages else None
+
     csum = clocks.summary()
     per_rank = gather([rank_total_ms / args.steps, csum["sm_mhz"] or 0.0, rank_page])
     gpu_launches = launches_per_step * args.steps
@@ -464,6 +490,8 @@ def b200_arm(args):
         if page is not None:
             line["page_p50_ms"] = page["p50_ms"]
             line["page"] = page
+        if abi is not None:
+            line["abi_forward"] = abi
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
@@ -529,6 +557,108 @@ def _event_steps(stream, steps, body, flush):
         ends[i].record(stream)
     stream.synchronize()
     return [a.elapsed_time(b) for a, b in zip(starts, ends)]
+
+
+def abi_forward(so_path, weights_path, dev, steps: int, warmup: int, seed: int = SEED):
+    """Device time of one full-batch ppocr_model_enqueue of a Model ABI v2
+    library (model_abi.h:11-38), bound through the seven reference symbols
+    only, as the reference's catalog loader binds them
+    (model_engine_compiled.cpp:43-75): f32 NCHW input resident in HBM, L2
+    flushed by a 256 MB write outside the timed events, CUDA events on the
+    enqueue stream. The same call times this repository's libraries and the
+    reference's own compiled runtime, so the two are compared on one
+    interface. Returns {"batch", "ms" (median), "ms_min", "output_shape"}."""
+    import ctypes
+    from ctypes import c_char_p, c_int, c_size_t, c_void_p
+
+    import numpy as np
+    import torch
+
+    from ppocr_b200 import capi
+
+    dll = ctypes.CDLL(str(so_path), mode=ctypes.RTLD_LOCAL)
+    sig = {"ppocr_model_info": (c_void_p, []), "ppocr_model_load_weights": (c_void_p, [c_char_p]),
+           "ppocr_model_create": (c_void_p, [c_void_p, c_void_p, c_size_t, c_void_p]),
+           "ppocr_model_enqueue": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+           "ppocr_model_destroy": (None, [c_void_p]), "ppocr_model_error": (c_char_p, []),
+           "ppocr_model_release_resources": (None, [c_void_p])}
+    for name, (res, args) in sig.items():
+        fn = getattr(dll, name)
+        fn.restype, fn.argtypes = res, args
+    info = capi.PpocrModelInfo.from_address(dll.ppocr_model_info())
+    resources = capi.PpocrModelResources()
+    weights = dll.ppocr_model_load_weights(str(weights_path).encode())
+    if not weights:
+        raise RuntimeError(dll.ppocr_model_error().decode())
+    scratch = torch.empty(info.scratch_bytes, dtype=torch.uint8, device=dev)
+    handle = dll.ppocr_model_create(weights, scratch.data_ptr(), info.scratch_bytes, ctypes.byref(resources))
+    if not handle:
+        raise RuntimeError(dll.ppocr_model_error().decode())
+    in_shape = tuple(info.input_shape)
+    out_shape = tuple(info.output_shape[: info.output_rank])
+    batch = in_shape[0]
+    rng = np.random.default_rng(seed)
+    x = torch.from_numpy(rng.uniform(-1, 1, in_shape).astype(np.float32)).to(dev)
+    out = torch.empty(out_shape, dtype=torch.float16 if info.output_element_bytes == 2 else torch.float32,
+                      device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(dev)
+    s = c_void_p(stream.cuda_stream)
+
+    def body(i):
+        if dll.ppocr_model_enqueue(handle, x.data_ptr(), out.data_ptr(), batch, s) != 0:
+            raise RuntimeError(dll.ppocr_model_error().decode())
+
+    try:
+        for i in range(max(warmup, 3)):
+            body(i)
+        stream.synchronize()
+        ms = _event_steps(stream, steps, body, flush)
+    finally:
+        stream.synchronize()
+        dll.ppocr_model_destroy(handle)
+        dll.ppocr_model_release_resources(ctypes.byref(resources))
+    ms.sort()
+    return {"batch": batch, "ms": round(ms[len(ms) // 2], 4), "ms_min": round(ms[0], 4),
+            "output_shape": list(out_shape)}
+
+
+def abi_comparison(which: str, dev, steps: int = 10, warmup: int = 3) -> dict:
+    """Recognizer (B = 512, 256 and 64 lines) and detector (8 and 1 pages of 960^2) forwards
+    through ppocr_model_enqueue: which = "b200" times this repository's fused
+    libraries, which = "reference" the reference's own compiled runtime
+    (model_library.cu + runtime.cuh on cuDNN / cuBLAS / cuBLASLt / CUTLASS,
+    built unmodified around the exporter-vocabulary twin of the same graph
+    under oracle/_ref/models/). Same seeded weights function, same input."""
+    from ppocr_b200 import models
+
+    res = {"call": "ppocr_model_enqueue (Model ABI v2), f32 NCHW input resident in HBM, full batch, "
+                   "L2 flushed between steps, median of %d steps" % steps}
+    for key, name in (("recognizer_b512", "rec_b512"), ("recognizer_b256", "rec_b256"),
+                      ("recognizer_b64", "rec_b64"), ("detector_8x960", "det_b8"),
+                      ("detector_1x960", "det_b1")):
+        if which == "b200":
+            from ppocr_b200 import capi
+
+            capi.load()  # the model shells link libppocr_b200.so
+            so, wname = models.library_path(name), name
+        else:
+            wname = name + "_xv"
+            so = REPO / "oracle" / "_ref" / "models" / wname / "model.so"
+        if not Path(so).exists():
+            res[key] = {"unavailable": f"{Path(so).relative_to(REPO)} is not built"}
+            continue
+        try:
+            r = abi_forward(so, models.ensure_weights(wname), dev, steps, warmup)
+        except RuntimeError as exc:  # e.g. the reference's own workspace-capacity check
+            res[key] = {"unavailable": f"{exc}"[:200]}
+            continue
+        if key.startswith("recognizer"):
+            r["lines_per_s"] = round(r["batch"] / (r["ms"] / 1e3), 1)
+        else:
+            r["pages_per_s"] = round(r["batch"] / (r["ms"] / 1e3), 1)
+        res[key] = r
+    return res
 
 
 def op_bytes(g, index: int) -> float:

@@ -32,6 +32,7 @@ SHAPES = {
     "rec_b64": ("recognizer", 64, None),
     "rec_b2": ("recognizer", 2, None),
     "det_b8": ("detector", 8, 960),
+    "det_b1": ("detector", 1, 960),
     "det_b1_s128": ("detector", 1, 128),
     "block_b16": ("block", 16, None),
     "block_b2": ("block", 2, None),
@@ -39,8 +40,11 @@ SHAPES = {
     "neck_b4": ("neck", 4, None),
     "rec_b2_xv": ("recognizer", 2, None),
     "rec_b64_xv": ("recognizer", 64, None),
+    "rec_b512_xv": ("recognizer", 512, None),
+    "rec_b256_xv": ("recognizer", 256, None),
     "det_b1_s128_xv": ("detector", 1, 128),
     "det_b1_xv": ("detector", 1, 960),
+    "det_b8_xv": ("detector", 8, 960),
     "block_b16_xv": ("block", 16, None),
     "neck_b256_xv": ("neck", 256, None),
     "zoo_xv": ("zoo", 2, None),
