@@ -71,9 +71,66 @@ __device__ __forceinline__ void halo_fail(const HaloArgs &g, volatile int *abort
   if (g.err)
     atomicCAS(g.err, 0, code);
 }
+__device__ __forceinline__ void halo_fail(int *err, volatile int *abort, int code) {
+  *abort = 1;
+  if (err)
+    atomicCAS(err, 0, code);
+}
 
 // TMEM columns for one accumulator of BN columns.
 template <int BN> constexpr int acc_cols() { return BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256; }
+
+// Epilogue of one 128-row accumulator: TMEM lane = padded-flat output
+// index qrow (row i = qrow / wp, column j); rows past the slab, columns past
+// Wt and pixels outside the image are not stored. Round to fp16, + bias,
+// activation, 16-byte NHWC stores of up to BN columns from n0.
+template <int BN, int ACT>
+__device__ __forceinline__ void halo_drain_tile(uint32_t taddr, int qrow, int wp, int R, int Wt, int rb, int cb,
+                                                int n, int OH, int OW, int ldo, int n0, int Co, const half *bias,
+                                                half *out, int act) {
+  const int i = qrow / wp, j = qrow - i * wp;
+  const int oh = rb * R + i, ow = cb * Wt + j;
+  const bool valid = i < R && j < Wt && oh < OH && ow < OW;
+  half *dst = out + ((static_cast<long long>(n) * OH + oh) * OW + ow) * ldo;
+  // Up to 64 columns per TMEM round trip: all loads, then one wait.
+#pragma unroll
+  for (int c0 = 0; c0 < BN; c0 += 64) {
+    constexpr int kMax = BN < 64 ? BN : 64;
+    uint32_t r[kMax];
+#pragma unroll
+    for (int c = 0; c < kMax; c += 16)
+      tmem_ld16(taddr + c0 + c, *reinterpret_cast<uint32_t(*)[16]>(r + c));
+    tmem_ld_wait();
+    if (valid) {
+#pragma unroll
+      for (int h = 0; h < kMax / 8; ++h) {
+        const int cc = n0 + c0 + 8 * h;
+        if (cc < Co) {
+          float v[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            v[e] = round_half(__uint_as_float(r[8 * h + e]));
+          if (bias) {
+            const uint4 bb = __ldg(reinterpret_cast<const uint4 *>(bias + cc));
+            const half2 *bh = reinterpret_cast<const half2 *>(&bb);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __half22float2(bh[e]);
+              v[2 * e] += f.x;
+              v[2 * e + 1] += f.y;
+            }
+          }
+          uint4 o;
+          half2 *oh2 = reinterpret_cast<half2 *>(&o);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            oh2[e] = __floats2half2_rn(act_t<ACT>(v[2 * e], act), act_t<ACT>(v[2 * e + 1], act));
+          *reinterpret_cast<uint4 *>(dst + cc) = o;
+        }
+      }
+    }
+  }
+}
 
 // NT: 128-row tiles per slab, computed together.
 template <int BN, int ACT, int NT>
@@ -239,52 +296,210 @@ __global__ void __launch_bounds__(kHaloThreads, 1)
       }
       tc_fence_after();
 #pragma unroll 1
-      for (int t = 0; t < NT; ++t) {
-        const int qrow = t * 128 + q * 32 + lane; // padded-flat output index
-        const int i = qrow / wp, j = qrow - i * wp;
-        const int oh = rb * R + i, ow = cb * Wt + j;
-        const bool valid = i < R && j < Wt && oh < OH && ow < OW;
-        half *dst = out + ((static_cast<long long>(n) * OH + oh) * OW + ow) * ldo;
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + (set * NT + t) * ACC;
-        // Up to 64 columns per TMEM round trip: all loads, then one wait.
-#pragma unroll
-        for (int c0 = 0; c0 < BN; c0 += 64) {
-          constexpr int kMax = BN < 64 ? BN : 64;
-          uint32_t r[kMax];
-#pragma unroll
-          for (int c = 0; c < kMax; c += 16)
-            tmem_ld16(taddr + c0 + c, *reinterpret_cast<uint32_t(*)[16]>(r + c));
-          tmem_ld_wait();
-          if (valid) {
-#pragma unroll
-            for (int h = 0; h < kMax / 8; ++h) {
-              const int cc = n0 + c0 + 8 * h;
-              if (cc < Co) {
-                float v[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e)
-                  v[e] = round_half(__uint_as_float(r[8 * h + e]));
-                if (bias) {
-                  const uint4 bb = __ldg(reinterpret_cast<const uint4 *>(bias + cc));
-                  const half2 *bh = reinterpret_cast<const half2 *>(&bb);
-#pragma unroll
-                  for (int e = 0; e < 4; ++e) {
-                    const float2 f = __half22float2(bh[e]);
-                    v[2 * e] += f.x;
-                    v[2 * e + 1] += f.y;
-                  }
-                }
-                uint4 o;
-                half2 *oh2 = reinterpret_cast<half2 *>(&o);
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  oh2[e] = __floats2half2_rn(act_t<ACT>(v[2 * e], g.act), act_t<ACT>(v[2 * e + 1], g.act));
-                *reinterpret_cast<uint4 *>(dst + cc) = o;
-              }
-            }
+      for (int t = 0; t < NT; ++t)
+        halo_drain_tile<BN, ACT>(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + (set * NT + t) * ACC,
+                                 t * 128 + q * 32 + lane, wp, R, Wt, rb, cb, n, OH, OW, ldo, n0, Co, bias, out,
+                                 g.act);
+      tc_fence_before();
+      mbar_arrive(&tempty[set]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Streamed-filter form for wide inputs (Ci = 128..1024 in 64-channel chunks)
+// and narrow outputs (Co <= 64): the detector's FPN and DB-head 3x3 convs
+// (256 -> 64 at 30..240 pixels square).
+//
+// The generic implicit GEMM loads one 128-byte channel block per pixel per
+// tap, nine loads of every input pixel per 64 output channels; with N = 64
+// that L2 -> shared-memory traffic (2.7 GB per 240x240x8 layer) is the
+// bound. Here a stage is one filter row kh and one 64-channel chunk c: the
+// R input rows (oh0 + kh - 1 ..) of the slab as one SW128 TMA box of Wp =
+// Wt + 2 pixels per row, plus the three taps (kh, 0..2) of chunk c (3 x 64
+// rows of 128 bytes). The kw taps address the box through UMMA descriptors
+// shifted by kw rows, exactly as the resident-filter kernel above does for
+// all nine taps; the filter cannot stay resident (9 x 256 x 64 fp16 = 295
+// KB), so it streams with the activations, once per slab and stage. Per
+// slab: 3 x (Ci / 64) stages accumulate into the slab's NT accumulators
+// (double-buffered across slabs); input pixels cross L2 -> SM three times
+// instead of nine. Roles and bounded waits as in halo_conv_kernel.
+struct StreamArgs {
+  int OH, OW, batch;
+  int R, Wt, Wp;
+  int row_blocks, col_blocks, slabs;
+  int nck;               // 64-channel input chunks
+  int nbuf;              // stage ring depth
+  uint32_t a_bytes;      // R * Wp * 128: the TMA box of one stage
+  uint32_t a_stride;     // a_bytes + overreach, 1 KB aligned
+  uint32_t stage_stride; // a_stride + 3 taps x 64 rows x 128 B
+  int Co, ldo;
+  const half *bias;
+  half *out;
+  int act;
+  int *err;
+};
+
+template <int ACT, int NT>
+__global__ void __launch_bounds__(kHaloThreads, 1)
+    halo_stream_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_constant__ CUtensorMap mapW,
+                       const __grid_constant__ StreamArgs g) {
+  constexpr int BN = 64, ACC = 64;
+  constexpr uint32_t TMEM_COLS = 2 * NT * ACC <= 128 ? 128 : 2 * NT * ACC <= 256 ? 256 : 512;
+  static_assert(2 * NT * ACC <= 512, "accumulators exceed TMEM");
+  constexpr uint32_t TAP_BYTES = BN * 128;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *bars = smem + g.nbuf * g.stage_stride;
+  uint64_t *full = reinterpret_cast<uint64_t *>(bars);
+  uint64_t *empty = full + kMaxBufs;
+  uint64_t *tfull = empty + kMaxBufs;
+  uint64_t *tempty = tfull + 2;
+  uint64_t *drain = tempty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int first = blockIdx.x, step = gridDim.x;
+  const int stages_per_slab = 3 * g.nck;
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < kMaxBufs; ++b) {
+      mbar_init(&full[b], 1);
+      mbar_init(&empty[b], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  // Nothing above touches global memory (programmatic dependent launch).
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tensormap(&mapX);
+      prefetch_tensormap(&mapW);
+      uint32_t issued = 0, issued_par = 0;
+      int it = 0;
+      bool ok = true;
+      for (int s = first; ok && s < g.slabs; s += step) {
+        const int cb = s % g.col_blocks;
+        const int rest = s / g.col_blocks;
+        const int rb = rest % g.row_blocks;
+        const int n = rest / g.row_blocks;
+        for (int st = 0; st < stages_per_slab; ++st, ++it) {
+          const int kh = st / g.nck, c = st - kh * g.nck;
+          const int b = it % g.nbuf;
+          const uint32_t par = (it / g.nbuf) & 1;
+          if (!mbar_wait(&empty[b], par ^ 1, abort)) {
+            halo_fail(g.err, abort, 16);
+            ok = false;
+            break;
           }
+          uint8_t *stage = smem + b * g.stage_stride;
+          mbar_arrive_expect_tx(&full[b], g.a_bytes + 3 * TAP_BYTES);
+          issued |= 1u << b;
+          issued_par = (issued_par & ~(1u << b)) | (par << b);
+          // Input rows rb * R + kh - 1 .. (+R), columns cb * Wt - 1 .. (+Wp);
+          // outside the image the box is zero-filled (the conv padding).
+          tma_load_4d(stage, &mapX, &full[b], c * 64, cb * g.Wt - 1, rb * g.R + kh - 1, n);
+          for (int kw = 0; kw < 3; ++kw)
+            tma_load_3d(stage + g.a_stride + kw * TAP_BYTES, &mapW, &full[b], c * 64, kh * 3 + kw, 0);
         }
       }
+      // Every load issued must land before shared memory goes away.
+      for (int b = 0; b < kMaxBufs; ++b)
+        if (issued & (1u << b)) {
+          const long long t0 = clock64();
+          while (!mbar_try_wait(&full[b], (issued_par >> b) & 1u) && clock64() - t0 < kWaitBudgetCycles) {
+          }
+        }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16_f32(128, BN);
+      const int slabs = g.slabs, nbuf = g.nbuf;
+      bool ok = true;
+      int it = 0, sl = 0;
+      for (int s = first; ok && s < slabs; s += step, ++sl) {
+        const int set = sl & 1;
+        if (!mbar_wait(&tempty[set], ((sl >> 1) & 1) ^ 1, abort)) {
+          halo_fail(g.err, abort, 17);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + set * NT * ACC;
+        for (int st = 0; st < stages_per_slab; ++st, ++it) {
+          const int b = it % nbuf;
+          if (!mbar_wait(&full[b], (it / nbuf) & 1, abort)) {
+            halo_fail(g.err, abort, 18);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint8_t *stage = smem + b * g.stage_stride;
+          const uint64_t a0 = sdesc_k_sw128(smem_u32(stage));
+          const uint64_t b0 = sdesc_k_sw128(smem_u32(stage + g.a_stride));
+#pragma unroll
+          for (int kw = 0; kw < 3; ++kw)
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+#pragma unroll
+              for (int t = 0; t < NT; ++t)
+                umma_f16(d + t * ACC, a0 + t * 128 * 8 + kw * 8 + 2 * k, b0 + kw * (TAP_BYTES >> 4) + 2 * k, idesc,
+                         (st | kw | k) != 0);
+          umma_commit(&empty[b]); // the stage is free once its MMAs complete
+        }
+        if (ok)
+          umma_commit(&tfull[set]);
+      }
+      umma_commit(drain);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(drain, 0) && clock64() - t0 < kWaitBudgetCycles) {
+      }
+    }
+  } else {
+    // Epilogue: warp w drains TMEM lane quarter w % 4.
+    const int q = warp & 3;
+    bool ok = true;
+    int sl = 0;
+    for (int s = first; ok && s < g.slabs; s += step, ++sl) {
+      const int cb = s % g.col_blocks;
+      const int rest = s / g.col_blocks;
+      const int rb = rest % g.row_blocks;
+      const int n = rest / g.row_blocks;
+      const int set = sl & 1;
+      if (!mbar_wait(&tfull[set], (sl >> 1) & 1, abort)) {
+        halo_fail(g.err, abort, 19);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll 1
+      for (int t = 0; t < NT; ++t)
+        halo_drain_tile<BN, ACT>(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + (set * NT + t) * ACC,
+                                 t * 128 + q * 32 + lane, g.Wp, g.R, g.Wt, rb, cb, n, g.OH, g.OW, g.ldo, 0,
+                                 g.Co, g.bias, g.out, g.act);
       tc_fence_before();
       mbar_arrive(&tempty[set]);
     }
@@ -411,6 +626,97 @@ bool pick_slab(int OH, int OW, uint32_t w_bytes, int &R, int &Wt, int &nbuf) {
   return true;
 }
 
+size_t stream_smem(const StreamArgs &g) { return 1024 + size_t(g.nbuf) * g.stage_stride + 256; }
+
+template <int ACT, int NT>
+cudaError_t launch_stream(const CUtensorMap &mx, const CUtensorMap &mw, const StreamArgs &g, cudaStream_t s) {
+  auto kernel = halo_stream_kernel<ACT, NT>;
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr = cudaSuccess;
+  std::call_once(once[dev & 63], [&] {
+    attr = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemLimit));
+  });
+  if (attr != cudaSuccess)
+    return attr;
+  const int grid = g.slabs < sm_count() ? g.slabs : sm_count();
+  launch_pdl(kernel, grid, kHaloThreads, stream_smem(g), s, mx, mw, g);
+  return cudaGetLastError();
+}
+
+template <int NT>
+cudaError_t dispatch_stream_act(const CUtensorMap &mx, const CUtensorMap &mw, const StreamArgs &g, cudaStream_t s) {
+  switch (g.act) {
+  case kActNone:
+    return launch_stream<kActNone, NT>(mx, mw, g, s);
+  case kActRelu:
+    return launch_stream<kActRelu, NT>(mx, mw, g, s);
+  default:
+    return launch_stream<-1, NT>(mx, mw, g, s);
+  }
+}
+
+// Slab shape for the streamed form: the most 128-row tiles per slab (up to
+// 4, interleaved) among shapes wasting at most 10 % more MMA rows than the
+// best, then the fewest wasted rows; the deepest ring (2..4 stages) that
+// fits. A stage holds R input rows of Wp pixels (+ the overreach of the
+// last tile) and three 8 KB filter taps.
+bool pick_stream_slab(int OH, int OW, StreamArgs &g) {
+  struct Cand {
+    int r, wt, nb, tiles;
+    uint32_t a_bytes, a_stride;
+    double eff;
+  };
+  Cand cands[16 * 16];
+  int nc = 0;
+  double best = 0.0;
+  for (int cbk = 1; cbk <= 16; ++cbk) {
+    const int wt = (OW + cbk - 1) / cbk;
+    const int wp = wt + 2;
+    if (wp > 256)
+      continue;
+    for (int r = 1; r <= 16; ++r) {
+      const int tiles = (r * wp + 127) / 128;
+      if (tiles > 4)
+        break;
+      const uint32_t a_bytes = static_cast<uint32_t>(r) * wp * 128;
+      const uint32_t a_stride = round1k(a_bytes + overreach_bytes(r, wp, tiles));
+      const uint32_t stage = a_stride + 3 * 64 * 128;
+      int nb = 0;
+      for (int k = kMaxBufs; k >= 2 && !nb; --k)
+        if (1024 + size_t(k) * stage + 256 <= kSmemLimit)
+          nb = k;
+      if (!nb)
+        break;
+      const int rbk = (OH + r - 1) / r;
+      const double eff = static_cast<double>(OH) * OW / (static_cast<double>(rbk) * cbk * tiles * 128);
+      cands[nc++] = {r, wt, nb, tiles, a_bytes, a_stride, eff};
+      if (eff > best)
+        best = eff;
+    }
+  }
+  int pick = -1;
+  for (int i = 0; i < nc; ++i) {
+    if (cands[i].eff < 0.9 * best)
+      continue;
+    if (pick < 0 || cands[i].tiles > cands[pick].tiles ||
+        (cands[i].tiles == cands[pick].tiles && cands[i].eff > cands[pick].eff + 1e-9))
+      pick = i;
+  }
+  if (pick < 0)
+    return false;
+  const Cand &c = cands[pick];
+  g.R = c.r;
+  g.Wt = c.wt;
+  g.Wp = c.wt + 2;
+  g.nbuf = c.nb;
+  g.a_bytes = c.a_bytes;
+  g.a_stride = c.a_stride;
+  g.stage_stride = c.a_stride + 3 * 64 * 128;
+  return true;
+}
+
 } // namespace
 
 bool halo_conv_supported(const ConvShape &s, const GemmEpilogue &epi) {
@@ -477,6 +783,68 @@ cudaError_t halo_conv(const half *x, const half *w, const ConvShape &s, const Ge
     return cudaErrorNotSupported;
   const size_t smem = halo_smem(w_bytes, g.slab_bytes, nbuf, g.slack);
   return BN == 48 ? dispatch_halo_nt<48>(mx, mw, g, smem, stream) : dispatch_halo_nt<64>(mx, mw, g, smem, stream);
+}
+
+bool halo_stream_supported(const ConvShape &s, const GemmEpilogue &epi) {
+  const int OH = s.out_h ? s.out_h : s.H + 2 * s.pad_h - s.KH + 1;
+  const int OW = s.out_w ? s.out_w : s.W + 2 * s.pad_w - s.KW + 1;
+  return !epi.residual && s.Ci % 64 == 0 && s.Ci >= 128 && s.Ci <= 1024 && s.Co % 16 == 0 && s.Co <= 64 &&
+         s.KH == 3 && s.KW == 3 && s.pad_h == 1 && s.pad_w == 1 && OH == s.H && OW == s.W && epi.ldo % 8 == 0;
+}
+
+cudaError_t halo_stream_conv(const half *x, const half *w, const ConvShape &s, const GemmEpilogue &epi,
+                             cudaStream_t stream) {
+  if (!halo_stream_supported(s, epi))
+    return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) ||
+      (reinterpret_cast<uintptr_t>(epi.out) & 15) || (epi.bias && (reinterpret_cast<uintptr_t>(epi.bias) & 15)))
+    return cudaErrorInvalidValue;
+  if (s.batch <= 0 || s.H <= 0 || s.W <= 0)
+    return cudaSuccess;
+  StreamArgs g{};
+  if (!pick_stream_slab(s.H, s.W, g))
+    return cudaErrorNotSupported;
+  g.OH = s.H;
+  g.OW = s.W;
+  g.batch = s.batch;
+  g.row_blocks = (s.H + g.R - 1) / g.R;
+  g.col_blocks = (s.W + g.Wt - 1) / g.Wt;
+  const long long slabs = static_cast<long long>(s.batch) * g.row_blocks * g.col_blocks;
+  if (slabs > 0x3fffffffLL)
+    return cudaErrorInvalidValue;
+  g.slabs = static_cast<int>(slabs);
+  g.nck = s.Ci / 64;
+  g.Co = s.Co;
+  g.ldo = epi.ldo;
+  g.bias = epi.bias;
+  g.out = epi.out;
+  g.act = epi.act;
+  g.err = device_error_word();
+  // x [batch][H][W][Ci]: boxes of 64 channels x Wp pixels x R rows.
+  CUtensorMap mx, mw;
+  cuuint64_t dx[4] = {static_cast<cuuint64_t>(s.Ci), static_cast<cuuint64_t>(s.W), static_cast<cuuint64_t>(s.H),
+                      static_cast<cuuint64_t>(s.batch)};
+  cuuint64_t sx[3] = {static_cast<cuuint64_t>(s.Ci) * 2, static_cast<cuuint64_t>(s.W) * s.Ci * 2,
+                      static_cast<cuuint64_t>(s.H) * s.W * s.Ci * 2};
+  cuuint32_t bx[4] = {64, static_cast<cuuint32_t>(g.Wp), static_cast<cuuint32_t>(g.R), 1};
+  // w [Co][9][Ci]: one 64-channel x 64-row box per tap and chunk (rows past
+  // Co zero-filled).
+  cuuint64_t dw[3] = {static_cast<cuuint64_t>(s.Ci), 9, static_cast<cuuint64_t>(s.Co)};
+  cuuint64_t sw[2] = {static_cast<cuuint64_t>(s.Ci) * 2, static_cast<cuuint64_t>(9) * s.Ci * 2};
+  cuuint32_t bw[3] = {64, 1, 64};
+  if (!encode_fp16_map(&mx, x, 4, dx, sx, bx, true) || !encode_fp16_map(&mw, w, 3, dw, sw, bw, true))
+    return cudaErrorNotSupported;
+  const int tiles = (g.R * g.Wp + 127) / 128;
+  switch (tiles) {
+  case 1:
+    return dispatch_stream_act<1>(mx, mw, g, stream);
+  case 2:
+    return dispatch_stream_act<2>(mx, mw, g, stream);
+  case 3:
+    return dispatch_stream_act<3>(mx, mw, g, stream);
+  default:
+    return dispatch_stream_act<4>(mx, mw, g, stream);
+  }
 }
 
 } // namespace pb2

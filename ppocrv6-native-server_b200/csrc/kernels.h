@@ -58,6 +58,14 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
 bool halo_conv_supported(const ConvShape &s, const GemmEpilogue &epi);
 cudaError_t halo_conv(const half *x, const half *w, const ConvShape &s,
                       const GemmEpilogue &epi, cudaStream_t stream);
+// Wide-input, narrow-output form (3x3, pad 1, stride 1, Ci a multiple of 64
+// from 128 to 1024, Co a multiple of 16 up to 64, no residual): stages of R
+// input rows x one 64-channel chunk, each read by the three taps of one
+// filter row through shifted UMMA descriptors, with the filter streamed per
+// stage. tc_conv routes such layers here.
+bool halo_stream_supported(const ConvShape &s, const GemmEpilogue &epi);
+cudaError_t halo_stream_conv(const half *x, const half *w, const ConvShape &s,
+                             const GemmEpilogue &epi, cudaStream_t stream);
 
 // Transposed convolution with kernel == stride (no padding) on the tensor
 // cores, Co a multiple of 64: a 1x1 implicit GEMM over the input pixels with

@@ -962,6 +962,11 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
     if (e != cudaErrorNotSupported)
       return e;
   }
+  if (halo_stream_supported(s, epi)) {
+    const cudaError_t e = halo_stream_conv(x, w, s, epi, stream);
+    if (e != cudaErrorNotSupported)
+      return e;
+  }
   int bn = pick_bn(s.Co);
   const int taps = s.KH * s.KW;
   // Segment length: 32 pixels when that pads the output row no more than

@@ -396,6 +396,37 @@ def test_upsample_concat(native, cuda, batch, oh, ow, levels):
     assert torch.equal(host(y), want)
 
 
+STREAM_CASES = [
+    # batch, h, w, ci, co, act: wide-input 3x3 convs with Co <= 64, staged
+    # per filter row and 64-channel chunk with the filter streamed
+    (1, 240, 240, 256, 64, 1),  # the C5 FPN / DB-head layer: 2-row slabs, 4 tiles, 4 chunks
+    (2, 32, 32, 256, 64, 0),    # 11-row slabs, 3 tiles, 3-deep ring, no activation
+    (1, 30, 30, 256, 64, 1),    # 15-row slabs, partial last row block
+    (2, 60, 60, 128, 64, 1),    # Ci 128 (2 chunks)
+    (1, 7, 100, 256, 32, 2),    # Co 32 (filter rows past Co zero-filled), 2 column blocks, GELU switch
+    (3, 5, 254, 512, 48, 1),    # Wp 256, single-row slabs (2 tiles), 8 chunks, Co 48
+    (1, 9, 300, 192, 64, 1),    # 3 chunks, 2 column blocks of 150
+    (2, 4, 4, 256, 64, 1),      # tiny images: one tile, most rows discarded
+]
+
+
+@pytest.mark.parametrize("batch,h,w,ci,co,act", STREAM_CASES)
+def test_halo_stream_conv(native, cuda, batch, h, w, ci, co, act):
+    r = rng(700 + batch + h + w + ci + co)
+    x = f16(r.uniform(-1, 1, (batch, h, w, ci)))
+    wt = f16(r.standard_normal((co, 3, 3, ci)) * np.sqrt(2.0 / (ci * 9)))
+    b = f16(r.normal(0, 0.1, co))
+    y = torch.full((batch, h, w, co), float("nan"), dtype=torch.float16, device=cuda)
+    dx, dw, db = dev(x), dev(wt), dev(b)
+    rc = native.ppocr_b200_conv_nhwc(ptr(dx), ptr(dw), ptr(db), ptr(y), batch, ci, h, w, co, 3, 3,
+                                     1, 1, 1, 1, 1, act, stream_handle())
+    assert rc == 0, native.ppocr_b200_last_error()
+    sync()
+    check_device_error(native)
+    want = L.conv_nhwc(x, wt, b, (1, 1), (1, 1), 1, act)
+    assert_close(host(y), want, what=f"streamed halo conv {batch}x{h}x{w}x{ci}->{co} act {act}")
+
+
 DECONV_CASES = [
     # batch, h, w, ci, co, act, bias
     (2, 16, 16, 64, 64, 1, True),     # tensor-core path (Co % 64 == 0)
