@@ -100,3 +100,52 @@ def test_catalog_through_reference_engine(native, cuda, engine_lib, tmp_path, fa
     finally:
         engine_lib.ref_engine_destroy(h)
 
+
+
+def test_package_through_reference_engine(native, cuda, engine_lib, tmp_path):
+    """A deployment package written by ppocr_b200.package from shape
+    directories in export.py's format (package.sh's layout: catalog rows
+    relative to models.tsv, shared weights.f32, the runtime library at the
+    package root) loads in the reference's engine and runs bit-identical to
+    the ctypes path of the same shapes."""
+    import shutil
+
+    from ppocr_b200 import models
+    from ppocr_b200 import package as P
+
+    def shape_dir(name):
+        d = tmp_path / "src" / name
+        d.mkdir(parents=True)
+        shutil.copy2(models.MODELS_SRC / name / "model.inc", d / "model.inc")
+        shutil.copy2(models.ensure_weights(name), d / "weights.f32")
+        return d
+
+    out = P.package(tmp_path / "pkg", [shape_dir("rec_b2"), shape_dir("rec_b64")], [shape_dir("det_b1_s128")])
+    P.verify(out)
+    for kind, name, batch in (("recognition", "rec_b64", 5), ("detection", "det_b1_s128", 1)):
+        h = engine_lib.ref_engine_load(str(out / kind / "models.tsv").encode())
+        assert h, engine_lib.ref_engine_error().decode()
+        try:
+            shapes = []
+            for p in range(engine_lib.ref_engine_profiles(h)):
+                s = (ctypes.c_longlong * 4)()
+                engine_lib.ref_engine_profile_shape(h, p, s)
+                shapes.append(tuple(s))
+            m = P.read_model_inc(out / kind / name / "model.inc")
+            profile = shapes.index(tuple(m.input_shape))
+            x = rng(90 + batch).uniform(-1, 1, (batch,) + tuple(m.input_shape[1:])).astype(np.float32)
+            dx = torch.from_numpy(x).to(cuda)
+            f32 = engine_lib.ref_engine_output_is_f32(h)
+            out_t = torch.empty((batch,) + tuple(m.output_shape[1:]), dtype=torch.float32 if f32 else torch.float16,
+                                device=cuda)
+            ws = engine_lib.ref_engine_workspace_bytes(h)
+            scratch = torch.empty(ws, dtype=torch.uint8, device=cuda)
+            stream = torch.cuda.Stream(cuda)
+            rc = engine_lib.ref_engine_enqueue(h, profile, batch, ctypes.c_void_p(dx.data_ptr()),
+                                               ctypes.c_void_p(out_t.data_ptr()), ctypes.c_void_p(scratch.data_ptr()),
+                                               ws, ctypes.c_void_p(stream.cuda_stream))
+            assert rc == 0, engine_lib.ref_engine_error().decode()
+            stream.synchronize()
+            assert torch.equal(out_t.cpu(), _ours(name, x, cuda))
+        finally:
+            engine_lib.ref_engine_destroy(h)
