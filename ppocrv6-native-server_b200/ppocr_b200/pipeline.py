@@ -303,6 +303,64 @@ class PagePipeline:
                                                 ctypes.c_void_p(self.stream.cuda_stream)))
         self.rec.enqueue(crops_nhwc)
 
+    def enqueue_host(self, pages_h: torch.Tensor, crops_h: torch.Tensor, bitmap_h: torch.Tensor,
+                     ids_h: torch.Tensor, len_h: torch.Tensor, score_h: torch.Tensor) -> None:
+        """One page batch end to end from pinned host memory, asynchronous on
+        the pipeline's stream: pages in, binary maps and decoded lines out.
+
+        The reference's full-page worker copies, detects, reads the map back
+        and then recognizes in turn (full_page_worker.cpp:361-497,
+        detection_worker.cpp:402-405). Here the crops' host->device copy runs
+        on a copy stream during the detector (after the pages' copy, which
+        the detector waits for), and the binary map's
+        device->host copy on a second copy stream during the recognizer; the
+        batch is complete when the pipeline's stream passes both (so an event
+        recorded on it after this call marks the end of the whole batch).
+        A later call's copies wait for this call's readers of the staging
+        buffers. bitmap_h: uint8 [>=pages, 1, S, S]; ids_h int32 [>=lines, T];
+        len_h int32 [>=lines]; score_h f32 [>=lines]."""
+        if not hasattr(self, "_h2d"):
+            with torch.cuda.device(self.device):
+                self._h2d = torch.cuda.Stream(self.device)
+                self._d2h = torch.cuda.Stream(self.device)
+                self._stage_pages = torch.empty(self.pages, self.size, self.size, 3, dtype=torch.float16,
+                                                device=self.device)
+                b, c, h, w = self.rec.model.input_shape
+                self._stage_crops = torch.empty(b, h, w, c, dtype=torch.float16, device=self.device)
+                self._pages_in = torch.cuda.Event()
+                self._crops_in, self._crops_read = torch.cuda.Event(), torch.cuda.Event()
+                self._map_ready, self._map_out = torch.cuda.Event(), torch.cuda.Event()
+        s = self.stream
+        m, n = pages_h.shape[0], crops_h.shape[0]
+        with torch.cuda.stream(s):
+            self._stage_pages[:m].copy_(pages_h, non_blocking=True)
+            self._pages_in.record(s)
+        # The crops follow the pages over the link (not beside them: the
+        # detector waits for the pages alone), and land during the detector.
+        self._h2d.wait_event(self._pages_in)
+        self._h2d.wait_event(self._crops_read)  # previous batch's recognizer is done with the crops
+        with torch.cuda.stream(self._h2d):
+            self._stage_crops[:n].copy_(crops_h, non_blocking=True)
+            self._crops_in.record(self._h2d)
+        self.det.enqueue_nhwc(self._stage_pages[:m], self.prob, s)
+        s.wait_event(self._map_out)  # previous batch's map is on the host before it is overwritten
+        px = m * self.size * self.size
+        capi.check(self.lib.ppocr_b200_binarize(_p(self.prob), _p(self.bitmap), px, self.thresh,
+                                                ctypes.c_void_p(s.cuda_stream)))
+        self._map_ready.record(s)
+        self._d2h.wait_event(self._map_ready)
+        with torch.cuda.stream(self._d2h):
+            bitmap_h.view(-1)[:px].copy_(self.bitmap.view(-1)[:px], non_blocking=True)
+            self._map_out.record(self._d2h)
+        s.wait_event(self._crops_in)
+        self.rec.enqueue(self._stage_crops[:n])
+        self._crops_read.record(s)
+        with torch.cuda.stream(s):
+            ids_h[:n].copy_(self.rec.out_ids[:n], non_blocking=True)
+            len_h[:n].copy_(self.rec.out_len[:n], non_blocking=True)
+            score_h[:n].copy_(self.rec.out_score[:n], non_blocking=True)
+        s.wait_event(self._map_out)
+
     def close(self) -> None:
         self.det.close()
         self.rec.close()

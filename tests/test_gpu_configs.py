@@ -139,5 +139,27 @@ def test_c5_page_pipeline_full_size(native, cuda):
         assert torch.equal(pp.prob.cpu(), prob.flip(0))
         ids2, lens2, scores2 = pp.rec.results(512)
         assert np.array_equal(ids, ids2) and np.array_equal(lens, lens2) and np.array_equal(scores, scores2)
+        # End to end from pinned host memory (copies overlapped with the
+        # detector and recognizer on side streams): the same maps and tokens,
+        # twice in a row (the second call reuses the staging buffers), and
+        # with fewer crops than the compiled batch.
+        ph, ch = torch.from_numpy(pages).pin_memory(), torch.from_numpy(crops).pin_memory()
+        bm_h = torch.zeros(8, 1, 960, 960, dtype=torch.uint8).pin_memory()
+        ids_h = torch.zeros(512, pp.rec.T, dtype=torch.int32).pin_memory()
+        len_h = torch.zeros(512, dtype=torch.int32).pin_memory()
+        sc_h = torch.zeros(512, dtype=torch.float32).pin_memory()
+        for _ in range(2):
+            bm_h.zero_()
+            ids_h.zero_()
+            pp.enqueue_host(ph, ch, bm_h, ids_h, len_h, sc_h)
+            pp.stream.synchronize()
+            assert torch.equal(bm_h, bitmap)
+            assert np.array_equal(ids_h.numpy(), ids) and np.array_equal(len_h.numpy(), lens)
+            assert np.array_equal(sc_h.numpy(), scores)
+        len_h.fill_(-1)
+        pp.enqueue_host(ph, ch[:100], bm_h, ids_h, len_h, sc_h)
+        pp.stream.synchronize()
+        assert np.array_equal(len_h[:100].numpy(), lens[:100]) and (len_h[100:] == -1).all()
+        assert native.ppocr_b200_device_error() == 0
     finally:
         pp.close()
