@@ -657,26 +657,29 @@ cudaError_t dispatch_stream_act(const CUtensorMap &mx, const CUtensorMap &mw, co
   }
 }
 
-// Slab shape for the streamed form: the most 128-row tiles per slab (up to
-// 4, interleaved) among shapes wasting at most 10 % more MMA rows than the
-// best, then the fewest wasted rows; the deepest ring (2..4 stages) that
-// fits. A stage holds R input rows of Wp pixels (+ the overreach of the
-// last tile) and three 8 KB filter taps.
-bool pick_stream_slab(int OH, int OW, StreamArgs &g) {
-  struct Cand {
-    int r, wt, nb, tiles;
-    uint32_t a_bytes, a_stride;
-    double eff;
-  };
-  Cand cands[16 * 16];
-  int nc = 0;
-  double best = 0.0;
+// Slab shape for the streamed form, from a cost model of the persistent
+// grid: time ~ waves x tiles per slab x the per-MMA cost of that many
+// interleaved accumulators (consecutive MMAs into one accumulator wait on
+// each other at N = 64: one tile runs at about half rate, two at 0.8),
+// waves = ceil(slabs / SMs). Large layers take 4-tile slabs (the 240^2
+// detector layers: 2-row slabs); small ones trade tiles per slab for more
+// slabs in flight (30^2 x 8 pages: 64 one-tile slabs instead of 16
+// four-tile ones). Ties go to more tiles per slab, then fewer wasted rows.
+// The ring is the deepest (2..4 stages) that fits; a stage holds R input
+// rows of Wp pixels (+ the overreach of the last tile) and three 8 KB
+// filter taps.
+bool pick_stream_slab(int batch, int OH, int OW, StreamArgs &g) {
+  static const double kTilePenalty[5] = {0.0, 2.0, 1.25, 1.05, 1.0};
+  const int sms = sm_count();
+  bool found = false;
+  double best_cost = 0.0, best_eff = 0.0;
+  int best_tiles = 0;
   for (int cbk = 1; cbk <= 16; ++cbk) {
     const int wt = (OW + cbk - 1) / cbk;
     const int wp = wt + 2;
     if (wp > 256)
       continue;
-    for (int r = 1; r <= 16; ++r) {
+    for (int r = 1; r <= 16 && r <= OH + 15; ++r) {
       const int tiles = (r * wp + 127) / 128;
       if (tiles > 4)
         break;
@@ -690,31 +693,31 @@ bool pick_stream_slab(int OH, int OW, StreamArgs &g) {
       if (!nb)
         break;
       const int rbk = (OH + r - 1) / r;
+      const long long slabs = static_cast<long long>(batch) * rbk * cbk;
+      const double waves = static_cast<double>((slabs + sms - 1) / sms);
+      const double cost = waves * tiles * kTilePenalty[tiles];
       const double eff = static_cast<double>(OH) * OW / (static_cast<double>(rbk) * cbk * tiles * 128);
-      cands[nc++] = {r, wt, nb, tiles, a_bytes, a_stride, eff};
-      if (eff > best)
-        best = eff;
+      const bool better = !found || cost < best_cost * (1 - 1e-9) ||
+                          (cost <= best_cost * (1 + 1e-9) &&
+                           (tiles > best_tiles || (tiles == best_tiles && eff > best_eff + 1e-9)));
+      if (better) {
+        found = true;
+        best_cost = cost;
+        best_eff = eff;
+        best_tiles = tiles;
+        g.R = r;
+        g.Wt = wt;
+        g.Wp = wp;
+        g.nbuf = nb;
+        g.a_bytes = a_bytes;
+        g.a_stride = a_stride;
+        g.stage_stride = stage;
+      }
+      if (r >= OH)
+        break; // taller slabs only add empty rows
     }
   }
-  int pick = -1;
-  for (int i = 0; i < nc; ++i) {
-    if (cands[i].eff < 0.9 * best)
-      continue;
-    if (pick < 0 || cands[i].tiles > cands[pick].tiles ||
-        (cands[i].tiles == cands[pick].tiles && cands[i].eff > cands[pick].eff + 1e-9))
-      pick = i;
-  }
-  if (pick < 0)
-    return false;
-  const Cand &c = cands[pick];
-  g.R = c.r;
-  g.Wt = c.wt;
-  g.Wp = c.wt + 2;
-  g.nbuf = c.nb;
-  g.a_bytes = c.a_bytes;
-  g.a_stride = c.a_stride;
-  g.stage_stride = c.a_stride + 3 * 64 * 128;
-  return true;
+  return found;
 }
 
 } // namespace
@@ -802,7 +805,7 @@ cudaError_t halo_stream_conv(const half *x, const half *w, const ConvShape &s, c
   if (s.batch <= 0 || s.H <= 0 || s.W <= 0)
     return cudaSuccess;
   StreamArgs g{};
-  if (!pick_stream_slab(s.H, s.W, g))
+  if (!pick_stream_slab(s.batch, s.H, s.W, g))
     return cudaErrorNotSupported;
   g.OH = s.H;
   g.OW = s.W;

@@ -398,14 +398,17 @@ def test_upsample_concat(native, cuda, batch, oh, ow, levels):
 
 STREAM_CASES = [
     # batch, h, w, ci, co, act: wide-input 3x3 convs with Co <= 64, staged
-    # per filter row and 64-channel chunk with the filter streamed
-    (1, 240, 240, 256, 64, 1),  # the C5 FPN / DB-head layer: 2-row slabs, 4 tiles, 4 chunks
-    (2, 32, 32, 256, 64, 0),    # 11-row slabs, 3 tiles, 3-deep ring, no activation
-    (1, 30, 30, 256, 64, 1),    # 15-row slabs, partial last row block
-    (2, 60, 60, 128, 64, 1),    # Ci 128 (2 chunks)
-    (1, 7, 100, 256, 32, 2),    # Co 32 (filter rows past Co zero-filled), 2 column blocks, GELU switch
-    (3, 5, 254, 512, 48, 1),    # Wp 256, single-row slabs (2 tiles), 8 chunks, Co 48
-    (1, 9, 300, 192, 64, 1),    # 3 chunks, 2 column blocks of 150
+    # per filter row and 64-channel chunk with the filter streamed; the slab
+    # plan (rows x columns, tiles per slab, ring depth) follows from the
+    # shape and the SM count
+    (1, 240, 240, 256, 64, 1),  # the C5 FPN / DB-head layer: 2-row slabs, 4 tiles, 2-deep ring
+    (8, 60, 60, 256, 64, 0),    # C5's 60^2 level: 4-row slabs, 2 tiles, 3-deep ring, no activation
+    (8, 30, 30, 256, 64, 1),    # C5's 30^2 level: 4-row one-tile slabs, 4-deep ring, partial row block
+    (4, 96, 96, 256, 64, 1),    # 3 tiles per slab, 3 column blocks of 32
+    (2, 32, 32, 128, 64, 1),    # Ci 128 (2 chunks), 2 column blocks
+    (1, 7, 100, 256, 32, 2),    # Co 32 (filter rows past Co zero-filled), single-row slabs, GELU switch
+    (3, 5, 254, 512, 48, 1),    # 8 chunks, Co 48, many narrow column blocks
+    (1, 9, 300, 192, 64, 1),    # 3 chunks, width in column blocks
     (2, 4, 4, 256, 64, 1),      # tiny images: one tile, most rows discarded
 ]
 
