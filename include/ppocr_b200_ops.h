@@ -137,6 +137,18 @@ int ppocr_b200_mean_nhwc(const void *x, void *y, int batch, int c, int spatial,
 int ppocr_b200_deconv_nhwc(const void *x, const void *w, const void *bias,
                            void *y, int batch, int h, int w_, int ci, int co,
                            int kh, int kw, int activation, cudaStream_t stream);
+
+// The DB head's last two layers in one pass (Runtime::deconv twice,
+// runtime.cuh:426-453, as export.py emits the head): y2 = act2(deconv(
+// act(deconv(x, w, bias)), w2, bias2)), both 2x2 stride 2; x [batch][h][w_]
+// [ci] (ci a multiple of 8), w [ci][2][2][64], bias [64] or null, w2
+// [64][2][2][1], bias2 [1] or null, y2 [batch][4h][4w_][1]. Bit-identical to
+// ppocr_b200_deconv_nhwc with co = 64 followed by co = 1; the 64-channel map
+// is never written. Same activation codes.
+int ppocr_b200_deconv_db_tail(const void *x, const void *w, const void *bias,
+                              int act, const void *w2, const void *bias2,
+                              int act2, void *y2, int batch, int h, int w_,
+                              int ci, cudaStream_t stream);
 // DB binarize (native/src/detection/db_postprocess.cpp:189-190, on device):
 // map[i] = prob[i] > thresh ? 255 : 0. prob float32, map uint8.
 int ppocr_b200_binarize(const float *prob, uint8_t *map, size_t n,

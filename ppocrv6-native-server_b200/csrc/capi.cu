@@ -476,6 +476,35 @@ int ppocr_b200_deconv_nhwc(const void *x, const void *w, const void *bias,
                 "deconv");
 }
 
+int ppocr_b200_deconv_db_tail(const void *x, const void *w, const void *bias,
+                              int act, const void *w2, const void *bias2,
+                              int act2, void *y2, int batch, int h, int w_,
+                              int ci, cudaStream_t stream) {
+  g_error.clear();
+  if (!x || !w || !w2 || !y2 || batch < 0 || h <= 0 || w_ <= 0 || ci <= 0 || ci % 8)
+    return fail("invalid deconv_db_tail arguments");
+  // Packed first filter, repeated bias and the fp32 second filter in
+  // stream-ordered temporaries, released on the same stream.
+  const size_t wn = static_cast<size_t>(ci) * 4 * 64;
+  void *wp = nullptr, *bp = nullptr, *w2f = nullptr;
+  cudaError_t e = cudaMallocAsync(&wp, wn * 2, stream);
+  if (e == cudaSuccess && bias)
+    e = cudaMallocAsync(&bp, 4 * 64 * 2, stream);
+  if (e == cudaSuccess)
+    e = cudaMallocAsync(&w2f, 256 * sizeof(float), stream);
+  if (e == cudaSuccess)
+    e = deconv_pack(H(w), H(bias), static_cast<half *>(wp), static_cast<half *>(bp), ci, 64, 2, 2, stream);
+  if (e == cudaSuccess)
+    e = widen_f16(H(w2), static_cast<float *>(w2f), 256, stream);
+  if (e == cudaSuccess)
+    e = tc_deconv_db_tail(H(x), static_cast<half *>(wp), static_cast<half *>(bp), act,
+                          static_cast<float *>(w2f), H(bias2), act2, Hm(y2), batch, h, w_, ci, stream);
+  for (void *p : {wp, bp, w2f})
+    if (p)
+      cudaFreeAsync(p, stream);
+  return status(e, "deconv_db_tail");
+}
+
 int ppocr_b200_dwpw_block(const void *x, const void *w_dw, const void *b_dw,
                           int act_dw, const void *w_pw, const void *b_pw,
                           int act_pw, void *y, int batch, int h, int w_,

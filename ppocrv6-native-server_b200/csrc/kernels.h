@@ -76,6 +76,17 @@ cudaError_t halo_stream_conv(const half *x, const half *w, const ConvShape &s,
 cudaError_t tc_deconv(const half *x, const half *wpacked, const half *bias_rep,
                       half *y, int batch, int H, int W, int Ci, int Co, int KH,
                       int KW, int act, cudaStream_t stream);
+// The DB head's two transposed convs in one pass: tc_deconv (Ci -> 64, 2x2
+// stride 2, bias_rep / act) whose fp16 outputs feed, inside the epilogue, a
+// 2x2 stride-2 transposed conv 64 -> 1 (w2 fp32 [64][4] = [Ci][KH][KW],
+// bias2 fp16 or null, act2) written to y2 fp16 [batch][4 H][4 W];
+// bit-identical to tc_deconv followed by deconv_kxk, without the 64-channel
+// map in between.
+cudaError_t tc_deconv_db_tail(const half *x, const half *wpacked, const half *bias_rep, int act,
+                              const float *w2, const half *bias2, int act2, half *y2, int batch,
+                              int H, int W, int Ci, cudaStream_t stream);
+// dst[i] = float(src[i]) (filters kept as fp32 by a fused epilogue).
+cudaError_t widen_f16(const half *src, float *dst, int n, cudaStream_t stream);
 
 // Vocabulary projection with fused row argmax / softmax-max reduction:
 // logits[r][v] = hidden[r][:] . wt[v][:] + bias[v] (fp32), reduced over v to

@@ -74,6 +74,7 @@ void Runtime::add(const char *name, std::function<void()> f) {
   op_names.emplace_back(name);
   ops.push_back(std::move(f));
   last_dw_.op = -1;
+  last_dc_.op = -1;
 }
 
 void Runtime::reads(std::initializer_list<int> ids) {
@@ -90,9 +91,9 @@ void Runtime::reads(std::initializer_list<int> ids) {
     fused_.erase(fused_.begin() + static_cast<long>(i));
     op_names.resize(ops.size());
     ops[f.op] = f.dw_op;
-    op_names[f.op] = "depthwise";
+    op_names[f.op] = f.first_name;
     ops.insert(ops.begin() + f.op + 1, f.pw_op);
-    op_names.insert(op_names.begin() + f.op + 1, "gemm_epilogue");
+    op_names.insert(op_names.begin() + f.op + 1, f.second_name);
     for (auto &g : fused_)
       if (g.op > f.op)
         ++g.op;
@@ -217,13 +218,37 @@ void Runtime::deconv(int ai, int wi, int yi, Shape xs, Shape ws, Shape ys,
                       stream),
             "tc_deconv");
     });
+    if (Co == 64 && KH == 2 && KW == 2)
+      last_dc_ = {static_cast<int>(ops.size()) - 1, ai, yi, B, H, W, Ci, Co, KH, KW, activation, wp, bp};
     return;
   }
-  add("deconv", [=] {
+  auto plain = [=] {
     check(deconv_kxk(t[ai], t[wi], bias_id >= 0 ? t[bias_id] : nullptr, t[yi],
                      B, H, W, Ci, Co, KH, KW, activation, stream),
           "deconv");
-  });
+  };
+  const PendingDeconv d = last_dc_;
+  if (d.op >= 0 && d.op == static_cast<int>(ops.size()) - 1 && ai == d.yi && wi != d.yi &&
+      bias_id != d.yi && Ci == 64 && Co == 1 && KH == 2 && KW == 2 && B == d.B &&
+      H == 2 * d.H && W == 2 * d.W && is_constant(t[wi], wn) &&
+      (bias_id < 0 || is_constant(t[bias_id], 1))) {
+    // DB tail: the 64 -> 1 conv reduces the previous transposed conv's
+    // outputs inside its epilogue; the 64-channel map is not materialised.
+    reads({wi, bias_id});
+    float *w2 = static_cast<float *>(own(wn * sizeof(float)));
+    prepare.emplace_back([=] { check(widen_f16(t[wi], w2, static_cast<int>(wn), stream), "widen tail filter"); });
+    fused_.push_back({d.op, d.yi, ops[d.op], plain, "deconv_tc", "deconv"});
+    ops[d.op] = [=] {
+      check(tc_deconv_db_tail(t[d.ai], d.wp, d.bp, d.act, w2, bias_id >= 0 ? t[bias_id] : nullptr, activation,
+                              t[yi], d.B, d.H, d.W, d.Ci, stream),
+            "tc_deconv_db_tail");
+    };
+    op_names.resize(ops.size());
+    op_names[d.op] = "deconv_db_tail";
+    last_dc_.op = -1;
+    return;
+  }
+  add("deconv", plain);
 }
 
 void Runtime::gemm_epilogue(int ai, int wi, int bi, int ri, int yi, int rows,

@@ -146,11 +146,20 @@ private:
     int op = -1;
     int ai, wi, yi, bias_id, act, B, C, H, W, K;
   } last_dw_;
-  // Fused blocks whose depthwise output is not materialised.
+  // The tensor-core transposed conv recorded by the last add(), if it can
+  // lead a fused DB tail (a 64 -> 1 transposed conv reading only its output).
+  struct PendingDeconv {
+    int op = -1;
+    int ai, yi, B, H, W, Ci, Co, KH, KW, act;
+    half *wp, *bp;
+  } last_dc_;
+  // Fused pairs (depthwise + pointwise block, DB tail) whose intermediate
+  // tensor is not materialised; a later read of it splits the pair back.
   struct FusedDw {
     int op;
-    int virt; // tensor id of the depthwise output
-    std::function<void()> dw_op, pw_op;
+    int virt; // tensor id of the first op's output
+    std::function<void()> dw_op, pw_op; // the first and second op, unfused
+    const char *first_name = "depthwise", *second_name = "gemm_epilogue";
   };
   std::vector<FusedDw> fused_;
   std::vector<void *> owned_; // device buffers owned by this runtime

@@ -43,15 +43,21 @@ constexpr int kBK = 64;
 // partials, and the transposed-convolution store (each 64-column chunk is
 // one filter tap of KH x KW, written to its stride-interleaved output
 // pixels through a 5-D tensor map).
-enum Epi : int { kEpiStore = 0, kEpiVocab = 1, kEpiDeconv = 2 };
+// kEpiDbTail: the DB head's last two transposed convs in one pass -- the
+// 2x2 stride-2 conv to 64 channels computed on the tensor cores, its fp16
+// outputs (bias, activation) reduced on the spot by the following 2x2
+// stride-2 conv to one channel (+ bias, sigmoid), so the 64-channel map at
+// twice the resolution is never written.
+enum Epi : int { kEpiStore = 0, kEpiVocab = 1, kEpiDeconv = 2, kEpiDbTail = 3 };
 
 // Epilogue warps: 8 for stores, two per TMEM lane quarter: with 256-row
 // tiles each drains one M half, with 128-row tiles of 128 or 256 columns
 // each drains one column half (a lone tile's epilogue is a latency chain per
 // warp, so two warps per quarter halve it); 16 for the exp-heavy vocabulary
-// reduction (four warps per quarter, 64 columns each).
+// reduction (four warps per quarter, 64 columns each) and for the DB tail
+// (one 64-column chunk each: 100 us against 125 us with 8 warps at C5).
 template <int EPI, int MH> struct EpiWarps {
-  static constexpr int value = EPI == kEpiVocab ? 16 : 8;
+  static constexpr int value = EPI == kEpiVocab || EPI == kEpiDbTail ? 16 : 8;
 };
 static_assert(kEpiDeconv != kEpiVocab, "deconv uses the store warps");
 template <int EPI, int MH> constexpr int threads_for() {
@@ -79,6 +85,18 @@ struct Args {
   float *part_sum;
   int part_ld, calc_prob;
   int dec_co, dec_kw; // deconv: output channels, filter width
+  // conv mode with a plain 2-D A map: the pixel segments of every tile are
+  // consecutive rows of [pixels][Ci] (1x1 over the input pixels with no
+  // segment padding), loaded as MH boxes of 128 rows instead of one box per
+  // segment (transposed conv; fewer TMA issues for the producer thread)
+  int plain_a;
+  // kEpiDbTail: the second transposed conv (64 -> 1, 2x2 stride 2): filter
+  // as fp32 [64 channels][4 taps], fp16 bias (or null), activation, and its
+  // fp16 output [batch][4 H][4 W].
+  const float *tail_w;
+  const half *tail_bias;
+  half *tail_out;
+  int tail_act;
   int *err;
 };
 
@@ -310,11 +328,17 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
           issued |= 1u << stage;
           issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
           if (CONV) {
+            if (g.plain_a) {
 #pragma unroll
-            for (int s = 0; s < BM / 16; ++s)
-              if (s < nbox)
-                tma_load_4d(sa + (g.row_segs ? s * g.seg_len * 128 : s << box_shift), &mapA,
-                            &full[stage], cb * kBK, seg_x[s] + kw, seg_y[s] + kh, seg_n[s]);
+              for (int h = 0; h < MH; ++h)
+                tma_load_2d(sa + h * C::A_HALF, &mapA, &full[stage], cb * kBK, mb * BM + h * kBM);
+            } else {
+#pragma unroll
+              for (int s = 0; s < BM / 16; ++s)
+                if (s < nbox)
+                  tma_load_4d(sa + (g.row_segs ? s * g.seg_len * 128 : s << box_shift), &mapA,
+                              &full[stage], cb * kBK, seg_x[s] + kw, seg_y[s] + kh, seg_n[s]);
+            }
             tma_load_3d(sb, &mapB, &full[stage], cb * kBK, tap, nb * BN);
             if (++cb == g.kb_per_tap) {
               cb = 0;
@@ -400,7 +424,9 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
     // Epilogue warps: TMEM lane quarter is fixed by warp id modulo 4.
     const int q = warp & 3;          // TMEM lane quarter
     const int hf = (warp - 2) >> 2;  // vocab: column quarter; stores: M or column half
-    const int mh = MH == 2 ? hf : 0; // M half drained by this warp
+    // M half drained by this warp (DB tail: 16 warps, 4 per lane quarter,
+    // each one 64-column tap chunk of one M half)
+    const int mh = MH == 2 ? (EPI == kEpiDbTail ? (hf & 1) : hf) : 0;
     const int row_in_tile = mh * kBM + q * 32 + lane;
     const int ew = warp - 2;         // epilogue warp index (staging buffer)
     // Stores with 128-row tiles of 128 or 256 columns: the two warps of a
@@ -575,6 +601,105 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
                 continue;
               *reinterpret_cast<uint4 *>(e.out + orow * e.ldo + n0) =
                   epilogue8<ACT>(r + 8 * h, e, fetch_extra8(e, n0, g.N, orow));
+            }
+          }
+        }
+      } else if constexpr (EPI == kEpiDbTail) {
+        // This thread's row is input pixel (n, ih, iw); each 64-column chunk
+        // is tap (a, b) of the first transposed conv, i.e. the 64 channels
+        // of pixel (2 ih + a, 2 iw + b) at twice the resolution, exactly as
+        // the unfused layer would store them (epilogue8: fp16 rounding,
+        // bias, activation). The second conv maps that pixel to the 2 x 2
+        // block (2 (2 ih + a) + ki, 2 (2 iw + b) + kj) of the output with
+        // the arithmetic of its standalone kernel (deconv_group_kernel in
+        // detect.cu, eight lanes of eight channels): per group of eight
+        // channels one fp32 FMA chain in channel order, the eight group
+        // sums added as ((g0+g4) + (g2+g6)) + ((g1+g5) + (g3+g7)), then
+        // round to fp16, + bias, activation, fp16 store -- bit-identical.
+        const GemmEpilogue &e = g.epi;
+        // Tile rows are the input pixels in order (a plain [B*H*W][Ci]
+        // operand: two TMA boxes per k-block instead of one per segment).
+        const int m = mb * BM + row_in_tile;
+        const bool valid = m < g.M;
+        const int hw = g.OH * g.OW;
+        const int n = m / hw, ih = (m - n * hw) / g.OW, iw = m - n * hw - ih * g.OW;
+        const long long OW2 = 4LL * g.OW;
+        const float tb = g.tail_bias ? __half2float(*g.tail_bias) : 0.f;
+        // The (M half, 64-column chunk) pairs of the tile are dealt to the
+        // warps of each TMEM lane quarter in turn; a warp's pairs share its
+        // M half. A chunk is one tap of the first conv.
+        constexpr int kWq = EpiWarps<EPI, MH>::value / 4;
+        // Per warp, in its 2 KB of the (otherwise unused) store-staging
+        // smem, once: the second filter, fp32 [64 channels][4 taps], read as
+        // broadcast 16-byte loads with taps (0, 1) and (2, 3) as packed
+        // pairs, and the first conv's bias for all N = 256 columns (fp16 -0
+        // when absent, as fetch_extra8 gives).
+        float *wsm = reinterpret_cast<float *>(epi_smem + ew * 2048);
+        uint4 *bsm = reinterpret_cast<uint4 *>(epi_smem + ew * 2048 + 1024);
+        if (it == 0) {
+          for (int i = lane; i < 256; i += 32)
+            wsm[i] = g.tail_w[i];
+          bsm[lane] = e.bias ? *reinterpret_cast<const uint4 *>(e.bias + 8 * lane)
+                             : make_uint4(0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u);
+          __syncwarp();
+        }
+#pragma unroll 1
+        for (int pr = hf; pr < MH * (BN / 64); pr += kWq) {
+          const int c = pr / MH * 64;
+          const uint4 *bchunk = bsm + (n_base + c) / 8;
+          uint64_t p01[8], p23[8];
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t r[32];
+            tmem_ld16(taddr + c + 32 * half, *reinterpret_cast<uint32_t(*)[16]>(r));
+            tmem_ld16(taddr + c + 32 * half + 16, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
+            tmem_ld_wait();
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int gi = half * 4 + k;
+              Extra8 x;
+              x.bias = bchunk[gi];
+              x.res = make_uint4(0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u);
+              const uint4 hv = epilogue8<ACT>(r + 8 * k, e, x);
+              const half2 *h2 = reinterpret_cast<const half2 *>(&hv);
+              uint64_t a01 = 0, a23 = 0; // +0, +0 in both lanes
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 f = __half22float2(h2[j]);
+                const ulonglong2 w0 = *reinterpret_cast<const ulonglong2 *>(wsm + (gi * 8 + 2 * j) * 4);
+                const ulonglong2 w1 = *reinterpret_cast<const ulonglong2 *>(wsm + (gi * 8 + 2 * j + 1) * 4);
+                ffma2_bcast(a01, f.x, w0.x);
+                ffma2_bcast(a23, f.x, w0.y);
+                ffma2_bcast(a01, f.y, w1.x);
+                ffma2_bcast(a23, f.y, w1.y);
+              }
+              p01[gi] = a01;
+              p23[gi] = a23;
+            }
+          }
+          if (valid) {
+            float sum[4];
+            sum[0] = ((lo_f32(p01[0]) + lo_f32(p01[4])) + (lo_f32(p01[2]) + lo_f32(p01[6]))) +
+                     ((lo_f32(p01[1]) + lo_f32(p01[5])) + (lo_f32(p01[3]) + lo_f32(p01[7])));
+            sum[1] = ((hi_f32(p01[0]) + hi_f32(p01[4])) + (hi_f32(p01[2]) + hi_f32(p01[6]))) +
+                     ((hi_f32(p01[1]) + hi_f32(p01[5])) + (hi_f32(p01[3]) + hi_f32(p01[7])));
+            sum[2] = ((lo_f32(p23[0]) + lo_f32(p23[4])) + (lo_f32(p23[2]) + lo_f32(p23[6]))) +
+                     ((lo_f32(p23[1]) + lo_f32(p23[5])) + (lo_f32(p23[3]) + lo_f32(p23[7])));
+            sum[3] = ((hi_f32(p23[0]) + hi_f32(p23[4])) + (hi_f32(p23[2]) + hi_f32(p23[6]))) +
+                     ((hi_f32(p23[1]) + hi_f32(p23[5])) + (hi_f32(p23[3]) + hi_f32(p23[7])));
+            const int tap = (n_base + c) / g.dec_co;
+            const int a = tap / g.dec_kw, b = tap - a * g.dec_kw;
+#pragma unroll
+            for (int ki = 0; ki < 2; ++ki) {
+              float v0 = round_half(sum[2 * ki]), v1 = round_half(sum[2 * ki + 1]);
+              if (g.tail_bias) {
+                v0 += tb;
+                v1 += tb;
+              }
+              const long long row = 4LL * ih + 2 * a + ki;
+              *reinterpret_cast<half2 *>(g.tail_out + (static_cast<long long>(n) * 4 * g.OH + row) * OW2 +
+                                         4LL * iw + 2 * b) =
+                  __floats2half2_rn(apply_act(v0, g.tail_act), apply_act(v1, g.tail_act));
             }
           }
         }
@@ -1068,11 +1193,25 @@ cudaError_t tc_conv(const half *x, const half *w, const ConvShape &s,
   return dispatch_bn<true, kEpiStore>(bn, two, ma, mb, mc, g, stream);
 }
 
-cudaError_t tc_deconv(const half *x, const half *wpacked, const half *bias_rep,
-                      half *y, int batch, int H, int W, int Ci, int Co, int KH,
-                      int KW, int act, cudaStream_t stream) {
+namespace {
+// The second conv of a fused DB tail (kEpiDbTail); null for a plain deconv.
+struct DbTail {
+  const float *w;    // fp32 [64][4]
+  const half *bias;  // or null
+  half *out;         // fp16 [batch][4 H][4 W]
+  int act;
+};
+
+cudaError_t deconv_impl(const half *x, const half *wpacked, const half *bias_rep,
+                        half *y, int batch, int H, int W, int Ci, int Co, int KH,
+                        int KW, int act, const DbTail *tail, cudaStream_t stream) {
   if (batch <= 0 || H <= 0 || W <= 0)
     return cudaSuccess;
+  if (tail && (Co != 64 || KH != 2 || KW != 2 || !tail->w || !tail->out ||
+               (reinterpret_cast<uintptr_t>(tail->out) & 3)))
+    return cudaErrorInvalidValue;
+  if (tail)
+    y = tail->out; // the 64-channel map is not written; the store map goes unused
   const int N = KH * KW * Co;
   if (Co % 64 || Ci % 8 || !aligned16(x) || !aligned16(wpacked) ||
       !aligned16(y) || (bias_rep && !aligned16(bias_rep)))
@@ -1114,6 +1253,16 @@ cudaError_t tc_deconv(const half *x, const half *wpacked, const half *bias_rep,
       !encode(&mc, y, 5, dc, scs, bc))
     return cudaErrorInvalidValue;
   Args g{};
+  if (!tail && W % static_cast<int>(seg) == 0 && static_cast<long long>(batch) * H * W <= 0x7fffffffLL) {
+    // No segment padding: the tiles' pixel rows are consecutive rows of
+    // [pixels][Ci]; load them as 128-row boxes.
+    cuuint64_t pa[2] = {static_cast<cuuint64_t>(Ci), static_cast<cuuint64_t>(batch) * H * W};
+    cuuint64_t psa[1] = {static_cast<cuuint64_t>(Ci) * 2};
+    cuuint32_t pba[2] = {kBK, kBM};
+    if (!encode(&ma, x, 2, pa, psa, pba))
+      return cudaErrorInvalidValue;
+    g.plain_a = 1;
+  }
   g.seg_log2 = seg_log2;
   g.Wseg = (W + static_cast<int>(seg) - 1) / static_cast<int>(seg);
   g.OH = H;
@@ -1133,6 +1282,36 @@ cudaError_t tc_deconv(const half *x, const half *wpacked, const half *bias_rep,
   g.dec_co = Co;
   g.dec_kw = KW;
   g.err = device_error_word();
+  if (tail) {
+    // A pointwise GEMM over the input pixels: plain 2-D operand maps (the
+    // pixel-segment maps above only serve the strided stores of a plain
+    // deconv, which the fused tail does not make).
+    const long long pixels = static_cast<long long>(batch) * H * W;
+    if (pixels > 0x7fffffffLL)
+      return cudaErrorInvalidValue;
+    const int bt = two ? 128 : 256;
+    cuuint64_t pa[2] = {static_cast<cuuint64_t>(Ci), static_cast<cuuint64_t>(pixels)};
+    cuuint64_t psa[1] = {static_cast<cuuint64_t>(Ci) * 2};
+    cuuint32_t pba[2] = {kBK, kBM};
+    cuuint64_t pb[2] = {static_cast<cuuint64_t>(Ci), static_cast<cuuint64_t>(N)};
+    cuuint64_t psb[1] = {static_cast<cuuint64_t>(Ci) * 2};
+    cuuint32_t pbb[2] = {kBK, static_cast<cuuint32_t>(bt)};
+    CUtensorMap pma, pmb;
+    if (!encode(&pma, x, 2, pa, psa, pba) || !encode(&pmb, wpacked, 2, pb, psb, pbb))
+      return cudaErrorInvalidValue;
+    g.M = static_cast<int>(pixels);
+    g.mt = (g.M + (two ? 2 * kBM : kBM) - 1) / (two ? 2 * kBM : kBM);
+    g.nt = N / bt;
+    g.tail_w = tail->w;
+    g.tail_bias = tail->bias;
+    g.tail_out = tail->out;
+    g.tail_act = tail->act;
+    if (two)
+      return act == kActRelu ? launch<128, false, kEpiDbTail, kActRelu, 2>(pma, pmb, pma, g, stream)
+                             : launch<128, false, kEpiDbTail, -1, 2>(pma, pmb, pma, g, stream);
+    return act == kActRelu ? launch<256, false, kEpiDbTail, kActRelu>(pma, pmb, pma, g, stream)
+                           : launch<256, false, kEpiDbTail, -1>(pma, pmb, pma, g, stream);
+  }
   if (two)
     return act == kActRelu ? launch<128, true, kEpiDeconv, kActRelu, 2>(ma, mb, mc, g, stream)
                            : launch<128, true, kEpiDeconv, -1, 2>(ma, mb, mc, g, stream);
@@ -1147,6 +1326,33 @@ cudaError_t tc_deconv(const half *x, const half *wpacked, const half *bias_rep,
     return act == kActRelu ? launch<256, true, kEpiDeconv, kActRelu>(ma, mb, mc, g, stream)
                            : launch<256, true, kEpiDeconv, -1>(ma, mb, mc, g, stream);
   }
+}
+
+__global__ void widen_kernel(const half *__restrict__ src, float *__restrict__ dst, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n)
+    dst[i] = __half2float(src[i]);
+}
+} // namespace
+
+cudaError_t tc_deconv(const half *x, const half *wpacked, const half *bias_rep,
+                      half *y, int batch, int H, int W, int Ci, int Co, int KH,
+                      int KW, int act, cudaStream_t stream) {
+  return deconv_impl(x, wpacked, bias_rep, y, batch, H, W, Ci, Co, KH, KW, act, nullptr, stream);
+}
+
+cudaError_t tc_deconv_db_tail(const half *x, const half *wpacked, const half *bias_rep, int act,
+                              const float *w2, const half *bias2, int act2, half *y2, int batch,
+                              int H, int W, int Ci, cudaStream_t stream) {
+  const DbTail tail{w2, bias2, y2, act2};
+  return deconv_impl(x, wpacked, bias_rep, nullptr, batch, H, W, Ci, 64, 2, 2, act, &tail, stream);
+}
+
+cudaError_t widen_f16(const half *src, float *dst, int n, cudaStream_t stream) {
+  if (n <= 0)
+    return cudaSuccess;
+  widen_kernel<<<(n + 255) / 256, 256, 0, stream>>>(src, dst, n);
+  return cudaGetLastError();
 }
 
 cudaError_t tc_vocab_partials(const half *hidden, int rows, int H,

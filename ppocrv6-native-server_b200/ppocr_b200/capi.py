@@ -61,6 +61,7 @@ SIGNATURES = {
     "ppocr_b200_binary_flat": (I, [V, V, V, L, I, I, I, I, I, V]),
     "ppocr_b200_mean_nhwc": (I, [V, V, I, I, I, V]),
     "ppocr_b200_deconv_nhwc": (I, [V, V, V, V, I, I, I, I, I, I, I, I, V]),
+    "ppocr_b200_deconv_db_tail": (I, [V, V, V, I, V, V, I, V, I, I, I, I, V]),
     "ppocr_b200_binarize": (I, [V, V, S, F, V]),
     "ppocr_b200_dwpw_block": (I, [V, V, V, I, V, V, I, V, I, I, I, I, I, I, V]),
     "ppocr_b200_db_components_workspace": (S, [I, I, I, I]),

@@ -460,6 +460,48 @@ def test_deconv(native, cuda, batch, h, w, ci, co, act, bias):
     assert_close(host(y), L.deconv_kxk(x, wt, b, act), what=f"deconv {batch}x{h}x{w}x{ci}->{co}")
 
 
+DB_TAIL_CASES = [
+    # batch, h, w, ci, act, act2, bias: the DB head's two transposed convs
+    # (ci -> 64 -> 1, 2x2 stride 2) fused, against the two separate ops
+    (1, 240, 240, 64, 1, 4, True),    # the C5 head at one page: 256-row x 128-column tiles
+    (2, 32, 32, 64, 1, 4, True),      # few tiles: 128-row x 256-column tiles, column-split epilogue
+    (3, 17, 50, 64, 1, 4, False),     # ragged 16-pixel segments (width 50), no biases
+    (1, 9, 64, 128, 0, 0, True),      # Ci 128 (two k-blocks), no activations, 32-pixel segments
+    (2, 6, 10, 64, 2, 4, True),       # runtime activation switch (GELU) in the first conv
+]
+
+
+@pytest.mark.parametrize("batch,h,w,ci,act,act2,bias", DB_TAIL_CASES)
+def test_deconv_db_tail(native, cuda, batch, h, w, ci, act, act2, bias):
+    """Fused DB tail bit-identical to deconv(ci -> 64) then deconv(64 -> 1),
+    and within the fp16 bar of the oracle."""
+    r = rng(80 + h + w + ci)
+    x = f16(r.uniform(-1, 1, (batch, h, w, ci)))
+    w1 = f16(r.standard_normal((ci, 2, 2, 64)) * np.sqrt(2.0 / (4 * ci)))
+    b1 = f16(r.normal(0, 0.1, 64)) if bias else None
+    w2 = f16(r.standard_normal((64, 2, 2, 1)) * np.sqrt(2.0 / 256))
+    b2 = f16(r.normal(0, 0.1, 1)) if bias else None
+    dx, dw1, dw2 = dev(x), dev(w1), dev(w2)
+    db1, db2 = (dev(b1), dev(b2)) if bias else (None, None)
+    mid = torch.empty(batch, 2 * h, 2 * w, 64, dtype=torch.float16, device=cuda)
+    want = torch.full((batch, 4 * h, 4 * w, 1), float("nan"), dtype=torch.float16, device=cuda)
+    got = torch.full((batch, 4 * h, 4 * w, 1), float("nan"), dtype=torch.float16, device=cuda)
+    s = stream_handle()
+    assert native.ppocr_b200_deconv_nhwc(ptr(dx), ptr(dw1), ptr(db1) if bias else None, ptr(mid), batch, h, w, ci,
+                                         64, 2, 2, act, s) == 0, native.ppocr_b200_last_error()
+    assert native.ppocr_b200_deconv_nhwc(ptr(mid), ptr(dw2), ptr(db2) if bias else None, ptr(want), batch,
+                                         2 * h, 2 * w, 64, 1, 2, 2, act2, s) == 0, native.ppocr_b200_last_error()
+    for _ in range(2):  # twice: the same bits on a repeat
+        assert native.ppocr_b200_deconv_db_tail(ptr(dx), ptr(dw1), ptr(db1) if bias else None, act, ptr(dw2),
+                                                ptr(db2) if bias else None, act2, ptr(got), batch, h, w, ci,
+                                                s) == 0, native.ppocr_b200_last_error()
+        sync()
+        check_device_error(native)
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    ref = L.deconv_kxk(L.deconv_kxk(x, w1, b1, act), w2, b2, act2)
+    assert_close(host(got), ref, what=f"db tail {batch}x{h}x{w}x{ci}")
+
+
 @pytest.mark.parametrize("kh,kw,ci", [(1, 2, 64), (2, 1, 128), (1, 1, 64)])
 def test_deconv_fewer_taps(native, cuda, kh, kw, ci):
     """Kernel == stride with fewer than four outputs per input pixel: the
