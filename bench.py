@@ -339,7 +339,7 @@ def b200_arm(args):
     op_names = rec.model.lib.op_names(rec.model.handle)
     # graph ops after the leading NCHW->NHWC transpose (replaced by a staging
     # copy, no kernel) + vocabulary projection (2 kernels) + collapse (1)
-    launches_per_step = len(op_names) - 1 + 2 + 1
+    launches_per_step = sum(1 for n in op_names[1:] if n != "fused") + 2 + 1
 
     # ---- device-resident timing
     for _ in range(args.warmup):
@@ -792,7 +792,8 @@ def measure_pages(dev, runs, warm, flush, with_cpu=False, seed_offset=0):
     out["runs"] = runs
     # detector ops after the staged transpose, binarize, recognizer ops
     # after its staged transpose, vocabulary projection (2), collapse (1)
-    out["launches_per_run"] = (len(names) - 1) + 1 + (len(pp.rec.model.lib.op_names(pp.rec.model.handle)) - 1) + 3
+    launched = lambda ns: sum(1 for n in ns[1:] if n != "fused")  # noqa: E731
+    out["launches_per_run"] = launched(names) + 1 + launched(pp.rec.model.lib.op_names(pp.rec.model.handle)) + 3
     out["clocks_obj"] = clocks
     out["clocks"] = clocks.summary()
     out["cpu_baseline"] = _cpu_c5() if with_cpu else None

@@ -34,6 +34,11 @@ struct GemmEpilogue {
   half *out = nullptr; // [rows][ldo]
   int ldo = 0;
   int act = 0;
+  // Nearest 2x upsampled residual (plain GEMMs): the rows are the pixels of
+  // [batch][2 res_h][2 res_w] images and the residual is [batch][res_h]
+  // [res_w][ldr]; output pixel (y, x) adds residual pixel (y / 2, x / 2) --
+  // the FPN's resize_nearest_add_nhwc folded into the lateral 1x1 conv.
+  int res_up = 0, res_h = 0, res_w = 0;
 };
 // Plain GEMM: out[M][N] = A[M][K] (row stride lda) x W[N][K]^T (row stride ldw).
 cudaError_t tc_gemm(const half *A, int M, int K, int lda, const half *W, int N,

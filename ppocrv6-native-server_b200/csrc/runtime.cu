@@ -75,6 +75,7 @@ void Runtime::add(const char *name, std::function<void()> f) {
   ops.push_back(std::move(f));
   last_dw_.op = -1;
   last_dc_.op = -1;
+  last_gemm_.op = -1;
 }
 
 void Runtime::reads(std::initializer_list<int> ids) {
@@ -86,18 +87,22 @@ void Runtime::reads(std::initializer_list<int> ids) {
       ++i;
       continue;
     }
-    // Split: the depthwise launch (writing its output) then the GEMM.
+    // Split: the first op (writing the intermediate) then the second, in
+    // the pair's two slots (the second held an empty placeholder).
     const FusedDw f = fused_[i];
     fused_.erase(fused_.begin() + static_cast<long>(i));
     op_names.resize(ops.size());
     ops[f.op] = f.dw_op;
     op_names[f.op] = f.first_name;
-    ops.insert(ops.begin() + f.op + 1, f.pw_op);
-    op_names.insert(op_names.begin() + f.op + 1, f.second_name);
-    for (auto &g : fused_)
-      if (g.op > f.op)
-        ++g.op;
+    ops[f.op + 1] = f.pw_op;
+    op_names[f.op + 1] = f.second_name;
   }
+}
+
+void Runtime::add_fused_placeholder() {
+  // Keeps one op slot per graph operator: the fused pair's second slot
+  // launches nothing (and is reported as "fused") unless the pair splits.
+  add("fused", [] {});
 }
 
 namespace pb2 {
@@ -245,7 +250,7 @@ void Runtime::deconv(int ai, int wi, int yi, Shape xs, Shape ws, Shape ys,
     };
     op_names.resize(ops.size());
     op_names[d.op] = "deconv_db_tail";
-    last_dc_.op = -1;
+    add_fused_placeholder();
     return;
   }
   add("deconv", plain);
@@ -278,11 +283,13 @@ void Runtime::gemm_epilogue(int ai, int wi, int bi, int ri, int yi, int rows,
     };
     op_names.resize(ops.size());
     op_names[d.op] = "dwpw_block";
-    last_dw_.op = -1;
+    add_fused_placeholder();
     return;
   }
   reads({ai, wi, bi, ri});
   add("gemm_epilogue", pw);
+  if (ri < 0)
+    last_gemm_ = {static_cast<int>(ops.size()) - 1, ai, wi, bi, yi, rows, ci, co, activation};
 }
 
 void Runtime::matmul(int a, int b, int y, int batches, int m, int n, int k) {
@@ -528,12 +535,41 @@ void Runtime::upsample_concat_nhwc(std::vector<int> srcs, int y, std::vector<Sha
 void Runtime::resize_nearest_add_nhwc(int a, int addend, int y, Shape xs,
                                       Shape ys, float sh, float sw) {
   reads({a, addend});
-  add("resize_add_nhwc", [=] {
+  auto plain = [=] {
     check(::pb2::resize_nearest_nhwc(t[a], t[addend], t[y], xs[0], xs[1],
                                      xs[2], xs[3], ys[2], ys[3], sh, sw,
                                      stream),
           "resize_add_nhwc");
-  });
+  };
+  const PendingGemm m = last_gemm_;
+  const int B = xs[0], C = xs[1], H = xs[2], W = xs[3];
+  if (m.op >= 0 && m.op == static_cast<int>(ops.size()) - 1 && addend == m.yi && a != m.yi && a != m.ai &&
+      sh == 2.f && sw == 2.f && ys[0] == B && ys[1] == C && ys[2] == 2 * H && ys[3] == 2 * W &&
+      m.co == C && static_cast<long long>(m.rows) == 4LL * B * H * W && C % 8 == 0) {
+    // FPN step folded into the lateral 1x1 conv that produced the addend:
+    // its epilogue adds the nearest-upsampled coarser map and writes y (the
+    // same fp16 rounding points: round(lateral) + up(a), rounded).
+    reads({a});
+    fused_.push_back({m.op, m.yi, ops[m.op], plain, "gemm_epilogue", "resize_add_nhwc"});
+    ops[m.op] = [=] {
+      GemmEpilogue e;
+      e.bias = m.bi >= 0 ? t[m.bi] : nullptr;
+      e.residual = t[a];
+      e.ldr = C;
+      e.res_up = 1;
+      e.res_h = H;
+      e.res_w = W;
+      e.out = t[y];
+      e.ldo = m.co;
+      e.act = m.act;
+      check(tc_gemm(t[m.ai], m.rows, m.ci, m.ci, t[m.wi], m.co, m.ci, e, stream), "tc_gemm");
+    };
+    op_names.resize(ops.size());
+    op_names[m.op] = "gemm_resize_add";
+    add_fused_placeholder();
+    return;
+  }
+  add("resize_add_nhwc", plain);
 }
 
 void Runtime::attention(int qkv, int y, int lines, int seq, int heads,

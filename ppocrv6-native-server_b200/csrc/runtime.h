@@ -153,7 +153,14 @@ private:
     int ai, yi, B, H, W, Ci, Co, KH, KW, act;
     half *wp, *bp;
   } last_dc_;
-  // Fused pairs (depthwise + pointwise block, DB tail) whose intermediate
+  // The last gemm_epilogue without a residual, which an FPN resize-add of
+  // its output can fold into (upsampled residual in the GEMM epilogue).
+  struct PendingGemm {
+    int op = -1;
+    int ai, wi, bi, yi, rows, ci, co, act;
+  } last_gemm_;
+  // Fused pairs (depthwise + pointwise block, DB tail, lateral conv + FPN
+  // resize-add) whose intermediate
   // tensor is not materialised; a later read of it splits the pair back.
   struct FusedDw {
     int op;
@@ -166,4 +173,5 @@ private:
   void *own(size_t bytes);
   bool is_constant(const Scalar *p, size_t elements) const;
   void add(const char *name, std::function<void()> f);
+  void add_fused_placeholder();
 };

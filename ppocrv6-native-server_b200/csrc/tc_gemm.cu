@@ -467,6 +467,14 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
         if (m < g.M)
           orow = m;
       }
+      // Residual row of this output row (the row itself, or its nearest 2x
+      // source pixel for an upsampled residual).
+      long long rrow = orow;
+      if (!CONV && g.epi.res_up && orow >= 0) {
+        const long long ow2 = 2LL * g.epi.res_w, img = 2LL * g.epi.res_h * ow2;
+        const long long n = orow / img, rem = orow - n * img, y = rem / ow2, x = rem - y * ow2;
+        rrow = (n * g.epi.res_h + (y >> 1)) * g.epi.res_w + (x >> 1);
+      }
       const int n_base = nb * BN;
       // Bias and residual of this warp's first 64-column chunk are fetched
       // before the accumulator wait, each later chunk's while the previous
@@ -477,7 +485,7 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
         if (drains) {
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            nx[j] = fetch_extra8(g.epi, n_base + c_lo + 8 * j, g.N, orow);
+            nx[j] = fetch_extra8(g.epi, n_base + c_lo + 8 * j, g.N, rrow);
         }
       }
       if (!mbar_wait(&tfull[acc], acc_phase, abort)) {
@@ -550,7 +558,7 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
           if (c + 64 < c_hi) {
 #pragma unroll
             for (int j = 0; j < 8; ++j)
-              nx[j] = fetch_extra8(e, n_base + c + 64 + 8 * j, g.N, orow);
+              nx[j] = fetch_extra8(e, n_base + c + 64 + 8 * j, g.N, rrow);
           }
           // The store issued from this warp's buffer for the previous chunk
           // must have read its source before the buffer is overwritten.
@@ -600,7 +608,7 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
               if (n0 + 8 > g.N)
                 continue;
               *reinterpret_cast<uint4 *>(e.out + orow * e.ldo + n0) =
-                  epilogue8<ACT>(r + 8 * h, e, fetch_extra8(e, n0, g.N, orow));
+                  epilogue8<ACT>(r + 8 * h, e, fetch_extra8(e, n0, g.N, rrow));
             }
           }
         }
@@ -1021,6 +1029,9 @@ cudaError_t tc_gemm(const half *A, int M, int K, int lda, const half *W, int N,
       !aligned16(W) || !aligned16(epi.out) ||
       (epi.bias && !aligned16(epi.bias)) ||
       (epi.residual && (!aligned16(epi.residual) || epi.ldr % 8)))
+    return cudaErrorInvalidValue;
+  if (epi.res_up && (!epi.residual || epi.res_h <= 0 || epi.res_w <= 0 ||
+                     static_cast<long long>(M) % (4LL * epi.res_h * epi.res_w) != 0))
     return cudaErrorInvalidValue;
   int bn = pick_bn(N);
   const int num_kb = (K + kBK - 1) / kBK;

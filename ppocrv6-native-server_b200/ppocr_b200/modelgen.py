@@ -574,6 +574,17 @@ def build_neck(spec: dict, batch: int, seed: int, xv: bool = False):
     return g, x
 
 
+def _move_op_before(g: Graph, src_out: int, dst_out: int) -> None:
+    """Moves the op writing src_out (and its layer record) to just before the
+    op writing dst_out; ops and layers are aligned one to one here."""
+    assert len(g.ops) == len(g.layers)
+    i = next(k for k, op in enumerate(g.ops) if op[1] == src_out)
+    op, layer = g.ops.pop(i), g.layers.pop(i)
+    j = next(k for k, o in enumerate(g.ops) if o[1] == dst_out)
+    g.ops.insert(j, op)
+    g.layers.insert(j, layer)
+
+
 def build_detector(spec: dict, batch: int, size: int, seed: int, fused_fpn_tail: bool = True,
                    xv: bool = False):
     """Backbone at strides 2..32 + FPN(256) + DB head -> sigmoid map [B,1,S,S]."""
@@ -615,6 +626,13 @@ def build_detector(spec: dict, batch: int, size: int, seed: int, fused_fpn_tail:
              f"{flit(sh)},{flit(sw)});",
              {"op": "resize_add", "in": td[i + 1], "add": lat[i], "out": y, "scale": [sh, sw]})
         td[i] = y
+    if not xv:
+        # Each lateral 1x1 conv runs right before the resize-add that reads
+        # it (same weights, drawn in level order above), so the Runtime can
+        # fold the add into the conv's epilogue (the exporter keeps its own
+        # order in the `_xv` twin).
+        for i in range(len(lat) - 1):
+            _move_op_before(g, lat[i], td[i])
     outs = [bd.conv_bn_act(t, fpn // 4, 3, act="none") for t in td]
     # Upsample each level to the finest and concatenate channels. The
     # exporter writes this as one Resize per level and a chain of Concats;
