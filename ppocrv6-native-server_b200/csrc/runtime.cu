@@ -64,6 +64,14 @@ void *Runtime::own(size_t bytes) {
   return p;
 }
 
+// A fused pair reads the first op's inputs and writes the second op's
+// output in one kernel; the arena planner may have given that output the
+// space of a first-op input that dies after the first op, so fusion
+// requires the two ranges to be disjoint.
+static bool disjoint(const Scalar *a, size_t na, const Scalar *b, size_t nb) {
+  return a + na <= b || b + nb <= a;
+}
+
 bool Runtime::is_constant(const Scalar *p, size_t elements) const {
   return weights && weight_elements && p >= weights &&
          p + elements <= weights + weight_elements;
@@ -236,7 +244,9 @@ void Runtime::deconv(int ai, int wi, int yi, Shape xs, Shape ws, Shape ys,
   if (d.op >= 0 && d.op == static_cast<int>(ops.size()) - 1 && ai == d.yi && wi != d.yi &&
       bias_id != d.yi && Ci == 64 && Co == 1 && KH == 2 && KW == 2 && B == d.B &&
       H == 2 * d.H && W == 2 * d.W && is_constant(t[wi], wn) &&
-      (bias_id < 0 || is_constant(t[bias_id], 1))) {
+      (bias_id < 0 || is_constant(t[bias_id], 1)) &&
+      disjoint(t[d.ai], static_cast<size_t>(d.B) * d.H * d.W * d.Ci, t[yi],
+               static_cast<size_t>(B) * 4 * H * W)) {
     // DB tail: the 64 -> 1 conv reduces the previous transposed conv's
     // outputs inside its epilogue; the 64-channel map is not materialised.
     reads({wi, bias_id});
@@ -272,7 +282,8 @@ void Runtime::gemm_epilogue(int ai, int wi, int bi, int ri, int yi, int rows,
   };
   const PendingDw d = last_dw_;
   if (d.op >= 0 && d.op == static_cast<int>(ops.size()) - 1 && ai == d.yi && ri < 0 && wi != d.yi &&
-      bi != d.yi && rows == d.B * d.H * d.W && ci == d.C && dwpw_supported(d.C, d.K, co)) {
+      bi != d.yi && rows == d.B * d.H * d.W && ci == d.C && dwpw_supported(d.C, d.K, co) &&
+      disjoint(t[d.ai], static_cast<size_t>(rows) * ci, t[yi], static_cast<size_t>(rows) * co)) {
     // Fused depthwise + pointwise block: the depthwise output stays on chip.
     reads({wi, bi});
     fused_.push_back({d.op, d.yi, ops[d.op], pw});
@@ -545,7 +556,9 @@ void Runtime::resize_nearest_add_nhwc(int a, int addend, int y, Shape xs,
   const int B = xs[0], C = xs[1], H = xs[2], W = xs[3];
   if (m.op >= 0 && m.op == static_cast<int>(ops.size()) - 1 && addend == m.yi && a != m.yi && a != m.ai &&
       sh == 2.f && sw == 2.f && ys[0] == B && ys[1] == C && ys[2] == 2 * H && ys[3] == 2 * W &&
-      m.co == C && static_cast<long long>(m.rows) == 4LL * B * H * W && C % 8 == 0) {
+      m.co == C && static_cast<long long>(m.rows) == 4LL * B * H * W && C % 8 == 0 &&
+      disjoint(t[m.ai], static_cast<size_t>(m.rows) * m.ci, t[y], static_cast<size_t>(m.rows) * m.co) &&
+      disjoint(t[a], static_cast<size_t>(B) * H * W * C, t[y], static_cast<size_t>(m.rows) * m.co)) {
     // FPN step folded into the lateral 1x1 conv that produced the addend:
     // its epilogue adds the nearest-upsampled coarser map and writes y (the
     // same fp16 rounding points: round(lateral) + up(a), rounded).
