@@ -403,18 +403,6 @@ __device__ __forceinline__ void ffma2(float2 &acc, float2 a, float2 b) {
   acc.x = __uint_as_float(static_cast<uint32_t>(d));
   acc.y = __uint_as_float(static_cast<uint32_t>(d >> 32));
 }
-// The same on packed registers: acc (lanes lo, hi) += (x, x) * w (lanes lo,
-// hi), for FMA chains kept in 64-bit register pairs (no repacking between
-// steps); each lane rounds like fmaf.
-__device__ __forceinline__ void ffma2_bcast(uint64_t &acc, float x, uint64_t w) {
-  asm("{.reg .b64 xx;\n\t"
-      "mov.b64 xx, {%1, %1};\n\t"
-      "fma.rn.f32x2 %0, xx, %2, %0;}"
-      : "+l"(acc)
-      : "f"(x), "l"(w));
-}
-__device__ __forceinline__ float lo_f32(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
-__device__ __forceinline__ float hi_f32(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
 // 2^x on the special-function unit (approximate, subnormal results flushed).
 // exp(v - m) is computed as ex2(v * log2(e) - m * log2(e)).
 __device__ __forceinline__ float ex2_ftz(float x) {

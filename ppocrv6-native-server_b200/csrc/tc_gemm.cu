@@ -639,9 +639,8 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
         constexpr int kWq = EpiWarps<EPI, MH>::value / 4;
         // Per warp, in its 2 KB of the (otherwise unused) store-staging
         // smem, once: the second filter, fp32 [64 channels][4 taps], read as
-        // broadcast 16-byte loads with taps (0, 1) and (2, 3) as packed
-        // pairs, and the first conv's bias for all N = 256 columns (fp16 -0
-        // when absent, as fetch_extra8 gives).
+        // broadcast 16-byte loads, and the first conv's bias for all N = 256
+        // columns (fp16 -0 when absent, as fetch_extra8 gives).
         float *wsm = reinterpret_cast<float *>(epi_smem + ew * 2048);
         uint4 *bsm = reinterpret_cast<uint4 *>(epi_smem + ew * 2048 + 1024);
         if (it == 0) {
@@ -655,7 +654,7 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
         for (int pr = hf; pr < MH * (BN / 64); pr += kWq) {
           const int c = pr / MH * 64;
           const uint4 *bchunk = bsm + (n_base + c) / 8;
-          uint64_t p01[8], p23[8];
+          float ps[4][8]; // group sums per output tap
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
             uint32_t r[32];
@@ -670,31 +669,32 @@ __global__ void __launch_bounds__(threads_for<EPI, MH>(), 1)
               x.res = make_uint4(0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u);
               const uint4 hv = epilogue8<ACT>(r + 8 * k, e, x);
               const half2 *h2 = reinterpret_cast<const half2 *>(&hv);
-              uint64_t a01 = 0, a23 = 0; // +0, +0 in both lanes
+              float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 const float2 f = __half22float2(h2[j]);
-                const ulonglong2 w0 = *reinterpret_cast<const ulonglong2 *>(wsm + (gi * 8 + 2 * j) * 4);
-                const ulonglong2 w1 = *reinterpret_cast<const ulonglong2 *>(wsm + (gi * 8 + 2 * j + 1) * 4);
-                ffma2_bcast(a01, f.x, w0.x);
-                ffma2_bcast(a23, f.x, w0.y);
-                ffma2_bcast(a01, f.y, w1.x);
-                ffma2_bcast(a23, f.y, w1.y);
+                const float4 w0 = *reinterpret_cast<const float4 *>(wsm + (gi * 8 + 2 * j) * 4);
+                const float4 w1 = *reinterpret_cast<const float4 *>(wsm + (gi * 8 + 2 * j + 1) * 4);
+                a0 = fmaf(f.x, w0.x, a0);
+                a1 = fmaf(f.x, w0.y, a1);
+                a2 = fmaf(f.x, w0.z, a2);
+                a3 = fmaf(f.x, w0.w, a3);
+                a0 = fmaf(f.y, w1.x, a0);
+                a1 = fmaf(f.y, w1.y, a1);
+                a2 = fmaf(f.y, w1.z, a2);
+                a3 = fmaf(f.y, w1.w, a3);
               }
-              p01[gi] = a01;
-              p23[gi] = a23;
+              ps[0][gi] = a0;
+              ps[1][gi] = a1;
+              ps[2][gi] = a2;
+              ps[3][gi] = a3;
             }
           }
           if (valid) {
             float sum[4];
-            sum[0] = ((lo_f32(p01[0]) + lo_f32(p01[4])) + (lo_f32(p01[2]) + lo_f32(p01[6]))) +
-                     ((lo_f32(p01[1]) + lo_f32(p01[5])) + (lo_f32(p01[3]) + lo_f32(p01[7])));
-            sum[1] = ((hi_f32(p01[0]) + hi_f32(p01[4])) + (hi_f32(p01[2]) + hi_f32(p01[6]))) +
-                     ((hi_f32(p01[1]) + hi_f32(p01[5])) + (hi_f32(p01[3]) + hi_f32(p01[7])));
-            sum[2] = ((lo_f32(p23[0]) + lo_f32(p23[4])) + (lo_f32(p23[2]) + lo_f32(p23[6]))) +
-                     ((lo_f32(p23[1]) + lo_f32(p23[5])) + (lo_f32(p23[3]) + lo_f32(p23[7])));
-            sum[3] = ((hi_f32(p23[0]) + hi_f32(p23[4])) + (hi_f32(p23[2]) + hi_f32(p23[6]))) +
-                     ((hi_f32(p23[1]) + hi_f32(p23[5])) + (hi_f32(p23[3]) + hi_f32(p23[7])));
+#pragma unroll
+            for (int o = 0; o < 4; ++o)
+              sum[o] = ((ps[o][0] + ps[o][4]) + (ps[o][2] + ps[o][6])) + ((ps[o][1] + ps[o][5]) + (ps[o][3] + ps[o][7]));
             const int tap = (n_base + c) / g.dec_co;
             const int a = tap / g.dec_kw, b = tap - a * g.dec_kw;
 #pragma unroll
