@@ -696,6 +696,68 @@ def build_detector(spec: dict, batch: int, size: int, seed: int, fused_fpn_tail:
     return g, out
 
 
+def build_fusion_probe(seed: int, split: bool, batch: int = 2, size: int = 16):
+    """Test graph for the Runtime's speculative fusions: a depthwise conv +
+    pointwise GEMM pair (fused block), a lateral 1x1 GEMM + nearest 2x
+    resize-add (upsampled residual in the GEMM epilogue) and the DB head's
+    two transposed convs (fused tail), chained. With split=True a later op
+    reads each pair's intermediate (its output feeds nothing), so every pair
+    must split back into its two ops; the chain's output is the same. The
+    pairs' inputs are read again at the end in both variants."""
+    g = Graph((batch, 3, size, size))
+    bd = Builder(g, Init(seed))
+    side = Init(seed + 1)  # the split readers' weights: the chain draws the same values either way
+
+    def read_later(t):
+        main, bd.init = bd.init, side
+        bd.pointwise(t, 64, act="none")
+        bd.init = main
+
+    x = bd.to_nhwc(0)
+    c1 = bd.conv_bn_act(x, 64, 3)
+    # dw 3x3 + pw: the fused depthwise + pointwise block
+    d = bd.conv_bn_act(c1, 64, 3, depthwise=True)
+    pw = bd.pointwise(d, 64)
+    if split:
+        read_later(d)
+    # lateral 1x1 + resize-add of a coarser map
+    coarse = bd.conv_bn_act(pw, 64, 3, stride=(2, 2), depthwise=True)
+    lat = bd.pointwise(pw, 64, act="none")
+    b, h, w, c = g.tensors[lat].shape
+    _, hs, ws_, _ = g.tensors[coarse].shape
+    y = g.act(bd._name("fpn_add"), (b, h, w, c))
+    g.op([coarse, lat], y,
+         f"r.resize_nearest_add_nhwc({coarse},{lat},{y},{vec((b, c, hs, ws_))},{vec((b, c, h, w))},"
+         f"{flit(h / hs)},{flit(w / ws_)});",
+         {"op": "resize_add", "in": coarse, "add": lat, "out": y, "scale": [h / hs, w / ws_]})
+    if split:
+        read_later(lat)
+    # DB tail: deconv 64 -> 64 (+ReLU) then 64 -> 1 (+sigmoid)
+    x = y
+    first = None
+    for co, act in ((64, "relu"), (1, "sigmoid")):
+        b, h, w, c = g.tensors[x].shape
+        name = bd._name("deconv")
+        wi = g.const(name + "_w", bd.init.he((c, 2, 2, co), c * 4))
+        bi = g.const(name + "_b", bd.init.normal((co,), 0.0, 0.1))
+        yd = g.act(name, (b, 2 * h, 2 * w, co))
+        g.op([x, wi, bi], yd,
+             f"r.deconv({x},{wi},{yd},{vec((b, c, h, w))},{vec((c, co, 2, 2))},{vec((b, co, 2 * h, 2 * w))},"
+             f"{{0,0}},{{2,2}},{{1,1}},true,{bi},{ACT[act]});",
+             {"op": "deconv", "in": x, "w": wi, "b": bi, "out": yd, "act": ACT[act]})
+        first = yd if first is None else first
+        x = yd
+    if split:
+        read_later(first)
+    # Keep every pair's input alive to the end, so the arena planner cannot
+    # hand a pair's output the space of its dying input (the Runtime fuses
+    # only when the fused kernel's input and output are disjoint).
+    for t in (c1, pw, y):
+        read_later(t)
+    b, h, w, _ = g.tensors[x].shape
+    return g, g.view(x, "maps", (b, 1, h, w))
+
+
 # Segments of the operator zoo's output, in order: (name, shape).
 ZOO_INPUT = (2, 8, 12, 16)
 

@@ -48,6 +48,10 @@ SHAPES = {
     "block_b16_xv": ("block", 16, None),
     "neck_b256_xv": ("neck", 256, None),
     "zoo_xv": ("zoo", 2, None),
+    # Runtime fusion test graphs: every fusable pair fused, or split back by
+    # a later read of its intermediate (same chain output).
+    "probe_fused": ("probe", 2, None),
+    "probe_split": ("probe_split", 2, None),
 }
 
 
@@ -71,6 +75,8 @@ def graph(name: str):
     if family == "zoo":
         g, out, _ = modelgen.build_zoo_xv(SEED)
         return g, out
+    if family in ("probe", "probe_split"):
+        return modelgen.build_fusion_probe(SEED, split=family == "probe_split", batch=batch)
     s = spec(family)
     if family == "recognizer":
         return modelgen.build_recognizer(s, batch, SEED, xv=xv)

@@ -224,3 +224,35 @@ def test_model_stream_matches_serial(cuda):
             assert torch.all(got[n:] == -1)
     finally:
         model.close()
+
+
+def test_runtime_fusions_and_split_back(native, cuda):
+    """The Runtime's speculative fusions (depthwise + pointwise block, lateral
+    1x1 + FPN resize-add, DB-head transposed-conv pair) on a chained test
+    graph: with nothing else reading the intermediates each pair runs fused
+    (its second slot an empty "fused" placeholder); in the twin graph a later
+    op reads every intermediate, so every pair splits back into its two ops
+    in place. The chain output is bit-identical both ways and within the
+    fp16 bar of the oracle."""
+    from ppocr_b200 import models, pipeline
+
+    x = _input(2, 16, 16, 77)
+    outs = {}
+    for name in ("probe_fused", "probe_split"):
+        m = pipeline.CompiledModel(name, cuda)
+        try:
+            names = m.lib.op_names(m.handle)
+            outs[name] = _run_f32(m, x).cpu()
+        finally:
+            m.close()
+        fused = {"dwpw_block", "gemm_resize_add", "deconv_db_tail"}
+        if name == "probe_fused":
+            assert fused <= set(names) and names.count("fused") == 3, names
+        else:
+            assert not fused & set(names) and "fused" not in names, names
+            assert {"depthwise", "resize_add_nhwc", "deconv_tc", "deconv"} <= set(names), names
+    assert torch.equal(outs["probe_fused"].view(torch.int16), outs["probe_split"].view(torch.int16))
+    g, out_id = models.graph("probe_fused")
+    want, _ = OM.run_graph(g, x, out_id)
+    assert_close(outs["probe_fused"], want, what="fusion probe")
+    assert native.ppocr_b200_device_error() == 0
