@@ -33,6 +33,7 @@ SHAPES = {
     "rec_b2": ("recognizer", 2, None),
     "det_b8": ("detector", 8, 960),
     "det_b1": ("detector", 1, 960),
+    "det_b4": ("detector", 4, 960),
     "det_b1_s128": ("detector", 1, 128),
     "block_b16": ("block", 16, None),
     "block_b2": ("block", 2, None),

@@ -310,14 +310,16 @@ class PagePipeline:
 
         The reference's full-page worker copies, detects, reads the map back
         and then recognizes in turn (full_page_worker.cpp:361-497,
-        detection_worker.cpp:402-405). Here the crops' host->device copy runs
-        on a copy stream during the detector (after the pages' copy, which
-        the detector waits for), and the binary map's
-        device->host copy on a second copy stream during the recognizer; the
-        batch is complete when the pipeline's stream passes both (so an event
-        recorded on it after this call marks the end of the whole batch).
-        A later call's copies wait for this call's readers of the staging
-        buffers. bitmap_h: uint8 [>=pages, 1, S, S]; ids_h int32 [>=lines, T];
+        detection_worker.cpp:402-405). Here one copy stream brings the first
+        half of the pages, the second half and then the crops in that order;
+        the detector runs on each half of the pages as soon as it lands
+        (a half-batch compiled shape, `half_detector`, sharing the detector's
+        weights), so the second half's copy and the crops' copy overlap
+        detection. The binary maps go back on a second copy stream during the
+        recognizer. The batch is complete when the pipeline's stream passes
+        every copy (an event recorded on it after this call marks the end of
+        the whole batch); a later call's copies start after this batch.
+        bitmap_h: uint8 [>=pages, 1, S, S]; ids_h int32 [>=lines, T];
         len_h int32 [>=lines]; score_h f32 [>=lines]."""
         if not hasattr(self, "_h2d"):
             with torch.cuda.device(self.device):
@@ -327,23 +329,29 @@ class PagePipeline:
                                                 device=self.device)
                 b, c, h, w = self.rec.model.input_shape
                 self._stage_crops = torch.empty(b, h, w, c, dtype=torch.float16, device=self.device)
-                self._pages_in = torch.cuda.Event()
-                self._crops_in, self._crops_read = torch.cuda.Event(), torch.cuda.Event()
+                self._half_in = [torch.cuda.Event(), torch.cuda.Event()]
+                self._crops_in = torch.cuda.Event()
                 self._map_ready, self._map_out = torch.cuda.Event(), torch.cuda.Event()
+            self._half = self.half_detector()
         s = self.stream
         m, n = pages_h.shape[0], crops_h.shape[0]
-        with torch.cuda.stream(s):
-            self._stage_pages[:m].copy_(pages_h, non_blocking=True)
-            self._pages_in.record(s)
-        # The crops follow the pages over the link (not beside them: the
-        # detector waits for the pages alone), and land during the detector.
-        self._h2d.wait_event(self._pages_in)
-        self._h2d.wait_event(self._crops_read)  # previous batch's recognizer is done with the crops
+        hb = self._half.input_shape[0] if self._half is not None else m
+        halves = [(0, min(m, hb))] + ([(hb, m)] if m > hb else [])
+        # Copies start after everything already queued on the pipeline's
+        # stream (the previous batch's readers of the staging buffers).
+        self._h2d.wait_stream(s)
         with torch.cuda.stream(self._h2d):
+            for k, (a, b) in enumerate(halves):
+                self._stage_pages[a:b].copy_(pages_h[a:b], non_blocking=True)
+                self._half_in[k].record(self._h2d)
             self._stage_crops[:n].copy_(crops_h, non_blocking=True)
             self._crops_in.record(self._h2d)
-        self.det.enqueue_nhwc(self._stage_pages[:m], self.prob, s)
-        s.wait_event(self._map_out)  # previous batch's map is on the host before it is overwritten
+        for k, (a, b) in enumerate(halves):
+            s.wait_event(self._half_in[k])
+            if self._half is not None:
+                self._half.enqueue_nhwc(self._stage_pages[a:b], self.prob[a:], s)
+            else:
+                self.det.enqueue_nhwc(self._stage_pages[a:b], self.prob, s)
         px = m * self.size * self.size
         capi.check(self.lib.ppocr_b200_binarize(_p(self.prob), _p(self.bitmap), px, self.thresh,
                                                 ctypes.c_void_p(s.cuda_stream)))
@@ -354,13 +362,23 @@ class PagePipeline:
             self._map_out.record(self._d2h)
         s.wait_event(self._crops_in)
         self.rec.enqueue(self._stage_crops[:n])
-        self._crops_read.record(s)
         with torch.cuda.stream(s):
             ids_h[:n].copy_(self.rec.out_ids[:n], non_blocking=True)
             len_h[:n].copy_(self.rec.out_len[:n], non_blocking=True)
             score_h[:n].copy_(self.rec.out_score[:n], non_blocking=True)
         s.wait_event(self._map_out)
 
+    def half_detector(self):
+        """The compiled shape with half the detector's pages (same size and
+        weights file), or None when the catalog has none."""
+        half = self.pages // 2
+        name = f"det_b{half}" if self.size == 960 else None
+        if not half or name is None or name not in models.SHAPES:
+            return None
+        return CompiledModel(name, self.device)
+
     def close(self) -> None:
         self.det.close()
         self.rec.close()
+        if getattr(self, "_half", None) is not None:
+            self._half.close()
