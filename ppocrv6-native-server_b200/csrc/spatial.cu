@@ -221,8 +221,10 @@ __global__ void __launch_bounds__(256)
   const int twin = (TW - 1) * SW + KW;
   half *xs = reinterpret_cast<half *>(dwt_smem);           // [KH][twin][CB]
   half *ws = xs + KH * twin * CB;                           // [TAPS][CB]
-  // block -> (n, oh, column tile, channel chunk)
-  int b = blockIdx.x;
+  // block -> (n, oh, column tile, channel chunk), last block first: the
+  // producer wrote its highest rows last, and those are still in L2 (the
+  // next kernel, walking upwards, then finds this one's lowest rows there).
+  int b = gridDim.x - 1 - blockIdx.x;
   const int chunk = b % chunks;
   b /= chunks;
   const int tw = b % tiles_w;
@@ -395,8 +397,9 @@ __global__ void __launch_bounds__(256)
   const int rin = (TH - 1) * SH + KH;
   half *xs = reinterpret_cast<half *>(dwt_smem); // [rin][twin][CB]
   half *ws = xs + rin * twin * CB;                // [TAPS][CB]
-  // block -> (n, row tile, column tile, channel chunk)
-  int b = blockIdx.x;
+  // block -> (n, row tile, column tile, channel chunk), last block first
+  // (the producer's most recently written rows are the ones still in L2).
+  int b = gridDim.x - 1 - blockIdx.x;
   const int chunk = b % chunks;
   b /= chunks;
   const int tw = b % tiles_w;
@@ -899,7 +902,9 @@ __global__ void __launch_bounds__(kBlock)
                       FastDiv by_groups, FastDiv by_ow, FastDiv by_oh) {
   pdl_begin();
   const int groups = C >> 3;
-  long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  // Last block first: the producer's most recently written rows are the ones
+  // still in L2.
+  long long i = static_cast<long long>(gridDim.x - 1 - blockIdx.x) * blockDim.x + threadIdx.x;
   const long long total = static_cast<long long>(batch) * OH * OW * groups;
   if (i >= total)
     return;
