@@ -1278,7 +1278,20 @@ def _cpu_c5():
                       f"run's 8 pages + 512 lines (the reference has no CPU layer path)"}
 
 
+def json_stdout():
+    """Under torchrun, native libraries write banners to the process's
+    stdout (NCCL prints its version at the first collective). Send file
+    descriptor 1 to stderr and keep the original stdout for the JSON line
+    alone, so that stdout holds exactly one line."""
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        sys.stdout.flush()
+        keep = os.dup(1)
+        os.dup2(2, 1)
+        sys.stdout = os.fdopen(keep, "w", buffering=1)
+
+
 def main():
+    json_stdout()
     args = parse()
     if args.steps is None:
         args.steps = 20 if args.config == "c4" or args.impl == "reference" else 200
